@@ -1,0 +1,635 @@
+// W4A16 GEMV / small-batch GEMM for sm_100a.
+//
+// Replaces torch._weight_int4pack_mm as called by the reference at
+// moss_tts_lite/fast.py:118 (FastMossTTS._linear), gptq.py:582
+// (kernel_linear) and fast_native.py:169 (_lin_fused): y = x . W_eff^T with
+// W_eff = (q - 8) * scale + zero per group (gptq.py:87-97), fp32
+// accumulation, bf16 output.  The AutoGPTQ face computes
+// W_eff = (q - z) * s with the same kernel.
+//
+// Design (HBM-bound at batch 1):
+//  * weights stream through a shared-memory ring filled by 1-D bulk copies
+//    (cp.async.bulk, ~16 KB = several 64-column x group tiles each) issued
+//    by a producer
+//    warp as soon as the CTA starts - before the upstream kernel has
+//    finished when launched with programmatic dependent launch;
+//  * stream-K partition: CTA c owns tiles [T c / G, T (c+1) / G), so every
+//    CTA streams the same number of bytes whatever N and K are;
+//  * codes go register -> bf16 pairs (128 + q) with three shifts and four
+//    LOP3 per 8 codes and into m16n8k16 bf16 MMAs whose B operand is the
+//    bf16 activation itself (batch in the MMA N dimension).  The per-group
+//    affine is applied after the group's MMAs: y += A (D - 128 Sx) + B Sx,
+//    where A/B are the group's scale/offset and Sx the group's sum of
+//    activations.  Products of bf16 values are exact in fp32;
+//  * split-K partials from different CTAs are combined by the last CTA to
+//    arrive at a column block, in fixed contributor order (deterministic),
+//    followed by the fused epilogue (store / residual add / SwiGLU).
+#include "common.cuh"
+#include "w4_gemv.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+
+namespace mtl {
+
+namespace {
+
+__host__ __device__ __forceinline__ int cta_of_tile(long long t, int G, int T) {
+  return (int)(((t + 1) * (long long)G - 1) / (long long)T);
+}
+
+__host__ __device__ __forceinline__ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+constexpr int kMiscWords = 256;  // [0,64) reductions, [64,72) 1/rms, [80] bail, [96,96+nblk) last flags
+
+struct SmemLayout {
+  size_t bar, ring, xs, bsum, gsum, part, fin, misc, total;
+};
+
+__host__ __device__ inline SmemLayout smem_layout(const W4Plan& p, int g, int M) {
+  SmemLayout L;
+  size_t o = 0;
+  L.bar = o;
+  o += align_up((size_t)2 * p.stages * 8, 128);
+  L.ring = o;
+  o += (size_t)p.stages * p.tps * p.tile_bytes;
+  o = align_up(o, 16);
+  L.xs = o;
+  o += (size_t)p.ng_max * M * g * 2;
+  o = align_up(o, 16);
+  L.bsum = o;
+  o += (size_t)p.ng_max * M * (g / 16) * 4;
+  L.gsum = o;
+  o += (size_t)p.ng_max * M * 4;
+  o = align_up(o, 16);
+  L.part = o;
+  o += (size_t)p.nblk_max * kW4Warps * kNT * M * 4;
+  L.fin = o;
+  o += (size_t)p.nblk_max * kNT * M * 4;
+  L.misc = o;
+  o += kMiscWords * 4;
+  L.total = align_up(o, 128);
+  return L;
+}
+
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// m16n8k16 bf16 MMA with fp32 accumulate (register-sourced operands).
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int FMT>
+__global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W4Args a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const W4Plan& p = a.p;
+  const int M = a.M, g = a.g, KT = p.KT;
+  const int cta = blockIdx.x;
+  const int t0 = (int)(((long long)p.T * cta) / p.G);
+  const int t1 = (int)(((long long)p.T * (cta + 1)) / p.G);
+  const int nt = t1 - t0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.stages, tps = p.tps;
+  const size_t stage_bytes = (size_t)tps * p.tile_bytes;
+  const SmemLayout L = smem_layout(p, g, M);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar);
+  uint64_t* empty = full + S;
+  uint8_t* ring = smem + L.ring;
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem + L.xs);
+  float* bsum = reinterpret_cast<float*>(smem + L.bsum);
+  float* gsum = reinterpret_cast<float*>(smem + L.gsum);
+  float* part = reinterpret_cast<float*>(smem + L.part);
+  float* fin = reinterpret_cast<float*>(smem + L.fin);
+  float* misc = reinterpret_cast<float*>(smem + L.misc);
+  int* imisc = reinterpret_cast<int*>(misc);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], tps);  // every warp that consumes a tile of the stage arrives
+    }
+    fence_mbar_init();
+  }
+  if (threadIdx.x < kMiscWords - 80) imisc[80 + threadIdx.x] = 0;
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == kW4Warps) {
+    // ------------------------------------------------------------ producer
+    // Weights do not depend on the upstream kernel: start streaming at once.
+    if (lane == 0) {
+      const int nst = (nt + tps - 1) / tps;
+      int issued = 0;
+      for (int st = 0; st < nst; ++st) {
+        const int s = st % S;
+        if (st >= S && !mbar_wait(&empty[s], ((st / S) - 1) & 1)) break;
+        const int ntile = min(tps, nt - st * tps);
+        const uint32_t bytes = (uint32_t)(ntile * p.tile_bytes);
+        mbar_arrive_expect_tx(&full[s], bytes);
+        bulk_g2s(ring + (size_t)s * stage_bytes, a.tiles + (size_t)(t0 + st * tps) * p.tile_bytes, bytes, &full[s]);
+        issued = st + 1;
+      }
+      // The last copy issued on each stage must land before the CTA exits
+      // (consumers normally waited on every one of them already).
+      const uint64_t deadline = globaltimer_ns() + kWaitNs;
+      for (int s = 0; s < S && s < issued; ++s) {
+        const int last = s + ((issued - 1 - s) / S) * S;
+        if (!mbar_wait_until(&full[s], (last / S) & 1, deadline)) {
+          flag_error(kDevCopyDrainTimeout);
+          break;
+        }
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int tid = threadIdx.x;  // 0..255
+  pdl_wait();
+
+  const int ng = min(KT, nt);   // groups touched: cyclic interval [gbeg, gbeg + ng)
+  const int gbeg = t0 % KT;
+  const int nb16 = g / 16;
+  float* red = misc;
+
+  // (a) RMSNorm statistics over the full row (permutation-invariant).
+  if (a.norm_w) {
+    for (int m = 0; m < M; ++m) {
+      float ss = 0.f;
+      const uint16_t* xr = a.x + (size_t)m * a.ldx;
+      if (a.xvec) {
+        for (int c = tid; c < a.K / 8; c += 256) {
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr) + c);
+          const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float lo = __uint_as_float(u[q] << 16), hi = __uint_as_float(u[q] & 0xFFFF0000u);
+            ss = fmaf(lo, lo, ss);
+            ss = fmaf(hi, hi, ss);
+          }
+        }
+      } else {
+        for (int k = tid; k < a.K; k += 256) {
+          const float h = bf16_bits_to_f32(xr[k]);
+          ss = fmaf(h, h, ss);
+        }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) red[warp * kW4MaxM + m] = ss;
+    }
+    consumer_sync();
+    if (tid < M) {
+      float ss = 0.f;
+      for (int w = 0; w < kW4Warps; ++w) ss += red[w * kW4MaxM + tid];
+      misc[64 + tid] = rsqrtf(ss / (float)a.K + a.norm_eps);
+    }
+    consumer_sync();
+  }
+
+  // (b) stage the groups this CTA needs as bf16 in MMA-B order: within each
+  //     16-block lane t reads [2t, 2t+1, 2t+8, 2t+9] at positions 4t..4t+3,
+  //     i.e. 32-bit words [w0, w4, w1, w5, w2, w6, w3, w7] of the input.
+  //     The per-16-block sums feed the bias / offset terms.
+  for (int job = tid; job < ng * M * nb16; job += 256) {
+    const int slot = job / (M * nb16);
+    const int rem = job - slot * (M * nb16);
+    const int m = rem / nb16, b = rem - m * nb16;
+    const int k0 = ((gbeg + slot) % KT) * g + b * 16;
+    const uint16_t* xr = a.x + (size_t)m * a.ldx;
+    uint32_t u[8], nw[8];
+    if (a.xvec) {
+      const uint4 v0 = __ldg(reinterpret_cast<const uint4*>(xr + k0));
+      const uint4 v1 = __ldg(reinterpret_cast<const uint4*>(xr + k0 + 8));
+      u[0] = v0.x; u[1] = v0.y; u[2] = v0.z; u[3] = v0.w; u[4] = v1.x; u[5] = v1.y; u[6] = v1.z; u[7] = v1.w;
+      if (a.norm_w) {
+        const uint4 n0 = __ldg(reinterpret_cast<const uint4*>(a.norm_w + k0));
+        const uint4 n1 = __ldg(reinterpret_cast<const uint4*>(a.norm_w + k0 + 8));
+        nw[0] = n0.x; nw[1] = n0.y; nw[2] = n0.z; nw[3] = n0.w; nw[4] = n1.x; nw[5] = n1.y; nw[6] = n1.z; nw[7] = n1.w;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int ka = a.k_perm ? a.k_perm[k0 + 2 * q] : k0 + 2 * q;
+        const int kb = a.k_perm ? a.k_perm[k0 + 2 * q + 1] : k0 + 2 * q + 1;
+        u[q] = (uint32_t)xr[ka] | ((uint32_t)xr[kb] << 16);
+        if (a.norm_w) nw[q] = (uint32_t)a.norm_w[ka] | ((uint32_t)a.norm_w[kb] << 16);
+      }
+    }
+    float bs = 0.f;
+    if (a.norm_w) {
+      const float rinv = misc[64 + m];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        // model.py:34-40: bf16(h * rsqrt(var + eps)), then bf16(weight * that)
+        const float v0 = round_bf16(__uint_as_float(nw[q] << 16) * round_bf16(__uint_as_float(u[q] << 16) * rinv));
+        const float v1 = round_bf16(__uint_as_float(nw[q] & 0xFFFF0000u) *
+                                    round_bf16(__uint_as_float(u[q] & 0xFFFF0000u) * rinv));
+        u[q] = (__float_as_uint(v0) >> 16) | (__float_as_uint(v1) & 0xFFFF0000u);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) bs += __uint_as_float(u[q] << 16) + __uint_as_float(u[q] & 0xFFFF0000u);
+    uint16_t* dst = xs + ((size_t)slot * M + m) * g + b * 16;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(u[0], u[4], u[1], u[5]);
+    *reinterpret_cast<uint4*>(dst + 8) = make_uint4(u[2], u[6], u[3], u[7]);
+    bsum[(slot * M + m) * nb16 + b] = bs;
+  }
+  for (int i = tid; i < p.nblk_max * kW4Warps * kNT * M; i += 256) part[i] = 0.f;
+  consumer_sync();
+  for (int job = tid; job < ng * M; job += 256) {
+    float s = 0.f;
+    for (int b = 0; b < nb16; ++b) s += bsum[job * nb16 + b];
+    gsum[job] = s;
+  }
+  consumer_sync();
+
+  // ------------------------------------------------------------ main loop
+  const int gr = lane >> 2, tq = lane & 3;
+  const int mrow = min(gr, M - 1);
+  const int KS = g >> 4;
+  const int blk_first = t0 / KT;
+  float yacc[4][4];
+  int cur = -1;
+  bool bail = false;
+
+  auto flush = [&](int blk) {
+    float* dst = part + ((size_t)(blk - blk_first) * kW4Warps + warp) * kNT * M;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = 16 * j + gr + ((e & 2) ? 8 : 0);
+        const int m = 2 * tq + (e & 1);
+        if (m < M) dst[col * M + m] = yacc[j][e];
+      }
+  };
+
+  for (int i = warp; i < nt; i += kW4Warps) {
+    const int t = t0 + i;
+    const int nb = t / KT, G = t - (t / KT) * KT;
+    if (nb != cur) {
+      if (cur >= 0) flush(cur);
+      cur = nb;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) yacc[j][e] = 0.f;
+    }
+    const int st = i / tps, s = st % S;
+    if (!mbar_wait(&full[s], (st / S) & 1)) {
+      bail = true;
+      break;
+    }
+    const uint8_t* tile = ring + (size_t)s * stage_bytes + (size_t)(i % tps) * p.tile_bytes;
+    const uint4* wt = reinterpret_cast<const uint4*>(tile);
+    const int slot = (G - gbeg + KT) % KT;
+    const uint16_t* xg = xs + ((size_t)slot * M + mrow) * g;
+    float d[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) d[j][e] = 0.f;
+#pragma unroll 4
+    for (int ks = 0; ks < KS; ++ks) {
+      const uint4 wv = wt[ks * 32 + lane];
+      const uint2 bx = *reinterpret_cast<const uint2*>(xg + ks * 16 + 4 * tq);
+      const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t w = wr[j];
+        const uint32_t a0 = lop3_and_or(w, 0x000F000Fu, 0x43004300u);
+        const uint32_t a1 = lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u);
+        const uint32_t a2 = lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u);
+        const uint32_t a3 = lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u);
+        mma_bf16_16816(d[j], a0, a1, a2, a3, bx.x, bx.y);
+      }
+    }
+    // group affine: D = sum x (128 + q)  =>  y += A (D - 128 Sx) + B Sx
+    const float sx0 = gsum[slot * M + min(2 * tq, M - 1)];
+    const float sx1 = gsum[slot * M + min(2 * tq + 1, M - 1)];
+    const uint8_t* prm = tile + kNT * g / 2;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int col = 16 * j + gr + 8 * hr;
+        float A, B;
+        if (FMT == kFmtRef) {
+          // gptq.py:87-97: w = (q - 8) * scale + zero = q * scale + (zero - 8 scale)
+          const uint32_t pw = reinterpret_cast<const uint32_t*>(prm)[col];
+          A = bf16_bits_to_f32((uint16_t)(pw & 0xFFFFu));
+          B = fmaf(-8.f, A, bf16_bits_to_f32((uint16_t)(pw >> 16)));
+        } else {
+          // w = (q - (z + zero_offset)) * s
+          A = __half2float(reinterpret_cast<const __half*>(prm)[col]);
+          const uint32_t zw = reinterpret_cast<const uint32_t*>(prm + 128)[col >> 3];
+          const int z = (int)((zw >> (4 * (col & 7))) & 0xFu) + a.zero_offset;
+          B = -(float)z * A;
+        }
+        yacc[j][2 * hr + 0] += fmaf(A, fmaf(-128.f, sx0, d[j][2 * hr + 0]), B * sx0);
+        yacc[j][2 * hr + 1] += fmaf(A, fmaf(-128.f, sx1, d[j][2 * hr + 1]), B * sx1);
+      }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  if (cur >= 0 && !bail) flush(cur);
+  if (bail) imisc[80] = 1;
+  consumer_sync();
+  if (imisc[80] == 1) return;
+
+  // ------------------------------------- CTA reduce + split-K fixup (all blocks at once)
+  const int blk_last = (t1 - 1) / KT;
+  const int nblk = blk_last - blk_first + 1;
+  const int per = kNT * M;
+  for (int i = tid; i < nblk * per; i += 256) {
+    const int bl = i / per, r = i - bl * per;
+    float v = 0.f;
+    for (int w = 0; w < kW4Warps; ++w) v += part[((size_t)bl * kW4Warps + w) * per + r];
+    fin[i] = v;
+  }
+  consumer_sync();
+  bool any_partial = false;
+  for (int bl = 0; bl < nblk; ++bl) {
+    const int blk = blk_first + bl;
+    any_partial |= !((blk * KT >= t0) && ((blk + 1) * KT <= t1));
+  }
+  if (any_partial) {
+    for (int i = tid; i < nblk * per; i += 256) {
+      const int bl = i / per, r = i - bl * per;
+      const int blk = blk_first + bl;
+      if ((blk * KT >= t0) && ((blk + 1) * KT <= t1)) continue;
+      const int c_lo = cta_of_tile((long long)blk * KT, p.G, p.T);
+      a.partials[((size_t)blk * p.maxc + (cta - c_lo)) * per + r] = fin[i];
+    }
+    consumer_sync();
+    if (tid < nblk) {
+      const int blk = blk_first + tid;
+      if (!((blk * KT >= t0) && ((blk + 1) * KT <= t1))) {
+        const int c_lo = cta_of_tile((long long)blk * KT, p.G, p.T);
+        const int c_hi = cta_of_tile((long long)(blk + 1) * KT - 1, p.G, p.T);
+        __threadfence();  // release this CTA's partials (cumulative over the barrier)
+        const int old = atomicAdd(&a.counters[blk], 1);
+        if (old == c_hi - c_lo) {
+          __threadfence();  // acquire the other contributors' partials
+          imisc[96 + tid] = 1;
+          a.counters[blk] = 0;  // re-arm for the next launch
+        }
+      }
+    }
+    consumer_sync();
+    for (int i = tid; i < nblk * per; i += 256) {
+      const int bl = i / per, r = i - bl * per;
+      if (!imisc[96 + bl]) continue;
+      const int blk = blk_first + bl;
+      const int c_lo = cta_of_tile((long long)blk * KT, p.G, p.T);
+      const int c_hi = cta_of_tile((long long)(blk + 1) * KT - 1, p.G, p.T);
+      float v = 0.f;
+      for (int j = 0; j <= c_hi - c_lo; ++j) v += __ldcg(a.partials + ((size_t)blk * p.maxc + j) * per + r);
+      fin[i] = v;
+    }
+    consumer_sync();
+  }
+
+  // ---------------------------------------------------------------- epilogue
+  for (int bl = 0; bl < nblk; ++bl) {
+    const int blk = blk_first + bl;
+    const bool complete = (blk * KT >= t0) && ((blk + 1) * KT <= t1);
+    if (!complete && !imisc[96 + bl]) continue;
+    const float* f = fin + (size_t)bl * per;
+    if (a.epi == kEpiSwiGLU) {
+      for (int i = tid; i < (kNT / 2) * M; i += 256) {
+        const int col = i / M, m = i - (i / M) * M;
+        // fast.py:170-171: bf16(silu(gate)) * up, each op rounded to bf16
+        const float gt = round_bf16(f[col * M + m]);
+        const float up = round_bf16(f[(col + kNT / 2) * M + m]);
+        const float sg = round_bf16(gt / (1.0f + expf(-gt)));
+        a.y[(size_t)m * a.ldy + blk * (kNT / 2) + col] = f32_to_bf16_bits(sg * up);
+      }
+    } else {
+      for (int i = tid; i < per; i += 256) {
+        const int col = i / M, m = i - (i / M) * M;
+        const int n = blk * kNT + col;
+        float v = f[i];
+        if (a.epi == kEpiResidual) {
+          // fast.py:168 / :170: residual + bf16(linear(...)), rounded to bf16
+          v = bf16_bits_to_f32(a.residual[(size_t)m * a.ldr + n]) + round_bf16(v);
+        }
+        a.y[(size_t)m * a.ldy + n] = f32_to_bf16_bits(v);
+      }
+    }
+  }
+}
+
+}  // namespace
+
+int w4_plan(int M, int K, int N, int g, int fmt, int num_sms, W4Plan* out) {
+  if (M < 1 || M > kW4MaxM || K <= 0 || N <= 0 || (N % kNT) || (K % g) || (g % 16)) return -1;
+  W4Plan p{};
+  p.KT = K / g;
+  p.nblocks = N / kNT;
+  p.T = p.nblocks * p.KT;
+  p.tile_bytes = tile_bytes(g, fmt);
+  // ~16 KB per bulk copy (large copies stream markedly better than 4 KB ones)
+  p.tps = 1;
+  while (p.tps < kW4Warps && (p.tps * 2) * p.tile_bytes <= 18 * 1024) p.tps *= 2;
+  const int ngroups = kW4Warps / p.tps;  // stage s is consumed by warp group s % ngroups
+  // CTAs per SM: 2 by default.  With 1, a CTA uses at most ~113 KB when it
+  // can, so that the next kernel of a chain (programmatic dependent launch)
+  // co-resides and starts streaming its weights while this one finishes.
+  static int ctas_per_sm = -1;
+  if (ctas_per_sm < 0) {
+    const char* e = std::getenv("MTL_W4_CTAS_PER_SM");
+    ctas_per_sm = (e && e[0] == '1') ? 1 : 2;
+  }
+  struct Try { int per_sm; size_t budget; };
+  const Try tries[3] = {{2, 113 * 1024}, {1, 113 * 1024}, {1, 225 * 1024}};
+  bool ok = false;
+  for (const Try& tr : tries) {
+    if (tr.per_sm > ctas_per_sm) continue;
+    int G = std::min(p.T, num_sms * tr.per_sm);
+    G = std::max(1, std::min(G, std::max(1, p.T / 2)));
+    p.G = G;
+    const int ntmax = (p.T + G - 1) / G;
+    p.ng_max = std::min(p.KT, ntmax);
+    p.nblk_max = std::min(p.nblocks, ntmax / p.KT + 2);
+    const int nst = (ntmax + p.tps - 1) / p.tps;
+    p.stages = std::max(ngroups, std::min(8, (nst + ngroups - 1) / ngroups * ngroups));
+    for (;;) {
+      SmemLayout L = smem_layout(p, g, M);
+      p.smem = L.total;
+      if (L.total <= tr.budget || p.stages <= ngroups) break;
+      p.stages -= ngroups;
+    }
+    if (p.smem <= tr.budget) { ok = true; break; }
+  }
+  if (!ok) return -2;
+  int maxc = 1;
+  for (int b = 0; b < p.nblocks; ++b) {
+    const int lo = cta_of_tile((long long)b * p.KT, p.G, p.T);
+    const int hi = cta_of_tile((long long)(b + 1) * p.KT - 1, p.G, p.T);
+    maxc = std::max(maxc, hi - lo + 1);
+  }
+  p.maxc = maxc;
+  p.partial_bytes = align_up((size_t)p.nblocks * p.maxc * kNT * M * 4, 256);
+  *out = p;
+  return 0;
+}
+
+cudaError_t w4_launch(const W4Args& a, int fmt, cudaStream_t stream, int use_pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.p.G);
+  cfg.blockDim = dim3((kW4Warps + 1) * 32);
+  cfg.dynamicSmemBytes = a.p.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = use_pdl ? 1 : 0;
+  // The shared-memory opt-in is set once per kernel (to the largest size any
+  // plan uses) so that launches inside a stream capture make no attribute calls.
+  static bool attr_done[2] = {false, false};
+  auto kern = (fmt == kFmtRef) ? w4_gemv_kernel<kFmtRef> : w4_gemv_kernel<kFmtGptq>;
+  const int fi = (fmt == kFmtRef) ? 0 : 1;
+  if (!attr_done[fi]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_done[fi] = true;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+// ------------------------------------------------------------------ packing
+
+namespace {
+
+// Source accessors for one code W[n][k] (n = output column).
+struct GptqSrc {
+  const int32_t* qweight;  // [K/8, N]
+  const int32_t* perm;     // nullable, sorted-k -> original k
+  int N;
+  __device__ __forceinline__ uint32_t code(int n, int k) const {
+    int kk = perm ? perm[k] : k;
+    return ((uint32_t)qweight[(size_t)(kk >> 3) * N + n] >> (4 * (kk & 7))) & 0xFu;
+  }
+};
+struct RefSrc {
+  const uint8_t* q;  // [N, K]
+  int K;
+  __device__ __forceinline__ uint32_t code(int n, int k) const { return q[(size_t)n * K + k] & 0xFu; }
+};
+
+template <class Src>
+__global__ void pack_words_kernel(Src src, int K, int N, int g, int tile_bytes, uint8_t* tiles) {
+  const int KT = K / g, KS = g / 16;
+  const long long words_per_tile = (long long)KS * 32 * 4;
+  const long long total = (long long)(N / kNT) * KT * words_per_tile;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long t = idx / words_per_tile;
+    const int wi = (int)(idx % words_per_tile);
+    const int j = wi & 3, lane = (wi >> 2) & 31, ks = wi >> 7;
+    const int nb = (int)(t / KT), G = (int)(t % KT);
+    const int gr = lane >> 2, tq = lane & 3;
+    const int r0 = nb * kNT + 16 * j + gr, r1 = r0 + 8;
+    const int kb = G * g + 16 * ks;
+    uint32_t w = 0;
+    w |= src.code(r0, kb + 2 * tq) << 0;
+    w |= src.code(r1, kb + 2 * tq) << 4;
+    w |= src.code(r0, kb + 2 * tq + 8) << 8;
+    w |= src.code(r1, kb + 2 * tq + 8) << 12;
+    w |= src.code(r0, kb + 2 * tq + 1) << 16;
+    w |= src.code(r1, kb + 2 * tq + 1) << 20;
+    w |= src.code(r0, kb + 2 * tq + 9) << 24;
+    w |= src.code(r1, kb + 2 * tq + 9) << 28;
+    reinterpret_cast<uint32_t*>(tiles + t * tile_bytes)[wi] = w;
+  }
+}
+
+__global__ void pack_params_ref_kernel(const uint16_t* qsz, int K, int N, int g, int tile_bytes, uint8_t* tiles) {
+  const int KT = K / g;
+  const long long total = (long long)N * KT;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(idx % N), G = (int)(idx / N);
+    const long long t = (long long)(n / kNT) * KT + G;
+    const uint32_t sc = qsz[((size_t)G * N + n) * 2 + 0];
+    const uint32_t zr = qsz[((size_t)G * N + n) * 2 + 1];
+    reinterpret_cast<uint32_t*>(tiles + t * tile_bytes + kNT * g / 2)[n % kNT] = sc | (zr << 16);
+  }
+}
+
+__global__ void pack_params_gptq_kernel(const uint16_t* scales, const int32_t* qzeros, int K, int N, int g,
+                                        int tile_bytes, uint8_t* tiles) {
+  const int KT = K / g;
+  const long long total = (long long)N * KT;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(idx % N), G = (int)(idx / N);
+    const long long t = (long long)(n / kNT) * KT + G;
+    uint8_t* prm = tiles + t * tile_bytes + kNT * g / 2;
+    reinterpret_cast<uint16_t*>(prm)[n % kNT] = scales[(size_t)G * N + n];
+    if ((n & 7) == 0)
+      reinterpret_cast<uint32_t*>(prm + 128)[(n % kNT) >> 3] = (uint32_t)qzeros[(size_t)G * (N / 8) + n / 8];
+  }
+}
+
+// Inverse of the word packing, for bit-exact round-trip checks: codes[n][k].
+__global__ void unpack_codes_kernel(const uint8_t* tiles, int K, int N, int g, int tile_bytes, uint8_t* codes) {
+  const int KT = K / g;
+  const long long total = (long long)N * K;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(idx / K), k = (int)(idx % K);
+    const int nb = n / kNT, c = n % kNT, G = k / g, kin = k % g;
+    const int j = c / 16, rr = c % 16, gr = rr & 7, hi_row = rr >> 3;
+    const int ks = kin / 16, k16 = kin % 16;
+    const int hi_k = k16 >= 8 ? 1 : 0;
+    const int kk = k16 & 7, tq = kk >> 1, odd = kk & 1;
+    const int lane = gr * 4 + tq;
+    const int slot = (hi_row ? 1 : 0) + (hi_k ? 2 : 0) + (odd ? 4 : 0);
+    const long long t = (long long)nb * KT + G;
+    const uint32_t w = reinterpret_cast<const uint32_t*>(tiles + t * tile_bytes)[(ks * 32 + lane) * 4 + j];
+    codes[idx] = (uint8_t)((w >> (4 * slot)) & 0xFu);
+  }
+}
+
+inline int grid_for(long long work) {
+  long long b = (work + 255) / 256;
+  return (int)std::max<long long>(1, std::min<long long>(b, 148LL * 32));
+}
+
+}  // namespace
+
+cudaError_t w4_pack_gptq(const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                         const int32_t* perm, int K, int N, int g, uint8_t* tiles, cudaStream_t s) {
+  const int tb = tile_bytes(g, kFmtGptq);
+  GptqSrc src{qweight, perm, N};
+  long long words = (long long)(N / kNT) * (K / g) * (g / 16) * 128;
+  pack_words_kernel<<<grid_for(words), 256, 0, s>>>(src, K, N, g, tb, tiles);
+  pack_params_gptq_kernel<<<grid_for((long long)N * (K / g)), 256, 0, s>>>(scales, qzeros, K, N, g, tb, tiles);
+  return cudaGetLastError();
+}
+
+cudaError_t w4_pack_ref(const uint8_t* q, const uint16_t* qsz, int K, int N, int g, uint8_t* tiles,
+                        cudaStream_t s) {
+  const int tb = tile_bytes(g, kFmtRef);
+  RefSrc src{q, K};
+  long long words = (long long)(N / kNT) * (K / g) * (g / 16) * 128;
+  pack_words_kernel<<<grid_for(words), 256, 0, s>>>(src, K, N, g, tb, tiles);
+  pack_params_ref_kernel<<<grid_for((long long)N * (K / g)), 256, 0, s>>>(qsz, K, N, g, tb, tiles);
+  return cudaGetLastError();
+}
+
+cudaError_t w4_unpack_codes(const uint8_t* tiles, int K, int N, int g, int fmt, uint8_t* codes, cudaStream_t s) {
+  unpack_codes_kernel<<<grid_for((long long)N * K), 256, 0, s>>>(tiles, K, N, g, tile_bytes(g, fmt), codes);
+  return cudaGetLastError();
+}
+
+}  // namespace mtl

@@ -1,0 +1,189 @@
+"""W4A16 linears backed by the sm_100a kernels of libmtl_b200.so.
+
+Two faces over one packed device format (the MTL tile layout, see
+include/mtl_b200.h):
+
+* ``QuantLinear`` - the AutoGPTQ-style module named by the benchmark
+  configuration: ``qweight`` int32 [K/8, N], ``qzeros`` int32 [K/g, N/8],
+  fp16 ``scales`` [K/g, N], ``g_idx`` [K];  ``w = (q - (z + zero_offset)) * s``.
+* ``RefW4Linear`` - the reference's own W4 weight, integer codes
+  ``q`` uint8 [N, K] plus bf16 ``qsz`` [K/g, N, 2] with
+  ``w = (q - 8) * scale + zero`` (moss_tts_lite/gptq.py:87-97), i.e. what
+  ``FastMossTTS._quantize`` builds before the tinygemm packer
+  (moss_tts_lite/fast.py:85-100).
+
+Both call ``mtl_w4a16_linear``; torch only owns the device memory.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+_GROUPS = (32, 64, 128, 256)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+class W4Weight:
+    """A packed W4 weight plus its split-K scratch (one per linear)."""
+
+    def __init__(self, tiles: torch.Tensor, K: int, N: int, group_size: int, fmt: int,
+                 zero_offset: int = 0, k_perm: torch.Tensor | None = None):
+        self.tiles = tiles
+        self.K, self.N, self.group_size, self.fmt = int(K), int(N), int(group_size), int(fmt)
+        self.zero_offset = int(zero_offset)
+        self.k_perm = k_perm
+        _, sb = _lib.w4_plan(8, self.K, self.N, self.group_size, self.fmt)
+        self.scratch = torch.zeros(sb, dtype=torch.uint8, device=tiles.device)
+
+    @staticmethod
+    def alloc_tiles(K: int, N: int, g: int, fmt: int, device) -> torch.Tensor:
+        tb, _ = _lib.w4_plan(1, K, N, g, fmt)
+        return torch.empty(tb, dtype=torch.uint8, device=device)
+
+    @classmethod
+    def from_ref(cls, q: torch.Tensor, qsz: torch.Tensor, group_size: int) -> "W4Weight":
+        """Codes uint8 [N, K] (0..15) + qsz bf16 [K/g, N, 2] on a CUDA device."""
+        if group_size not in _GROUPS:
+            raise ValueError("w4_group_size must be 32/64/128/256")
+        N, K = q.shape
+        if tuple(qsz.shape) != (K // group_size, N, 2):
+            raise ValueError(f"qsz shape {tuple(qsz.shape)} != {(K // group_size, N, 2)}")
+        q = q.to(torch.uint8).contiguous()
+        qsz = qsz.to(torch.bfloat16).contiguous()
+        tiles = cls.alloc_tiles(K, N, group_size, _lib.MTL_FMT_REF, q.device)
+        _lib.call("mtl_w4_pack_ref", q.data_ptr(), qsz.data_ptr(), K, N, group_size,
+                  tiles.data_ptr(), _stream())
+        return cls(tiles, K, N, group_size, _lib.MTL_FMT_REF)
+
+    def unpack_codes(self) -> torch.Tensor:
+        """uint8 [N, K] codes in packed row order (bit-exact inverse of packing)."""
+        out = torch.empty(self.N, self.K, dtype=torch.uint8, device=self.tiles.device)
+        _lib.call("mtl_w4_unpack_codes", self.tiles.data_ptr(), self.K, self.N, self.group_size,
+                  self.fmt, out.data_ptr(), _stream())
+        return out
+
+    def linear(self, x: torch.Tensor, *, out: torch.Tensor | None = None,
+               residual: torch.Tensor | None = None, norm_weight: torch.Tensor | None = None,
+               norm_eps: float = 1e-6, swiglu: bool = False) -> torch.Tensor:
+        """``x`` bf16 [..., K] -> bf16 [..., N] (or [..., N/2] with swiglu)."""
+        if x.dtype != torch.bfloat16:
+            raise TypeError(f"x must be bfloat16, got {x.dtype}")
+        if x.shape[-1] != self.K:
+            raise ValueError(f"x last dim {x.shape[-1]} != K={self.K}")
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, self.K)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        M = x2.shape[0]
+        nout = self.N // 2 if swiglu else self.N
+        epi = _lib.MTL_EPI_STORE
+        if swiglu:
+            epi = _lib.MTL_EPI_SWIGLU
+        elif residual is not None:
+            epi = _lib.MTL_EPI_RESIDUAL
+            residual = residual.reshape(M, self.N)
+            if residual.dtype != torch.bfloat16 or not residual.is_contiguous():
+                raise ValueError("residual must be contiguous bf16 [..., N]")
+        if out is None:
+            out = torch.empty(M, nout, dtype=torch.bfloat16, device=x.device)
+        if M == 0:
+            return out.reshape(*lead, nout)
+        _lib.call("mtl_w4a16_linear", x2.data_ptr(), self.K, M, self.K, self.N, self.group_size,
+                  self.fmt, self.tiles.data_ptr(), self.zero_offset, _ptr(self.k_perm),
+                  _ptr(norm_weight), ctypes.c_float(norm_eps), epi, _ptr(residual), out.data_ptr(),
+                  nout, self.scratch.data_ptr(), self.scratch.numel(), _stream())
+        return out.reshape(*lead, nout)
+
+
+class RefW4Linear(torch.nn.Module):
+    """The reference's W4 linear (``(packed, qsz)`` call sites of fast.py:118,
+    gptq.py:582) built from the codes before tinygemm packing."""
+
+    def __init__(self, q: torch.Tensor, qsz: torch.Tensor, group_size: int = 128):
+        super().__init__()
+        self.w = W4Weight.from_ref(q, qsz, group_size)
+        self.in_features, self.out_features = self.w.K, self.w.N
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.w.linear(x)
+
+
+class QuantLinear(torch.nn.Module):
+    """AutoGPTQ-style W4A16 linear (bits=4) on the B200 kernels.
+
+    Buffers follow AutoGPTQ: ``qweight`` int32 [K/8, N], ``qzeros`` int32
+    [K/g, N/8], ``scales`` fp16 [K/g, N], ``g_idx`` int32 [K]. Call
+    ``post_init()`` (or use ``from_tensors``) after filling them; that packs
+    the weight once into the device tile layout. Act-order checkpoints
+    (non-monotone ``g_idx``) are served by sorting K by group at packing
+    time and gathering x through the same permutation in the kernel.
+    """
+
+    def __init__(self, bits: int, group_size: int, infeatures: int, outfeatures: int,
+                 bias: bool = False, zero_offset: int = 0, device="cuda"):
+        super().__init__()
+        if bits != 4:
+            raise NotImplementedError("only 4-bit QuantLinear is provided")
+        if group_size == -1:
+            group_size = infeatures
+        if group_size not in _GROUPS:
+            raise ValueError(f"group_size {group_size} not in {_GROUPS}")
+        if bias:
+            raise NotImplementedError("MOSS-TTS linears carry no bias")
+        if infeatures % group_size or outfeatures % 64:
+            raise ValueError(f"infeatures {infeatures} % group_size and outfeatures {outfeatures} % 64 must be 0")
+        self.bits, self.group_size = bits, group_size
+        self.infeatures, self.outfeatures = infeatures, outfeatures
+        self.zero_offset = int(zero_offset)
+        G = infeatures // group_size
+        self.register_buffer("qweight", torch.zeros(infeatures // 8, outfeatures, dtype=torch.int32, device=device))
+        self.register_buffer("qzeros", torch.zeros(G, outfeatures // 8, dtype=torch.int32, device=device))
+        self.register_buffer("scales", torch.zeros(G, outfeatures, dtype=torch.float16, device=device))
+        self.register_buffer("g_idx", (torch.arange(infeatures, dtype=torch.int32, device=device) // group_size))
+        self.w: W4Weight | None = None
+
+    @classmethod
+    def from_tensors(cls, qweight, qzeros, scales, g_idx=None, group_size: int = 128,
+                     zero_offset: int = 0) -> "QuantLinear":
+        K = qweight.shape[0] * 8
+        N = qweight.shape[1]
+        m = cls(4, group_size, K, N, zero_offset=zero_offset, device=qweight.device)
+        m.qweight.copy_(qweight)
+        m.qzeros.copy_(qzeros)
+        m.scales.copy_(scales)
+        if g_idx is not None:
+            m.g_idx.copy_(g_idx)
+        m.post_init()
+        return m
+
+    def post_init(self) -> None:
+        K, N, g = self.infeatures, self.outfeatures, self.group_size
+        gi = self.g_idx.to(torch.int64)
+        if gi.min() < 0 or gi.max() >= K // g:
+            raise ValueError("g_idx out of range")
+        trivial = torch.equal(gi, torch.arange(K, device=gi.device) // g)
+        perm = None
+        if not trivial:
+            perm = torch.argsort(gi, stable=True)
+            if not torch.equal(gi[perm], torch.arange(K, device=gi.device) // g):
+                raise ValueError("g_idx must assign exactly group_size rows to every group")
+            perm = perm.to(torch.int32).contiguous()
+        tiles = W4Weight.alloc_tiles(K, N, g, _lib.MTL_FMT_GPTQ, self.qweight.device)
+        _lib.call("mtl_w4_pack_gptq", self.qweight.data_ptr(), self.qzeros.data_ptr(),
+                  self.scales.data_ptr(), _ptr(perm), K, N, g, tiles.data_ptr(), _stream())
+        self.w = W4Weight(tiles, K, N, g, _lib.MTL_FMT_GPTQ, self.zero_offset, perm)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.w is None:
+            self.post_init()
+        return self.w.linear(x)
