@@ -104,6 +104,80 @@ int mtl_w4a16_linear(const uint16_t* x, int ldx, int M, int K, int N, int group_
                      float norm_eps, int epilogue, const uint16_t* residual, uint16_t* y, int ldy,
                      void* scratch, size_t scratch_bytes, mtl_stream_t stream);
 
+
+/* ------------------------------------------------------ decoder step ops */
+
+/* Combined embedding of one decode row per stream (model.py:156-161,
+ * fast.py:123-128): out[m] = E_text[ids[m][0]] + E_audio[0][ids[m][1]] + ...
+ * + E_audio[31][ids[m][32]], each add rounded to bf16, in that order.
+ *   ids       int64 [M, 33] (device)
+ *   emb_text  bf16 [text_vocab, hidden];  emb_audio bf16 [32 * 1025, hidden]
+ *             (the 32 emb_ext tables stacked)
+ *   hidden % 8 == 0.  Out-of-range ids set device-status bit 1 and read row 0. */
+int mtl_embed_sum(const int64_t* ids, int M, const uint16_t* emb_text, int text_vocab,
+                  const uint16_t* emb_audio, int hidden, uint16_t* out, mtl_stream_t stream);
+
+/* Scratch for mtl_attn_decode (partials + per-KV-head counters); zero-fill
+ * once before first use. */
+int mtl_attn_scratch_bytes(int streams, int n_heads, int n_kv, int splits, size_t* out);
+
+/* One layer of decode attention for `streams` independent streams, fusing the
+ * q/k head RMSNorm (eps 1e-6), RoPE at the device position, the K/V append
+ * and split-KV GQA attention over positions [0, pos] (fast.py:138-162,
+ * model.py:175-190; replaces the eager F.scaled_dot_product_attention call
+ * between graph replays at fast.py:319-324).
+ *   qkv        bf16 [streams, (n_heads + 2 n_kv) * 128]: q | k | v projections
+ *   q_norm_w, k_norm_w  bf16 [128];  rope_cos/sin bf16 [max_seq, 128]
+ *   k_cache, v_cache    bf16 [n_kv, max_seq, 128] of this layer for stream 0;
+ *              stream s starts cache_stream_stride elements later
+ *   pos        int64 [streams] (device): position being decoded
+ *   splits     KV splits per head, ceil(max_seq / 512) <= splits <= 64
+ *   out        bf16 [streams, n_heads * 128]
+ * head_dim must be 128 and n_heads / n_kv <= 8. */
+int mtl_attn_decode(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_t* k_norm_w,
+                    const uint16_t* rope_cos, const uint16_t* rope_sin, uint16_t* k_cache, uint16_t* v_cache,
+                    long long cache_stream_stride, int max_seq, const int64_t* pos, int streams, int n_heads,
+                    int n_kv, int head_dim, int splits, uint16_t* out, void* scratch, size_t scratch_bytes,
+                    mtl_stream_t stream);
+
+/* y = epilogue(x . W^T) for bf16 weights W [N, K] (the lm heads,
+ * model.py:240-295, fast.py:174-194, and bf16 backbone linears: F.linear at
+ * model.py:171-196 and the bf16 keeps of gptq.py:689-697).
+ * norm_w (nullable) fuses an RMSNorm (model.py:34-40) into the prologue;
+ * x_normed (nullable) then receives the normed rows.  Epilogues as for
+ * mtl_w4a16_linear (MTL_EPI_*); MTL_EPI_SWIGLU expects the gate and up rows
+ * interleaved (row 2j = gate j, row 2j+1 = up j) and writes N/2 outputs; the
+ * residual of MTL_EPI_RESIDUAL has row stride ldy and may alias y.  When
+ * pad_period > 0 (store epilogue), output column n with
+ * n % pad_period == pad_col is set to -inf (AUDIO_PAD_CODE, model.py:292).
+ * M <= 4, K <= 8192, K % 8 == 0. */
+int mtl_bf16_linear(const uint16_t* x, int M, int K, int N, const uint16_t* W, const uint16_t* norm_w, float eps,
+                    uint16_t* x_normed, int pad_period, int pad_col, int epilogue, const uint16_t* residual,
+                    uint16_t* y, int ldy, mtl_stream_t stream);
+
+/* y[r] = RMSNorm(x[r]) * weight for bf16 rows of length K (Qwen3RMSNorm as
+ * restated at model.py:34-40: fp32 statistics, bf16 rounding before and after
+ * the weight multiply). */
+int mtl_rmsnorm(const uint16_t* x, int rows, int K, int ldx, const uint16_t* weight, float eps, uint16_t* y,
+                int ldy, mtl_stream_t stream);
+
+/* out[r] = index of the first maximum of row r (torch.argmax semantics,
+ * sampling.py:84-85) of bf16 logits [rows, ld]. */
+int mtl_argmax_rows(const uint16_t* x, int rows, int cols, int ld, int64_t* out, mtl_stream_t stream);
+
+/* out[0] = first-index argmax of one bf16 row of `cols` values, ignoring the
+ * `n_excluded` (<= 8) column indices listed in HOST array `excluded` (the
+ * greedy text decision of generate_fast, fast.py:481-514, with the -inf
+ * writes of fast.py:487 and 507-511 folded in). */
+int mtl_argmax_masked(const uint16_t* x, int cols, const int32_t* excluded, int n_excluded, int64_t* out,
+                      mtl_stream_t stream);
+
+/* Round-to-nearest W4 quantisation of a bf16 weight [N, K] exactly as
+ * FastMossTTS._quantize (fast.py:85-96) / gptq.rtn_quantize (gptq.py:54-64):
+ * q uint8 [N, K] codes and qsz bf16 [K/g, N, 2] = (scale, min + 8 scale). */
+int mtl_w4_rtn_quantize(const uint16_t* w, int N, int K, int group_size, uint8_t* q, uint16_t* qsz,
+                        mtl_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

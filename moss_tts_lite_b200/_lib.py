@@ -41,6 +41,19 @@ SIGNATURES = {
     "mtl_w4a16_linear": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p,
                                   _c_int, _c_void_p, _c_void_p, _c_float, _c_int, _c_void_p, _c_void_p,
                                   _c_int, _c_void_p, _c_size_t, _c_void_p]),
+    "mtl_embed_sum": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_void_p, _c_int, _c_void_p, _c_void_p]),
+    "mtl_attn_scratch_bytes": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_size_p]),
+    "mtl_attn_decode": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                 ctypes.c_longlong, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                 _c_void_p, _c_void_p, _c_size_t, _c_void_p]),
+    "mtl_bf16_linear": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_float, _c_void_p,
+                                 _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_int, _c_void_p]),
+    "mtl_argmax_rows": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
+    "mtl_argmax_masked": (_c_int, [_c_void_p, _c_int, ctypes.POINTER(ctypes.c_int32), _c_int, _c_void_p,
+                                   _c_void_p]),
+    "mtl_rmsnorm": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_float, _c_void_p, _c_int,
+                             _c_void_p]),
+    "mtl_w4_rtn_quantize": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p]),
 }
 
 
@@ -94,3 +107,9 @@ def w4_plan(M: int, K: int, N: int, g: int, fmt: int) -> tuple[int, int]:
     sb = ctypes.c_size_t(0)
     call("mtl_w4_plan", M, K, N, g, fmt, ctypes.byref(tb), ctypes.byref(sb))
     return int(tb.value), int(sb.value)
+
+
+def attn_scratch_bytes(streams: int, n_heads: int, n_kv: int, splits: int) -> int:
+    out = ctypes.c_size_t(0)
+    call("mtl_attn_scratch_bytes", streams, n_heads, n_kv, splits, ctypes.byref(out))
+    return int(out.value)

@@ -14,6 +14,17 @@
 #include <tuple>
 
 namespace mtl {
+cudaError_t launch_embed_sum(const int64_t* ids, int M, const uint16_t* emb_text, int text_vocab,
+                             const uint16_t* emb_audio, int H, uint16_t* out, cudaStream_t s, int use_pdl);
+cudaError_t launch_attn_decode(const AttnArgs& a, int streams, cudaStream_t s, int use_pdl);
+cudaError_t launch_bf16_gemv(const Bf16GemvArgs& a, int num_sms, cudaStream_t s, int use_pdl);
+cudaError_t launch_argmax_rows(const uint16_t* x, int rows, int cols, int ld, int64_t* out, cudaStream_t s,
+                               int use_pdl);
+cudaError_t launch_rtn_quantize(const uint16_t* w, int N, int K, int g, uint8_t* q, uint16_t* qsz, cudaStream_t s);
+cudaError_t launch_argmax_masked(const uint16_t* x, int cols, const int* excl, int n_excl, int64_t* out,
+                                 cudaStream_t s, int use_pdl);
+cudaError_t launch_rmsnorm_rows(const uint16_t* x, int rows, int K, int ldx, const uint16_t* w, float eps,
+                                uint16_t* y, int ldy, cudaStream_t s, int use_pdl);
 cudaError_t w4_pack_gptq(const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
                          const int32_t* perm, int K, int N, int g, uint8_t* tiles, cudaStream_t s);
 cudaError_t w4_pack_ref(const uint8_t* q, const uint16_t* qsz, int K, int N, int g, uint8_t* tiles,
@@ -210,6 +221,135 @@ int mtl_w4a16_linear(const uint16_t* x, int ldx, int M, int K, int N, int group_
     if (e != cudaSuccess) return cuda_fail(e, "mtl_w4a16_linear launch");
   }
   return MTL_OK;
+}
+
+int mtl_embed_sum(const int64_t* ids, int M, const uint16_t* emb_text, int text_vocab, const uint16_t* emb_audio,
+                  int hidden, uint16_t* out, mtl_stream_t stream) {
+  if (!ids || !emb_text || !emb_audio || !out) return fail(MTL_E_INVALID, "mtl_embed_sum: NULL pointer");
+  if (M < 1 || hidden <= 0 || hidden % 8 || text_vocab <= 0)
+    return fail(MTL_E_INVALID, "mtl_embed_sum: M=%d hidden=%d text_vocab=%d", M, hidden, text_vocab);
+  if (!aligned(emb_text, 16) || !aligned(emb_audio, 16) || !aligned(out, 16))
+    return fail(MTL_E_ALIGN, "mtl_embed_sum: tables and out must be 16-byte aligned");
+  cudaError_t e = mtl::launch_embed_sum(ids, M, emb_text, text_vocab, emb_audio, hidden, out, stream, use_pdl());
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_embed_sum");
+}
+
+static size_t attn_partial_floats(int streams, int n_heads, int n_kv, int splits) {
+  return (size_t)streams * n_kv * splits * (n_heads / n_kv) * (2 + mtl::kHeadDim);
+}
+static size_t attn_counter_bytes(int streams, int n_kv) { return ((size_t)streams * n_kv * 4 + 255) / 256 * 256; }
+
+int mtl_attn_scratch_bytes(int streams, int n_heads, int n_kv, int splits, size_t* out) {
+  if (!out || streams < 1 || n_kv < 1 || n_heads < n_kv || n_heads % n_kv || splits < 1)
+    return fail(MTL_E_INVALID, "mtl_attn_scratch_bytes: bad arguments");
+  *out = attn_counter_bytes(streams, n_kv) + attn_partial_floats(streams, n_heads, n_kv, splits) * 4;
+  return MTL_OK;
+}
+
+int mtl_attn_decode(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_t* k_norm_w,
+                    const uint16_t* rope_cos, const uint16_t* rope_sin, uint16_t* k_cache, uint16_t* v_cache,
+                    long long cache_stream_stride, int max_seq, const int64_t* pos, int streams, int n_heads,
+                    int n_kv, int head_dim, int splits, uint16_t* out, void* scratch, size_t scratch_bytes,
+                    mtl_stream_t stream) {
+  if (!qkv || !q_norm_w || !k_norm_w || !rope_cos || !rope_sin || !k_cache || !v_cache || !pos || !out || !scratch)
+    return fail(MTL_E_INVALID, "mtl_attn_decode: NULL pointer");
+  if (head_dim != mtl::kHeadDim) return fail(MTL_E_UNSUPPORTED, "head_dim %d (only 128)", head_dim);
+  if (n_kv < 1 || n_heads % n_kv || n_heads / n_kv > mtl::kAttnMaxRep)
+    return fail(MTL_E_UNSUPPORTED, "n_heads=%d n_kv=%d (n_heads/n_kv must divide and be <= 8)", n_heads, n_kv);
+  if (streams < 1 || max_seq < 1 || splits < 1 || splits > 64)
+    return fail(MTL_E_INVALID, "streams=%d max_seq=%d splits=%d", streams, max_seq, splits);
+  if ((long long)splits * mtl::kAttnMaxChunk < max_seq)
+    return fail(MTL_E_INVALID, "splits=%d too few for max_seq=%d (need >= %d)", splits, max_seq,
+                (max_seq + mtl::kAttnMaxChunk - 1) / mtl::kAttnMaxChunk);
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || cache_stream_stride % 8)
+    return fail(MTL_E_ALIGN, "KV cache must be 16-byte aligned");
+  size_t need = 0;
+  mtl_attn_scratch_bytes(streams, n_heads, n_kv, splits, &need);
+  if (scratch_bytes < need) return fail(MTL_E_SCRATCH, "attention scratch %zu < %zu", scratch_bytes, need);
+  if (!aligned(scratch, 256)) return fail(MTL_E_ALIGN, "scratch must be 256-byte aligned");
+  mtl::AttnArgs a{};
+  a.qkv = qkv;
+  a.q_norm_w = q_norm_w;
+  a.k_norm_w = k_norm_w;
+  a.rope_cos = rope_cos;
+  a.rope_sin = rope_sin;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.cache_stream_stride = cache_stream_stride;
+  a.max_seq = max_seq;
+  a.pos = pos;
+  a.nh = n_heads;
+  a.nkv = n_kv;
+  a.splits = splits;
+  a.out = out;
+  a.counters = static_cast<int*>(scratch);
+  a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + attn_counter_bytes(streams, n_kv));
+  a.scale = 1.0f / sqrtf((float)head_dim);
+  cudaError_t e = mtl::launch_attn_decode(a, streams, stream, use_pdl());
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_attn_decode");
+}
+
+int mtl_bf16_linear(const uint16_t* x, int M, int K, int N, const uint16_t* W, const uint16_t* norm_w, float eps,
+                    uint16_t* x_normed, int pad_period, int pad_col, int epilogue, const uint16_t* residual,
+                    uint16_t* y, int ldy, mtl_stream_t stream) {
+  if (!x || !W || !y) return fail(MTL_E_INVALID, "mtl_bf16_linear: NULL pointer");
+  if (epilogue < 0 || epilogue > 2) return fail(MTL_E_INVALID, "mtl_bf16_linear: unknown epilogue %d", epilogue);
+  if (epilogue == 1 && !residual) return fail(MTL_E_INVALID, "mtl_bf16_linear: residual epilogue needs residual");
+  if (epilogue == 2 && (N % 2)) return fail(MTL_E_INVALID, "mtl_bf16_linear: SwiGLU needs an even N");
+  const int nout = epilogue == 2 ? N / 2 : N;
+  if (M < 1 || M > mtl::kGemvMaxM || K <= 0 || K > mtl::kGemvMaxK || K % 8 || N <= 0 || ldy < nout)
+    return fail(MTL_E_INVALID, "mtl_bf16_linear: M=%d K=%d N=%d ldy=%d (M<=4, K<=8192, K%%8==0)", M, K, N, ldy);
+  if (pad_period < 0 || (pad_period > 0 && (pad_col < 0 || pad_col >= pad_period)))
+    return fail(MTL_E_INVALID, "mtl_bf16_linear: pad_period=%d pad_col=%d", pad_period, pad_col);
+  if (!aligned(W, 16)) return fail(MTL_E_ALIGN, "mtl_bf16_linear: W must be 16-byte aligned");
+  mtl::Bf16GemvArgs a{};
+  a.x = x;
+  a.M = M;
+  a.K = K;
+  a.N = N;
+  a.W = W;
+  a.norm_w = norm_w;
+  a.eps = eps;
+  a.x_normed = x_normed;
+  a.pad_period = pad_period;
+  a.pad_col = pad_col;
+  a.epi = epilogue;
+  a.residual = residual;
+  a.y = y;
+  a.ldy = ldy;
+  cudaError_t e = mtl::launch_bf16_gemv(a, num_sms(), stream, use_pdl());
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_bf16_linear");
+}
+
+int mtl_argmax_rows(const uint16_t* x, int rows, int cols, int ld, int64_t* out, mtl_stream_t stream) {
+  if (!x || !out || rows < 1 || cols < 1 || ld < cols) return fail(MTL_E_INVALID, "mtl_argmax_rows: bad arguments");
+  cudaError_t e = mtl::launch_argmax_rows(x, rows, cols, ld, out, stream, use_pdl());
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_argmax_rows");
+}
+
+int mtl_argmax_masked(const uint16_t* x, int cols, const int32_t* excluded, int n_excluded, int64_t* out,
+                      mtl_stream_t stream) {
+  if (!x || !out || cols < 1 || n_excluded < 0 || n_excluded > 8 || (n_excluded && !excluded))
+    return fail(MTL_E_INVALID, "mtl_argmax_masked: bad arguments");
+  cudaError_t e = mtl::launch_argmax_masked(x, cols, excluded, n_excluded, out, stream, use_pdl());
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_argmax_masked");
+}
+
+int mtl_rmsnorm(const uint16_t* x, int rows, int K, int ldx, const uint16_t* weight, float eps, uint16_t* y,
+                int ldy, mtl_stream_t stream) {
+  if (!x || !weight || !y || rows < 1 || K < 1 || ldx < K || ldy < K)
+    return fail(MTL_E_INVALID, "mtl_rmsnorm: bad arguments");
+  cudaError_t e = mtl::launch_rmsnorm_rows(x, rows, K, ldx, weight, eps, y, ldy, stream, use_pdl());
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_rmsnorm");
+}
+
+int mtl_w4_rtn_quantize(const uint16_t* w, int N, int K, int group_size, uint8_t* q, uint16_t* qsz,
+                        mtl_stream_t stream) {
+  if (!w || !q || !qsz) return fail(MTL_E_INVALID, "mtl_w4_rtn_quantize: NULL pointer");
+  if (!valid_group(group_size) || K % group_size || N < 1)
+    return fail(MTL_E_INVALID, "mtl_w4_rtn_quantize: N=%d K=%d group_size=%d", N, K, group_size);
+  cudaError_t e = mtl::launch_rtn_quantize(w, N, K, group_size, q, qsz, stream);
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4_rtn_quantize");
 }
 
 }  // extern "C"

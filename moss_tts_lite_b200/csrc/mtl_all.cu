@@ -1,4 +1,5 @@
 // Single translation unit for libmtl_b200.so (device globals such as the
 // error word are shared by every kernel without relocatable device code).
 #include "w4_gemv.cu"
+#include "step_kernels.cu"
 #include "capi.cu"

@@ -1,0 +1,611 @@
+"""CUDA-graph W4 / bf16 decode for MOSS-TTS on the sm_100a kernels.
+
+Drop-in for ``moss_tts_lite.fast`` (fast.py:31-610 of the reference):
+``FastMossTTS(model, quant=..., w4_group_size=...)`` with ``capture()``,
+``step(row, pos, audio2)``, ``prefill(input_ids)`` and the static output
+buffers, plus ``generate_fast``.  What changes is the step itself:
+
+* the reference replays 38 piecewise graphs per step with 36 eager
+  attention calls between them (fast.py:308-325) and ~2,300 torch kernels;
+* here ONE graph per phase holds the whole step - embedding sum, per layer
+  [q|k|v W4 GEMV with the input RMSNorm fused in] -> [q/k-norm + RoPE + KV
+  append + split-KV GQA attention] -> [o W4 GEMV + residual] -> [gate|up W4
+  GEMV with the post-attention RMSNorm and SwiGLU fused] -> [down W4 GEMV +
+  residual], then the final norm fused into the head GEMVs: 5 kernels per
+  layer, 183 per step.  The decode position is read from ``pos_dev`` on the
+  device, so one graph serves every cache length.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from . import kernels
+from .generate import GenResult
+from .model import (AUDIO_DELAY_SLOT_TOKEN_ID, AUDIO_END_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_PAD_CODE,
+                    AUDIO_START_TOKEN_ID, AUDIO_VOCAB, IM_END_TOKEN_ID, LIN_NAMES, N_VQ, PAD_TOKEN_ID,
+                    RMS_EPS, HiddenState)
+from .quant import W4Weight
+
+_INT64_MAX = 9223372036854775807
+_LIN_NAMES = LIN_NAMES
+_FUSE_BLOCK = 32  # gate/up interleave granularity of the SwiGLU epilogue
+
+
+# ------------------------------------------------------------------ linears
+class _W4Lin:
+    """A packed W4 linear (possibly fused q|k|v or gate|up)."""
+
+    def __init__(self, w: W4Weight):
+        self.w = w
+        self.N = w.N
+
+    def __call__(self, x, out, *, norm_weight=None, residual=None, swiglu=False):
+        return self.w.linear(x, out=out, norm_weight=norm_weight, norm_eps=RMS_EPS,
+                             residual=residual, swiglu=swiglu)
+
+
+class _Bf16Lin:
+    """A bf16 linear (F.linear semantics) on the bf16 GEMV kernel."""
+
+    def __init__(self, W: torch.Tensor):
+        self.W = W
+        self.N = W.shape[0]
+
+    def __call__(self, x, out, *, norm_weight=None, residual=None, swiglu=False):
+        M = x.numel() // x.shape[-1]
+        for r0 in range(0, M, 4):
+            r1 = min(M, r0 + 4)
+            kernels.bf16_linear(x.view(M, -1)[r0:r1], self.W, out.view(M, -1)[r0:r1], norm_weight=norm_weight,
+                                eps=RMS_EPS, residual=None if residual is None else residual.view(M, -1)[r0:r1],
+                                swiglu=swiglu)
+        return out
+
+
+def _interleave_rows(a: torch.Tensor, b: torch.Tensor, block: int) -> torch.Tensor:
+    """[N, ...] x2 -> [2N, ...] with blocks of `block` rows alternating a, b."""
+    n = a.shape[0]
+    rest = a.shape[1:]
+    return torch.stack([a.reshape(n // block, block, *rest), b.reshape(n // block, block, *rest)], 1) \
+        .reshape(2 * n, *rest)
+
+
+def _interleave_cols(a: torch.Tensor, b: torch.Tensor, block: int) -> torch.Tensor:
+    """qsz [G, N, 2] x2 -> [G, 2N, 2] interleaved along N in blocks."""
+    return _interleave_rows(a.transpose(0, 1), b.transpose(0, 1), block).transpose(0, 1).contiguous()
+
+
+def bf16_linears(m) -> list:
+    """Fused bf16 linears per layer.  The model's per-projection tensors are
+    replaced by views into the fused ones (no second copy stays alive)."""
+    lins = []
+    for lyr in m.layers:
+        qkv = torch.cat([lyr["q"], lyr["k"], lyr["v"]], 0).contiguous()
+        nq, nk = lyr["q"].shape[0], lyr["k"].shape[0]
+        lyr["q"], lyr["k"], lyr["v"] = qkv[:nq], qkv[nq:nq + nk], qkv[nq + nk:]
+        gu = torch.stack([lyr["gate"], lyr["up"]], 1).reshape(-1, lyr["gate"].shape[1]).contiguous()
+        lyr["gate"], lyr["up"] = gu[0::2], gu[1::2]
+        lins.append({"qkv": _Bf16Lin(qkv), "o": _Bf16Lin(lyr["o"]), "gu": _Bf16Lin(gu),
+                     "down": _Bf16Lin(lyr["down"])})
+    return lins
+
+
+def w4_from_codes(recs: dict, group_size: int) -> dict:
+    """{name: (q uint8 [N, K], qsz bf16 [K/g, N, 2])} of one layer -> fused
+    packed W4 linears (q|k|v concatenated, gate|up interleaved)."""
+    q = torch.cat([recs["q"][0], recs["k"][0], recs["v"][0]], 0)
+    qsz = torch.cat([recs["q"][1], recs["k"][1], recs["v"][1]], 1)
+    out = {"qkv": _W4Lin(W4Weight.from_ref(q, qsz, group_size))}
+    out["o"] = _W4Lin(W4Weight.from_ref(recs["o"][0], recs["o"][1], group_size))
+    gq = _interleave_rows(recs["gate"][0], recs["up"][0], _FUSE_BLOCK)
+    gs = _interleave_cols(recs["gate"][1], recs["up"][1], _FUSE_BLOCK)
+    out["gu"] = _W4Lin(W4Weight.from_ref(gq, gs, group_size))
+    out["down"] = _W4Lin(W4Weight.from_ref(recs["down"][0], recs["down"][1], group_size))
+    return out
+
+
+# ------------------------------------------------------------------- engine
+class _StepEngine:
+    """Launch sequence of one decode step (batch 1) over static buffers."""
+
+    def __init__(self, m, lins: list, buffers=None):
+        self.m = m
+        self.lins = lins
+        dev = m.device
+        H, D = m.hidden_size, m.head_dim
+        bf = torch.bfloat16
+        b = buffers
+        self.ids_row = b.ids_row if b is not None else torch.zeros(1, 1, N_VQ + 1, dtype=torch.long, device=dev)
+        self.pos_dev = b.pos_dev if b is not None else torch.zeros(1, dtype=torch.long, device=dev)
+        self.h = (b.h_static if b is not None else torch.zeros(1, 1, H, dtype=bf, device=dev)).view(1, H)
+        self.h_final = b.h_final if b is not None else torch.zeros(1, H, dtype=bf, device=dev)
+        self.lt = b.lt_static if b is not None else torch.zeros(m.text_vocab, dtype=bf, device=dev)
+        self.la = b.la_static if b is not None else torch.zeros(N_VQ, AUDIO_VOCAB, dtype=bf, device=dev)
+        self.two = b.two_static if b is not None else torch.zeros(2, dtype=bf, device=dev)
+        nq = m.n_heads * D
+        self.qkv = torch.zeros(1, nq + 2 * m.n_kv_heads * D, dtype=bf, device=dev)
+        self.attn = torch.zeros(1, nq, dtype=bf, device=dev)
+        inter = lins[0]["gu"].N // 2
+        self.act = torch.zeros(1, inter, dtype=bf, device=dev)
+        self.splits = max(16, math.ceil(m.max_seq_len / 512))
+        if self.splits > 64:
+            raise ValueError(f"max_seq_len {m.max_seq_len} > 32768 is not served by the decode attention")
+        from . import _lib
+        nbytes = _lib.attn_scratch_bytes(1, m.n_heads, m.n_kv_heads, self.splits)
+        self.attn_scratch = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        self.emb_audio = getattr(m, "emb_audio", None)
+        if self.emb_audio is None:   # reference MossTTSModel: stack its 32 tables once
+            self.emb_audio = torch.stack(list(m.emb_ext), 0).contiguous()
+        self.head_audio2d = m.head_audio.view(N_VQ * AUDIO_VOCAB, H)
+
+    def backbone(self) -> None:
+        m = self.m
+        kernels.embed_sum(self.ids_row.view(1, N_VQ + 1), m.embed_tokens, self.emb_audio, self.h)
+        for li in range(m.n_layers):
+            lyr, L = m.layers[li], self.lins[li]
+            L["qkv"](self.h, self.qkv, norm_weight=lyr["input_layernorm"])
+            kernels.attn_decode(self.qkv, lyr["q_norm"], lyr["k_norm"], m.rope_cos, m.rope_sin,
+                                m.k_cache[li], m.v_cache[li], self.pos_dev, m.n_heads, m.n_kv_heads,
+                                self.splits, self.attn, self.attn_scratch)
+            L["o"](self.attn, self.h, residual=self.h)
+            L["gu"](self.h, self.act, norm_weight=lyr["post_attention_layernorm"], swiglu=True)
+            L["down"](self.act, self.h, residual=self.h)
+
+    def heads(self, audio2: bool) -> None:
+        m = self.m
+        if audio2:
+            kernels.bf16_linear(self.h, m.head_2way, self.two.view(1, 2), norm_weight=m.final_norm,
+                                eps=RMS_EPS, x_normed=self.h_final)
+        else:
+            kernels.bf16_linear(self.h, m.head_text, self.lt.view(1, -1), norm_weight=m.final_norm,
+                                eps=RMS_EPS, x_normed=self.h_final)
+        kernels.bf16_linear(self.h, self.head_audio2d, self.la.view(1, -1), norm_weight=m.final_norm,
+                            eps=RMS_EPS, pad_period=AUDIO_VOCAB, pad_col=AUDIO_PAD_CODE)
+
+    def final_norm(self) -> None:
+        kernels.rmsnorm(self.h, self.m.final_norm, self.h_final, RMS_EPS)
+
+    def decode_row(self, row: torch.Tensor, pos: int) -> torch.Tensor:
+        """Eager decode of one row at ``pos``: returns a copy of the final-normed hidden [1, H]."""
+        self.ids_row.view(-1).copy_(row.view(-1))
+        self.pos_dev.fill_(pos)
+        self.backbone()
+        self.final_norm()
+        return self.h_final.clone()
+
+    def prefill_rows(self, ids: torch.Tensor) -> torch.Tensor:
+        """Prompt rows [L, 33] decoded one position at a time (each row's
+        math is the batched prefill's row math).  Returns [L, H]."""
+        L = ids.shape[0]
+        out = torch.empty(L, self.m.hidden_size, dtype=torch.bfloat16, device=self.m.device)
+        for t in range(L):
+            self.ids_row.view(-1).copy_(ids[t])
+            self.pos_dev.fill_(t)
+            self.backbone()
+            kernels.rmsnorm(self.h, self.m.final_norm, out[t:t + 1], RMS_EPS)
+        return out
+
+
+# --------------------------------------------------------------- FastMossTTS
+class FastMossTTS:
+    """CUDA-graph decoder around a MossTTSModel (weights / cache are shared)."""
+
+    def __init__(self, model, enable_gqa: bool = True, gqa_max_len: int = 640,
+                 quant: str | None = None, inner_k_tiles: int = 8, w4_group_size: int = 128):
+        self.m = model
+        dev = model.device
+        if dev.type != "cuda":
+            raise RuntimeError("FastMossTTS runs on CUDA (sm_100a) only")
+        self.enable_gqa = enable_gqa
+        self.gqa_max_len = gqa_max_len
+        self.quant = quant
+        if quant not in (None, "w8", "w4"):
+            raise ValueError(f"unsupported quant mode {quant!r} (None, 'w8' or 'w4')")
+        if quant == "w8":
+            raise NotImplementedError("the W8 tier is not part of the B200 W4 decode path")
+        self.inner_k_tiles = inner_k_tiles
+        if w4_group_size not in (32, 64, 128, 256):
+            raise ValueError("w4_group_size must be 32/64/128/256")
+        self.w4_group_size = w4_group_size
+        bf = model.dtype
+        self.ids_row = torch.zeros(1, 1, N_VQ + 1, dtype=torch.long, device=dev)
+        self.pos_dev = torch.zeros(1, dtype=torch.long, device=dev)
+        self.q_static = torch.zeros(1, model.n_heads, 1, model.head_dim, dtype=bf, device=dev)
+        self.o_static = torch.zeros(1, model.hidden_size, dtype=bf, device=dev)
+        self.h_static = torch.zeros(1, 1, model.hidden_size, dtype=bf, device=dev)
+        self.h_final = torch.zeros(1, model.hidden_size, dtype=bf, device=dev)
+        self.lt_static = torch.zeros(model.text_vocab, dtype=bf, device=dev)
+        self.la_static = torch.zeros(N_VQ, AUDIO_PAD_CODE + 1, dtype=bf, device=dev)
+        self.two_static = torch.zeros(2, dtype=bf, device=dev)
+        self.lt_buf = torch.full((model.text_vocab,), float("-inf"), dtype=bf, device=dev)
+        self.qlayers: list | None = None
+        if quant == "w4":
+            self._quantize()
+        else:
+            self._lins = bf16_linears(model)
+        self.engine = _StepEngine(model, self._lins, buffers=self)
+        self.graphs: list | None = None
+        self.capture_stream = torch.cuda.Stream(device=dev)
+
+    def _quantize(self) -> None:
+        """RTN W4 of the 7 backbone linears per layer with the reference's exact
+        codes and (scale, zero) (fast.py:70-105), packed into the tile layout;
+        the bf16 originals are dropped like the reference does."""
+        m = self.m
+        self.qlayers = []
+        self._lins = []
+        for li in range(m.n_layers):
+            lyr = m.layers[li]
+            recs = {name: kernels.rtn_quantize(lyr[name], self.w4_group_size) for name in _LIN_NAMES}
+            self._lins.append(w4_from_codes(recs, self.w4_group_size))
+            self.qlayers.append({name: self._lins[-1] for name in ("qkv", "o", "gu", "down")})
+            for name in _LIN_NAMES:
+                lyr.pop(name)
+            del recs
+        torch.cuda.empty_cache()
+
+    def _linear(self, x: torch.Tensor, li: int, name: str) -> torch.Tensor:
+        """One named backbone projection (the reference boundary of fast.py:107-121)
+        computed through the fused layer weights and sliced."""
+        m = self.m
+        L = self._lins[li]
+        D = m.head_dim
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        if name in ("q", "k", "v"):
+            out = torch.empty(x2.shape[0], L["qkv"].N, dtype=torch.bfloat16, device=x.device)
+            L["qkv"](x2, out)
+            nq, nk = m.n_heads * D, m.n_kv_heads * D
+            sl = {"q": slice(0, nq), "k": slice(nq, nq + nk), "v": slice(nq + nk, nq + 2 * nk)}[name]
+            y = out[:, sl]
+        elif name in ("gate", "up"):
+            lin = L["gu"]
+            out = torch.empty(x2.shape[0], lin.N, dtype=torch.bfloat16, device=x.device)
+            lin(x2, out)
+            if isinstance(lin, _W4Lin):
+                y = out.view(x2.shape[0], -1, 2, _FUSE_BLOCK)[:, :, 0 if name == "gate" else 1].reshape(x2.shape[0], -1)
+            else:
+                y = out[:, 0::2] if name == "gate" else out[:, 1::2]
+        else:
+            lin = L[name]
+            y = torch.empty(x2.shape[0], lin.N, dtype=torch.bfloat16, device=x.device)
+            lin(x2, y)
+        return y.contiguous().reshape(*x.shape[:-1], y.shape[-1])
+
+    def prefill(self, input_ids: torch.Tensor) -> HiddenState:
+        """fast.py:251-270: prompt [1, L, 33] -> final-normed hidden [1, L, H]."""
+        m = self.m
+        if input_ids.dim() != 3 or input_ids.shape[0] != 1 or input_ids.shape[-1] != N_VQ + 1:
+            raise ValueError(f"expected input ids [1, L, {N_VQ + 1}], got {tuple(input_ids.shape)}")
+        t = int(input_ids.shape[1])
+        if t > m.max_seq_len:
+            raise ValueError(f"seq len {t} exceeds KV cache {m.max_seq_len}")
+        m.reset()
+        ids = input_ids.to(device=m.device, dtype=torch.long)
+        h = self.engine.prefill_rows(ids[0])
+        m._seq = t
+        return HiddenState(h.view(1, t, m.hidden_size))
+
+    def _run_eager(self, audio2: bool) -> None:
+        self.engine.backbone()
+        self.engine.heads(audio2)
+
+    def capture(self) -> None:
+        """Warm up, then capture one whole-step graph per phase (text / audio2)."""
+        if self.graphs is not None:
+            return
+        m = self.m
+        self.pos_dev.fill_(m.max_seq_len - 1)       # scratch slot, as fast.py:280-281
+        s = torch.cuda.Stream(device=m.device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                self._run_eager(False)
+                self._run_eager(True)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        pool = torch.cuda.graph_pool_handle()
+        self.graphs = []
+        for audio2 in (False, True):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool, stream=self.capture_stream):
+                self._run_eager(audio2)
+            self.graphs.append(g)
+        torch.cuda.synchronize()
+
+    def step(self, row: torch.Tensor | None, pos: int, audio2: bool = False):
+        """Replay one decode step (fast.py:308-325); outputs alias static buffers."""
+        if self.graphs is None:
+            raise RuntimeError("call capture() first")
+        if row is not None:
+            src = row if row.dim() == 2 else row[0]
+            if src.data_ptr() != self.ids_row.data_ptr():
+                self.ids_row.copy_(src)
+        self.pos_dev.fill_(pos)
+        self.graphs[1 if audio2 else 0].replay()
+        return self.lt_static, self.la_static, self.h_final, self.two_static
+
+
+# ------------------------------------------------------------ generate_fast
+_WD_LOW_ENERGY_CH0 = frozenset(
+    (9, 60, 109, 123, 163, 209, 216, 365, 399, 402, 421, 580, 715, 734,
+     774, 795, 827, 888, 890, 936, 971, 996, 1001))
+_WD_SEGMENT_FLOOR = 640
+_WD_SEGMENT_BACKSTOP_RUN = 32
+
+
+@dataclass
+class GenResultWatchdog(GenResult):
+    """GenResult + watchdog metadata (fast.py:334-340)."""
+
+    watchdog_triggered: bool = False
+    watchdog_reason: str = ""
+    watchdog_stats: dict = field(default_factory=dict)
+
+
+class _Decider:
+    """Device-side token decisions of one generate_fast step: greedy argmax
+    over the 32 audio rows and the masked text decision, fetched with one
+    device->host copy."""
+
+    def __init__(self, fast: FastMossTTS):
+        dev = fast.m.device
+        self.fast = fast
+        self.dev_out = torch.zeros(N_VQ + 1, dtype=torch.long, device=dev)
+        self.host = torch.zeros(N_VQ + 1, dtype=torch.long, pin_memory=True)
+
+    def run(self, la, text_src, text_excluded, need_text: bool, need_audio: bool):
+        if need_audio:
+            kernels.argmax_rows(la, self.dev_out[1:])
+        if need_text:
+            kernels.argmax_masked(text_src, self.dev_out[0:1], text_excluded)
+        self.host.copy_(self.dev_out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return self.host.tolist()
+
+
+@torch.inference_mode()
+def generate_fast(
+    fast: FastMossTTS,
+    prompt: dict,
+    max_new_tokens=4096,
+    seed=1234,
+    greedy=False,
+    text_temperature=1.5,
+    text_top_p=1.0,
+    text_top_k=50,
+    audio_temperature=1.7,
+    audio_top_p=0.8,
+    audio_top_k=25,
+    audio_repetition_penalty=1.0,
+    stats: dict | None = None,
+    watchdog: bool = True,
+    watchdog_silence_frames: int | None = None,
+    watchdog_max_segment_frames: int | None = None,
+    max_requested_pause_s: float | None = None,
+) -> GenResult:
+    """Delay-pattern generation on FastMossTTS with the control flow of the
+    reference's generate_fast (fast.py:342-610): same text decision, per-
+    channel audio mask, watchdog and stopping rules.  Greedy decisions are
+    first-index argmaxes computed on the device; sampled decisions use the
+    fused sampling kernel (see moss_tts_lite_b200.sampling)."""
+    from .sampling import sample_rows
+    model = fast.m
+    device = model.device
+    input_ids = prompt["input_ids"].to(device=device, dtype=torch.long)
+    attention_mask = prompt.get("attention_mask")
+    if input_ids.dim() != 3 or input_ids.shape[0] != 1 or input_ids.shape[-1] != N_VQ + 1:
+        raise ValueError(f"expected prompt input_ids [1, L, {N_VQ + 1}], got {tuple(input_ids.shape)}")
+    if attention_mask is not None:
+        am = attention_mask.to(device)
+        if am.dim() == 1:
+            am = am.unsqueeze(0)
+        if tuple(am.shape) != (1, input_ids.shape[1]):
+            raise ValueError(f"bad attention_mask shape {tuple(am.shape)}")
+        if not bool(am.all()):
+            raise NotImplementedError("batch=1 generate_fast() requires an all-True prompt mask")
+    if int(input_ids.shape[1]) + max_new_tokens > model.max_seq_len:
+        raise ValueError(f"prompt {int(input_ids.shape[1])} + max_new_tokens {max_new_tokens} "
+                         f"exceeds KV cache {model.max_seq_len}")
+    seq_len = int(input_ids.shape[1])
+    _stats = stats if stats is not None else None
+
+    def _t0():
+        if _stats is None:
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    def _t1(e0, slot):
+        if _stats is None:
+            return
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        if slot == "prefill":
+            _stats["prefill"] = (e0, e)
+        else:
+            _stats.setdefault("step_ms", []).append((e0, e))
+
+    if greedy:
+        text_temperature = 0
+        audio_temperature = 0
+    text_do_sample = text_temperature > 0
+    if not text_do_sample:
+        text_temperature = 1
+    audio_do_sample = audio_temperature > 0
+    if not audio_do_sample:
+        audio_temperature = 1
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+
+    col0 = input_ids[0, :, 0].tolist()
+    last0 = col0[-1]
+    is_continuation = last0 in (AUDIO_START_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID)
+    hits = [i for i, c in enumerate(col0) if c == AUDIO_START_TOKEN_ID]
+    start_idx = hits[-1] if hits else -1
+    al = seq_len - start_idx if (is_continuation and start_idx != -1) else 0
+    is_audio = is_continuation and start_idx != -1
+    dl = _INT64_MAX
+    is_stopping = False
+    pre_exclude0 = (PAD_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_DELAY_SLOT_TOKEN_ID, AUDIO_END_TOKEN_ID)
+
+    prev_audio = input_ids[0, :, 1:].tolist()        # generation_ids[:, :, 1:] rows
+    text_steps: list = []
+    audio_steps: list = []
+    n_steps = 0
+    pos = seq_len
+    captured = False
+    decider = _Decider(fast)
+    wd_stop = False
+    wd_reason = ""
+    wd_silent_run = 0
+    wd_peak_segment = 0
+    wd_stats: dict = {}
+    wd_floor = watchdog_max_segment_frames if watchdog_max_segment_frames is not None else _WD_SEGMENT_FLOOR
+    wd_sil = watchdog_silence_frames if watchdog_silence_frames is not None else 64
+    if max_requested_pause_s is not None and max_requested_pause_s > 0:
+        wd_sil = max(wd_sil, math.ceil((max_requested_pause_s + 2.0) * 12.5))
+
+    for time_step in range(max_new_tokens):
+        e0 = _t0()
+        if time_step == 0:
+            hs = fast.prefill(input_ids)
+            if not captured:
+                fast.capture()
+                captured = True
+            _heads_from_hidden(fast, hs.last_hidden[0, -1:], audio2=is_audio)
+        else:
+            fast.step(None, pos, audio2=is_audio)
+            pos += 1
+        _t1(e0, "prefill" if time_step == 0 else "step")
+        lt_step, la_step, two_step = fast.lt_static, fast.la_static, fast.two_static
+
+        next_text = PAD_TOKEN_ID
+        if wd_stop:
+            if dl == _INT64_MAX or dl < N_VQ:
+                next_text = AUDIO_DELAY_SLOT_TOKEN_ID
+            else:
+                next_text = AUDIO_END_TOKEN_ID
+                is_audio = False
+        elif not is_stopping and dl < N_VQ:
+            next_text = AUDIO_DELAY_SLOT_TOKEN_ID
+        elif not is_stopping and dl == N_VQ:
+            next_text = AUDIO_END_TOKEN_ID
+            is_audio = False
+        sampling_text = (not is_stopping) and (not wd_stop) and dl > N_VQ
+        smask = [(al > j) and (dl == _INT64_MAX or j > dl - 1) for j in range(N_VQ)]
+        need_audio = any(smask)
+
+        if (sampling_text and not text_do_sample) or (need_audio and not audio_do_sample):
+            text_src, excluded = two_step, ()
+            if sampling_text and is_audio:
+                excluded = (1,) if time_step == 0 else ()
+            elif sampling_text:
+                text_src = lt_step
+                ex = list(pre_exclude0)
+                if time_step == 0:
+                    ex.append(AUDIO_DELAY_SLOT_TOKEN_ID)
+                if time_step <= N_VQ:
+                    ex.append(IM_END_TOKEN_ID)
+                excluded = tuple(sorted(set(ex)))
+            dec = decider.run(la_step, text_src, excluded,
+                              need_text=sampling_text and not text_do_sample,
+                              need_audio=need_audio and not audio_do_sample)
+        else:
+            dec = None
+
+        if sampling_text:
+            if not text_do_sample:
+                if is_audio:
+                    next_text = AUDIO_GEN_SLOT_TOKEN_ID if dec[0] == 0 else AUDIO_DELAY_SLOT_TOKEN_ID
+                else:
+                    next_text = int(dec[0])
+            else:
+                next_text = sample_rows.text(fast, is_audio, time_step, text_temperature, text_top_k,
+                                             text_top_p, gen)
+        if next_text == AUDIO_START_TOKEN_ID:
+            is_audio = True
+        if next_text == IM_END_TOKEN_ID:
+            is_stopping = True
+
+        next_audio = [AUDIO_PAD_CODE] * N_VQ
+        if need_audio:
+            if not audio_do_sample:
+                toks = dec[1:]
+            else:
+                toks = sample_rows.audio(fast, smask, audio_temperature, audio_top_k, audio_top_p,
+                                         audio_repetition_penalty, prev_audio, gen)
+            for j in range(N_VQ):
+                if smask[j]:
+                    next_audio[j] = int(toks[j])
+
+        ch0_val = next_audio[0]
+        if watchdog and not wd_stop and is_audio and dl == _INT64_MAX:
+            if ch0_val in _WD_LOW_ENERGY_CH0:
+                wd_silent_run += 1
+            else:
+                wd_silent_run = 0
+            seg_bound = max(wd_floor, 2 * wd_peak_segment)
+            if wd_silent_run >= wd_sil:
+                wd_stop, wd_reason = True, "silence"
+            elif al > seg_bound and wd_silent_run >= _WD_SEGMENT_BACKSTOP_RUN:
+                wd_stop, wd_reason = True, "max_segment"
+            if wd_stop:
+                wd_stats = {"reason": wd_reason, "step": n_steps + 1, "segment_frames": al,
+                            "silent_run": wd_silent_run, "peak_completed_segment": wd_peak_segment,
+                            "silence_threshold_frames": wd_sil, "segment_bound_frames": seg_bound,
+                            "max_requested_pause_s": max_requested_pause_s}
+
+        if next_text in (AUDIO_START_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_DELAY_SLOT_TOKEN_ID):
+            al += 1
+        if next_text == AUDIO_END_TOKEN_ID:
+            wd_peak_segment = max(wd_peak_segment, al)
+            wd_silent_run = 0
+            al = 0
+        if dl == _INT64_MAX and next_text == AUDIO_DELAY_SLOT_TOKEN_ID:
+            dl = 0
+        if dl != _INT64_MAX:
+            dl += 1
+        if dl > N_VQ:
+            dl = _INT64_MAX
+
+        # pageable source: the copy is staged before copy_ returns
+        fast.ids_row.view(-1).copy_(torch.tensor([next_text] + next_audio, dtype=torch.long))
+        prev_audio.append(next_audio)
+        text_steps.append(next_text)
+        audio_steps.append(next_audio)
+        n_steps += 1
+        if is_stopping:
+            break
+        if wd_stop and next_text == AUDIO_END_TOKEN_ID:
+            break
+
+    text_ids = torch.tensor(text_steps, dtype=torch.long) if text_steps else torch.empty(0, dtype=torch.long)
+    audio_frames = (torch.tensor(audio_steps, dtype=torch.long) if audio_steps
+                    else torch.empty(0, N_VQ, dtype=torch.long))
+    if _stats is not None:
+        torch.cuda.synchronize()
+        p = _stats.get("prefill")
+        _stats["prefill_ms"] = float(p[0].elapsed_time(p[1])) if p else None
+        _stats["step_ms"] = [float(a.elapsed_time(b)) for a, b in _stats.get("step_ms", [])]
+        _stats["steps"] = len(_stats["step_ms"])
+    return GenResultWatchdog(text_ids=text_ids, audio_frames=audio_frames,
+                             finished=bool(is_stopping) or bool(wd_stats), n_steps=n_steps,
+                             watchdog_triggered=bool(wd_stats), watchdog_reason=wd_reason,
+                             watchdog_stats=wd_stats)
+
+
+def _heads_from_hidden(fast: FastMossTTS, hv: torch.Tensor, audio2: bool) -> None:
+    """Time step 0 of generate_fast: logits of the final-normed last prompt
+    row (the reference calls model.text_logits / text_logits_2way /
+    audio_logits on it, fast.py:483-524)."""
+    m = fast.m
+    H = m.hidden_size
+    if audio2:
+        kernels.bf16_linear(hv, m.head_2way, fast.two_static.view(1, 2))
+    else:
+        kernels.bf16_linear(hv, m.head_text, fast.lt_static.view(1, -1))
+    kernels.bf16_linear(hv, m.head_audio.view(N_VQ * AUDIO_VOCAB, H), fast.la_static.view(1, -1),
+                        pad_period=AUDIO_VOCAB, pad_col=AUDIO_PAD_CODE)

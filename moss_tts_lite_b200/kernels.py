@@ -1,0 +1,97 @@
+"""Torch-tensor wrappers over the C ABI of libmtl_b200.so.
+
+torch owns the device memory and the current stream; every function here
+launches one of this package's sm_100a kernels on
+``torch.cuda.current_stream()`` and returns without synchronising, so all of
+them can be captured in a CUDA graph.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+
+def _s() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _bf16(t: torch.Tensor, name: str) -> None:
+    if t.dtype != torch.bfloat16:
+        raise TypeError(f"{name} must be bfloat16, got {t.dtype}")
+
+
+def embed_sum(ids: torch.Tensor, emb_text: torch.Tensor, emb_audio: torch.Tensor,
+              out: torch.Tensor) -> torch.Tensor:
+    """ids int64 [M, 33] -> out bf16 [M, H] (model.py:156-161)."""
+    M = ids.numel() // 33
+    _lib.call("mtl_embed_sum", ids.data_ptr(), M, emb_text.data_ptr(), emb_text.shape[0],
+              emb_audio.data_ptr(), emb_text.shape[1], out.data_ptr(), _s())
+    return out
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    K = x.shape[-1]
+    rows = x.numel() // K
+    _lib.call("mtl_rmsnorm", x.data_ptr(), rows, K, K, weight.data_ptr(), ctypes.c_float(eps),
+              out.data_ptr(), K, _s())
+    return out
+
+
+def attn_decode(qkv, q_norm_w, k_norm_w, rope_cos, rope_sin, k_cache_layer, v_cache_layer, pos_dev,
+                n_heads: int, n_kv: int, splits: int, out, scratch, streams: int = 1,
+                cache_stream_stride: int = 0) -> torch.Tensor:
+    max_seq = k_cache_layer.shape[-2]
+    _lib.call("mtl_attn_decode", qkv.data_ptr(), q_norm_w.data_ptr(), k_norm_w.data_ptr(),
+              rope_cos.data_ptr(), rope_sin.data_ptr(), k_cache_layer.data_ptr(), v_cache_layer.data_ptr(),
+              ctypes.c_longlong(cache_stream_stride), max_seq, pos_dev.data_ptr(), streams, n_heads, n_kv,
+              k_cache_layer.shape[-1], splits, out.data_ptr(), scratch.data_ptr(), scratch.numel(), _s())
+    return out
+
+
+def bf16_linear(x: torch.Tensor, W: torch.Tensor, out: torch.Tensor, *, norm_weight=None, eps: float = 1e-6,
+                x_normed=None, pad_period: int = 0, pad_col: int = 0, residual=None,
+                swiglu: bool = False) -> torch.Tensor:
+    """out = epilogue(x W^T) for bf16 W [N, K] (see include/mtl_b200.h)."""
+    K = x.shape[-1]
+    M = x.numel() // K
+    N = W.shape[0]
+    epi = _lib.MTL_EPI_SWIGLU if swiglu else (_lib.MTL_EPI_RESIDUAL if residual is not None else _lib.MTL_EPI_STORE)
+    ldy = out.shape[-1]
+    _lib.call("mtl_bf16_linear", x.data_ptr(), M, K, N, W.data_ptr(), _p(norm_weight), ctypes.c_float(eps),
+              _p(x_normed), pad_period, pad_col, epi, _p(residual), out.data_ptr(), ldy, _s())
+    return out
+
+
+def argmax_rows(x: torch.Tensor, out: torch.Tensor, cols: int | None = None) -> torch.Tensor:
+    """out int64 [rows] = first-index argmax of bf16 x [rows, ld]."""
+    _bf16(x, "x")
+    ld = x.shape[-1]
+    rows = x.numel() // ld
+    _lib.call("mtl_argmax_rows", x.data_ptr(), rows, ld if cols is None else cols, ld, out.data_ptr(), _s())
+    return out
+
+
+def argmax_masked(x: torch.Tensor, out: torch.Tensor, excluded=()) -> torch.Tensor:
+    """out[0] = first-index argmax of the bf16 row ``x`` ignoring ``excluded`` (<= 8 indices)."""
+    ex = list(excluded)
+    arr = (ctypes.c_int32 * max(1, len(ex)))(*ex)
+    _lib.call("mtl_argmax_masked", x.data_ptr(), x.numel(), arr, len(ex), out.data_ptr(), _s())
+    return out
+
+
+def rtn_quantize(w: torch.Tensor, group_size: int = 128) -> tuple[torch.Tensor, torch.Tensor]:
+    """Reference RTN W4 (fast.py:85-96): bf16 [N, K] -> (q uint8 [N, K], qsz bf16 [K/g, N, 2])."""
+    _bf16(w, "w")
+    w = w.contiguous()
+    N, K = w.shape
+    q = torch.empty(N, K, dtype=torch.uint8, device=w.device)
+    qsz = torch.empty(K // group_size, N, 2, dtype=torch.bfloat16, device=w.device)
+    _lib.call("mtl_w4_rtn_quantize", w.data_ptr(), N, K, group_size, q.data_ptr(), qsz.data_ptr(), _s())
+    return q, qsz

@@ -90,9 +90,14 @@ def gptq_dequant(qweight, qzeros, scales_f16, g_idx, zero_offset: int = 0) -> np
 # --------------------------------------------------------------------------
 
 
-def group_scales_from_weight(w: np.ndarray, group_size: int = 128):
-    """Restates gptq.py:35-45 (== fast.py:88-90): asymmetric group min/max.
+def group_scales_from_weight(w: np.ndarray, group_size: int = 128, device: str = "cuda"):
+    """Restates gptq.py:35-45 (== fast.py:88-90): asymmetric group min/max,
+    ``s = clamp((mx - mn) / 15, min=1e-6)``.
 
+    ``device`` selects PyTorch's arithmetic for the division by the Python
+    scalar 15: on CUDA it multiplies by the float reciprocal 1.0f/15.0f, on
+    CPU it divides.  The W4 path of the reference runs on CUDA
+    (fast.py:97 has no CPU kernel), so "cuda" is the default.
     ``w`` float32 [N, K]. Returns ``(s, mn)`` float32 [N, K/g]."""
     n, k = w.shape
     if k % group_size:
@@ -100,20 +105,27 @@ def group_scales_from_weight(w: np.ndarray, group_size: int = 128):
     wg = w.reshape(n, k // group_size, group_size)
     mx = wg.max(-1)
     mn = wg.min(-1)
-    s = np.maximum((mx - mn) / np.float32(15.0), np.float32(1e-6)).astype(np.float32)
+    if device == "cuda":
+        d = ((mx - mn) * (np.float32(1.0) / np.float32(15.0))).astype(np.float32)
+    elif device == "cpu":
+        d = ((mx - mn) / np.float32(15.0)).astype(np.float32)
+    else:
+        raise ValueError(f"device must be 'cuda' or 'cpu', got {device!r}")
+    s = np.maximum(d, np.float32(1e-6)).astype(np.float32)
     return s, mn.astype(np.float32)
 
 
-def rtn_quantize(w_bf16_bits: np.ndarray, group_size: int = 128):
+def rtn_quantize(w_bf16_bits: np.ndarray, group_size: int = 128, device: str = "cuda"):
     """Restates gptq.py:54-64 / fast.py:85-93 (round-to-nearest W4).
 
     ``w_bf16_bits`` uint16 [N, K] bf16 weights. Returns ``(q, s, mn)``:
     uint8 codes [N, K], float32 scale and min [N, K/g]. ``np.rint`` rounds
-    half to even like ``torch.round``."""
+    half to even like ``torch.round``; ``device`` as in
+    group_scales_from_weight."""
     w = bf16_to_f32(w_bf16_bits)
     n, k = w.shape
     g = group_size
-    s, mn = group_scales_from_weight(w, g)
+    s, mn = group_scales_from_weight(w, g, device)
     wg = w.reshape(n, k // g, g)
     q = np.clip(np.rint((wg - mn[..., None]) / s[..., None]), 0, 15)
     return q.astype(np.uint8).reshape(n, k), s, mn

@@ -21,8 +21,8 @@ def _load(name):
 
 @pytest.mark.parametrize("g", [32, 64, 128, 256])
 def test_rtn_quantize_pack_and_dequant_bit_exact(g):
-    z = _load("w4_ref.npz")
-    q, s, mn = ow.rtn_quantize(z[f"g{g}_w"], g)
+    z = _load("w4_ref.npz")          # reference run on CPU
+    q, s, mn = ow.rtn_quantize(z[f"g{g}_w"], g, device="cpu")
     assert np.array_equal(q, z[f"g{g}_q"])
     assert np.array_equal(s.view(np.uint32), z[f"g{g}_s"].view(np.uint32))
     assert np.array_equal(mn.view(np.uint32), z[f"g{g}_mn"].view(np.uint32))
@@ -30,6 +30,16 @@ def test_rtn_quantize_pack_and_dequant_bit_exact(g):
     assert np.array_equal(qsz, z[f"g{g}_qsz"])
     weff = ow.ref_effective_weight(q, qsz, g)
     assert np.array_equal(weff.view(np.uint32), z[f"g{g}_weff"].view(np.uint32))
+
+
+@pytest.mark.parametrize("g", [32, 64, 128, 256])
+def test_rtn_quantize_cuda_semantics_bit_exact(g):
+    """The reference's real W4 path runs on CUDA (tests/golden/make_golden_cuda.py)."""
+    z = _load("w4_ref_cuda.npz")
+    q, s, mn = ow.rtn_quantize(z[f"g{g}_w"], g, device="cuda")
+    assert np.array_equal(q, z[f"g{g}_q"])
+    assert np.array_equal(s.view(np.uint32), z[f"g{g}_s"].view(np.uint32))
+    assert np.array_equal(ow.pack_qsz(s, mn), z[f"g{g}_qsz"])
 
 
 def test_autogptq_pack_unpack_roundtrip():
