@@ -1,0 +1,440 @@
+"""Benchmark: W4 decode steps/s at batch 1 under CUDA graph (config 2 of the
+benchmark: 36 layers, hidden 4096, 32/8 heads, head_dim 128, SwiGLU 12288,
+vocab 151936 + 32 x 1025 audio codebooks, RTN W4 g128, 128-row prompt).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mtl|reference]
+
+One process per GPU (torchrun for N > 1); every GPU runs an independent
+replica on its own utterance (no collective on the data path), so scaling is
+weak and the value is the whole-job steps/s.
+
+* ``value``  - K steps of the device-resident greedy decode loop: one CUDA
+  graph per step (the whole decoder step in the audio phase plus a kernel
+  that feeds the argmax tokens back as the next row), replayed back to back;
+  weights (~3.9 GB per step) stream from HBM (inputs >> L2).
+* ``e2e``    - the same metric through the public API ``generate_fast``
+  (greedy): per step the graph replay, device-side decisions, a device->host
+  read of the 33 tokens, the host FSM and a host->device copy of the next row.
+* ``roofline`` - the dominant kernel (W4 GEMV): one graph of the 144 W4
+  GEMV launches of a step (same weights, same launch order) timed with CUDA
+  events; achieved = algorithmic bytes / average launch time.
+* ``cpu_baseline`` / ``--impl reference`` - the numpy oracle (the CPU
+  restatement of the reference decoder) timed on the host cores on a bounded
+  sample of the same step, scaled to the full model.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(hidden=4096, n_layers=36, n_heads=32, n_kv=8, head_dim=128, inter=12288, vocab=151936,
+           group_size=128, prompt_len=128, std=0.02, seed=0)
+METRIC = "W4 decode steps/s at batch 1 (CUDA graph)"
+MAX_SEQ = 8192
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def _ncu_traffic():
+    """Per-launch DRAM bytes of the W4 GEMV from the committed ncu summary."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "w4_gemv_traffic.json")) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = f"/tmp/mtl_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except Exception:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ model
+def build_fast(dev, seed: int):
+    """Random-init (seeded) full-size synthetic model -> FastMossTTS(quant='w4')."""
+    import torch
+    from moss_tts_lite_b200.fast import FastMossTTS
+    from moss_tts_lite_b200.model import N_VQ, MossTTSModel
+    c = CFG
+    H, D = c["hidden"], c["head_dim"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+
+    def r(*shape):
+        return (torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * c["std"]).to(torch.bfloat16)
+
+    ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=dev)  # noqa: E731
+    w = {"language_model.embed_tokens.weight": r(c["vocab"], H), "language_model.norm.weight": ones(H)}
+    for li in range(c["n_layers"]):
+        p = f"language_model.layers.{li}"
+        w[f"{p}.input_layernorm.weight"] = ones(H)
+        w[f"{p}.post_attention_layernorm.weight"] = ones(H)
+        w[f"{p}.self_attn.q_proj.weight"] = r(c["n_heads"] * D, H)
+        w[f"{p}.self_attn.k_proj.weight"] = r(c["n_kv"] * D, H)
+        w[f"{p}.self_attn.v_proj.weight"] = r(c["n_kv"] * D, H)
+        w[f"{p}.self_attn.o_proj.weight"] = r(H, c["n_heads"] * D)
+        w[f"{p}.self_attn.q_norm.weight"] = ones(D)
+        w[f"{p}.self_attn.k_norm.weight"] = ones(D)
+        w[f"{p}.mlp.gate_proj.weight"] = r(c["inter"], H)
+        w[f"{p}.mlp.up_proj.weight"] = r(c["inter"], H)
+        w[f"{p}.mlp.down_proj.weight"] = r(H, c["inter"])
+    for i in range(N_VQ):
+        w[f"emb_ext.{i}.weight"] = r(1025, H)
+    w["lm_heads.0.weight"] = r(c["vocab"], H)
+    for i in range(N_VQ):
+        w[f"lm_heads.{i + 1}.weight"] = r(1025, H)
+    model = MossTTSModel(w, device=dev, max_seq_len=MAX_SEQ)
+    del w
+    fast = FastMossTTS(model, quant="w4", w4_group_size=c["group_size"])
+    torch.cuda.synchronize()
+    return fast
+
+
+def make_prompt(seed: int):
+    import torch
+    from moss_tts_lite_b200.model import AUDIO_START_TOKEN_ID, N_VQ
+    g = torch.Generator().manual_seed(seed)
+    L = CFG["prompt_len"]
+    ids = torch.zeros(1, L, N_VQ + 1, dtype=torch.long)
+    ids[0, :, 0] = torch.randint(0, 151643, (L,), generator=g)
+    ids[0, :, 1:] = torch.randint(0, 1024, (L, N_VQ), generator=g)
+    ids[0, -1, 0] = AUDIO_START_TOKEN_ID
+    return ids
+
+
+# --------------------------------------------------------------- measures
+def time_decode_loop(fast, steps: int, warmup: int, dist_ctx):
+    """Device-resident greedy decode: `steps` graph replays, CUDA-event timed."""
+    import torch
+    loop = fast.capture_greedy_loop()
+    # continue the utterance after the prompt: capture() parked pos_dev on the
+    # scratch slot, the feed kernel advances it from here on
+    fast.pos_dev.fill_(CFG["prompt_len"])
+    for _ in range(warmup):
+        loop.replay()
+    torch.cuda.synchronize()
+    dist_ctx.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(torch.cuda.current_device())
+    with clocks:
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("mtl_timed")   # ncu --nvtx-include mtl_timed/ selects this region
+        e0.record()
+        for _ in range(steps):
+            loop.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+    dist_ctx.barrier()
+    return e0.elapsed_time(e1), clocks.summary()
+
+
+def time_w4_gemvs(fast, reps: int = 5):
+    """Roofline of the dominant kernel: the 144 W4 GEMV launches of one step
+    in one graph (production order, same buffers and weights)."""
+    import torch
+    eng = fast.engine
+    m = fast.m
+    launches, alg = 0, 0
+
+    def body():
+        nonlocal launches, alg
+        launches, alg = 0, 0
+        for li in range(m.n_layers):
+            lyr, L = m.layers[li], eng.lins[li]
+            L["qkv"](eng.h, eng.qkv, norm_weight=lyr["input_layernorm"])
+            L["o"](eng.attn, eng.h, residual=eng.h)
+            L["gu"](eng.h, eng.act, norm_weight=lyr["post_attention_layernorm"], swiglu=True)
+            L["down"](eng.act, eng.h, residual=eng.h)
+            for name, res in (("qkv", 0), ("o", 1), ("gu", 0), ("down", 1)):
+                w = L[name].w
+                nout = w.N // 2 if name == "gu" else w.N
+                alg += w.tiles.numel() + 2 * w.K + 2 * nout + (2 * w.N if res else 0)
+                launches += 1
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        body()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        body()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    per_launch_s = ms * 1e-3 / launches
+    per_launch_bytes = alg / launches
+    return per_launch_bytes, per_launch_s, launches
+
+
+def time_e2e(fast, prompt, steps: int, warmup: int):
+    """generate_fast (public API, greedy) wall-clock steps/s over steps warmup..warmup+steps."""
+    from moss_tts_lite_b200.fast import generate_fast
+    st = {}
+    res = generate_fast(fast, {"input_ids": prompt}, max_new_tokens=warmup + steps + 1, greedy=True,
+                        watchdog=False, stats=st)
+    wall = st.get("step_wall_s", [])
+    n = min(len(wall) - 1, warmup + steps)
+    if n <= warmup:
+        return None, res.n_steps
+    return (n - warmup) / (wall[n] - wall[warmup]), res.n_steps
+
+
+def cpu_baseline(seconds_budget: float = 20.0):
+    """The numpy oracle decode step on the host cores, bounded sample: 2 of
+    the 36 layers at the cfg2 shapes (fp32 BLAS on precomputed effective
+    weights, KV length 129) plus embedding and audio-phase heads, scaled to
+    the full model.  Returns (steps/s, cores, sample description)."""
+    import numpy as np
+    from oracle import step as ost
+    from oracle.bf16 import f32_to_bf16
+    c = CFG
+    H, D = c["hidden"], c["head_dim"]
+    rng = np.random.default_rng(1)
+
+    def r(*shape):
+        return f32_to_bf16((rng.standard_normal(shape, dtype=np.float32) * np.float32(c["std"])))
+
+    nl = 2
+    w = {"language_model.embed_tokens.weight": np.zeros((c["vocab"], H), np.uint16),
+         "language_model.norm.weight": f32_to_bf16(np.ones(H, np.float32))}
+    for li in range(nl):
+        p = f"language_model.layers.{li}"
+        w[f"{p}.input_layernorm.weight"] = f32_to_bf16(np.ones(H, np.float32))
+        w[f"{p}.post_attention_layernorm.weight"] = f32_to_bf16(np.ones(H, np.float32))
+        w[f"{p}.self_attn.q_proj.weight"] = r(c["n_heads"] * D, H)
+        w[f"{p}.self_attn.k_proj.weight"] = r(c["n_kv"] * D, H)
+        w[f"{p}.self_attn.v_proj.weight"] = r(c["n_kv"] * D, H)
+        w[f"{p}.self_attn.o_proj.weight"] = r(H, c["n_heads"] * D)
+        w[f"{p}.self_attn.q_norm.weight"] = f32_to_bf16(np.ones(D, np.float32))
+        w[f"{p}.self_attn.k_norm.weight"] = f32_to_bf16(np.ones(D, np.float32))
+        w[f"{p}.mlp.gate_proj.weight"] = r(c["inter"], H)
+        w[f"{p}.mlp.up_proj.weight"] = r(c["inter"], H)
+        w[f"{p}.mlp.down_proj.weight"] = r(H, c["inter"])
+    for i in range(32):
+        w[f"emb_ext.{i}.weight"] = r(1025, H)
+    w["lm_heads.0.weight"] = np.zeros((c["vocab"], H), np.uint16)
+    for i in range(32):
+        w[f"lm_heads.{i + 1}.weight"] = r(1025, H)
+    om = ost.OracleModel(w, max_seq_len=c["prompt_len"] + 8, fp32_linears=True)
+    om.seq = c["prompt_len"]
+    row = np.concatenate([[ost.AUDIO_GEN_SLOT_TOKEN_ID], rng.integers(0, 1024, 32)]).astype(np.int64)
+    reps, t_layers, t_rest = 0, 0.0, 0.0
+    t_start = time.perf_counter()
+    while reps < 3 and (reps == 0 or time.perf_counter() - t_start < seconds_budget):
+        t0 = time.perf_counter()
+        h = om.embed_rows(row.reshape(1, -1))
+        t1 = time.perf_counter()
+        for li in range(nl):
+            h = om.layer(li, h, om.seq)
+        t2 = time.perf_counter()
+        hf = ost.rms_norm(h, om.final_norm)
+        om.text_logits_2way(hf)
+        om.audio_logits(hf)
+        t3 = time.perf_counter()
+        t_layers += t2 - t1
+        t_rest += (t1 - t0) + (t3 - t2)
+        reps += 1
+    per_step = (t_rest + t_layers * c["n_layers"] / nl) / reps
+    cores = os.cpu_count() or 1
+    sample = (f"numpy oracle step at cfg2 shapes: {nl} of {c['n_layers']} layers timed (fp32 BLAS, effective "
+              f"weights precomputed, KV length {c['prompt_len'] + 1}) + embedding + audio-phase heads, "
+              f"{reps} reps, scaled to {c['n_layers']} layers")
+    return 1.0 / per_step, cores, sample
+
+
+# ------------------------------------------------------------------- main
+class _Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self):
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg is not None:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if self.pg is None:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.destroy_process_group()
+
+
+def run_reference_arm(args, ctx):
+    """--impl reference: the CPU restatement of the reference path (numpy
+    oracle) on the host cores; rank 0 only."""
+    if ctx.rank != 0:
+        return
+    vals = []
+    for _ in range(max(1, args.warmup)):
+        cpu_baseline(seconds_budget=5.0)
+    for _ in range(args.steps):
+        v, cores, sample = cpu_baseline(seconds_budget=5.0)
+        vals.append(v)
+    v = statistics.median(vals)
+    line = {"metric": METRIC, "value": v, "unit": "steps/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "cfg2: full synthetic MOSS-TTS-shaped W4 decode step, batch 1",
+                       "model": "synthetic MOSS-TTS (36L, h4096, 32/8 heads, ffn 12288)"},
+            "impl": "reference",
+            "cpu_baseline": {"value": v, "unit": "steps/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="mtl", choices=["mtl", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    ctx = _Dist()
+    if args.impl == "reference":
+        run_reference_arm(args, ctx)
+        return
+    import torch
+    torch.cuda.set_device(ctx.local)
+    ctx.init()
+    dev = torch.device("cuda", ctx.local)
+    t_build = time.time()
+    fast = build_fast(dev, seed=CFG["seed"] + ctx.rank)
+    prompt = make_prompt(CFG["seed"] + ctx.rank)
+    fast.prefill(prompt.to(dev))
+    fast.capture()
+    build_s = time.time() - t_build
+    steps, warmup = args.steps, max(3, args.warmup)
+    ms, clocks = time_decode_loop(fast, steps, warmup, ctx)
+    ms = ctx.max(ms)
+    ms_per_step = ms / steps
+    value = args.gpus * steps / (ms * 1e-3)
+    bytes_per_launch, s_per_launch, launches = time_w4_gemvs(fast)
+    e2e, e2e_steps = time_e2e(fast, prompt.to("cpu"), steps, warmup)
+    e2e_all = ctx.max(-(e2e or 0.0))  # slowest rank
+    e2e_val = args.gpus * (-e2e_all) if e2e else None
+    peak, peak_kind = _peaks()
+    achieved = bytes_per_launch / s_per_launch / 1e9
+    traffic = _ncu_traffic()
+    cpu = None
+    if ctx.rank == 0 and args.gpus == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_baseline()
+        cpu = {"value": v, "unit": "steps/s", "cores": cores, "kind": "port", "sample": sample}
+    if ctx.rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": args.gpus, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "cfg2: full synthetic MOSS-TTS-shaped W4 decode step, batch 1",
+                       "model": "synthetic MOSS-TTS (36L, h4096, 32/8 heads x128, ffn 12288, vocab 151936 + "
+                                "32x1025 codebooks, RTN W4 g128, random-init seed 0)",
+                       "global_batch": args.gpus, "seq_len": CFG["prompt_len"], "parallelism": f"replicas{args.gpus}",
+                       "phase": "audio (2-way text head + 32 audio heads), greedy tokens fed back on device",
+                       "l2": "inputs larger than L2 (~3.9 GB of weights per step)",
+                       "weights": "int4 codes + bf16 (scale, zero) per 128-group; activations bf16, fp32 accumulate",
+                       "build_s": round(build_s, 1)},
+            "e2e": {"value": e2e_val, "unit": "steps/s", "h2d_bytes_per_step": 33 * 8,
+                    "d2h_bytes_per_step": 33 * 8, "api": "moss_tts_lite_b200.fast.generate_fast(greedy=True)",
+                    "steps_generated": e2e_steps},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": (traffic or {}).get("dram_bytes_per_launch"),
+                         "kernel": "w4_gemv_kernel (144 launches per step: q|k|v, o, gate|up, down x 36)",
+                         "bytes_per_launch": bytes_per_launch, "us_per_launch": s_per_launch * 1e6},
+            "gpu_launches": steps * (1 + 5 * CFG["n_layers"] + 2 + 1),
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    ctx.barrier()
+    del fast
+    ctx.close()
+
+
+if __name__ == "__main__":
+    main()

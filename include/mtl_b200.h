@@ -131,7 +131,7 @@ int mtl_attn_scratch_bytes(int streams, int n_heads, int n_kv, int splits, size_
  *   k_cache, v_cache    bf16 [n_kv, max_seq, 128] of this layer for stream 0;
  *              stream s starts cache_stream_stride elements later
  *   pos        int64 [streams] (device): position being decoded
- *   splits     KV splits per head, ceil(max_seq / 512) <= splits <= 64
+ *   splits     KV splits per head (1..64); each covers >= 32 positions
  *   out        bf16 [streams, n_heads * 128]
  * head_dim must be 128 and n_heads / n_kv <= 8. */
 int mtl_attn_decode(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_t* k_norm_w,
@@ -171,6 +171,14 @@ int mtl_argmax_rows(const uint16_t* x, int rows, int cols, int ld, int64_t* out,
  * writes of fast.py:487 and 507-511 folded in). */
 int mtl_argmax_masked(const uint16_t* x, int cols, const int32_t* excluded, int n_excluded, int64_t* out,
                       mtl_stream_t stream);
+
+/* Device-side greedy feedback for an audio-phase decode loop with no host
+ * round trip: ids_row[1 + j] = argmax of audio row j (bf16 [32, 1025]),
+ * ids_row[0] = delay_slot_id if two_logits[1] > two_logits[0] else
+ * gen_slot_id (the greedy 2-way decision of fast.py:481-490), pos[0] += 1.
+ * No counterpart call in the reference (its loop decides on the host). */
+int mtl_greedy_feed(const uint16_t* audio_logits, const uint16_t* two_logits, int64_t* ids_row, int64_t* pos,
+                    int gen_slot_id, int delay_slot_id, mtl_stream_t stream);
 
 /* Round-to-nearest W4 quantisation of a bf16 weight [N, K] exactly as
  * FastMossTTS._quantize (fast.py:85-96) / gptq.rtn_quantize (gptq.py:54-64):

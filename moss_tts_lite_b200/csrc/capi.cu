@@ -23,6 +23,8 @@ cudaError_t launch_argmax_rows(const uint16_t* x, int rows, int cols, int ld, in
 cudaError_t launch_rtn_quantize(const uint16_t* w, int N, int K, int g, uint8_t* q, uint16_t* qsz, cudaStream_t s);
 cudaError_t launch_argmax_masked(const uint16_t* x, int cols, const int* excl, int n_excl, int64_t* out,
                                  cudaStream_t s, int use_pdl);
+cudaError_t launch_greedy_feed(const uint16_t* la, const uint16_t* two, int64_t* ids, int64_t* pos, int gen_slot,
+                               int delay_slot, cudaStream_t s, int use_pdl);
 cudaError_t launch_rmsnorm_rows(const uint16_t* x, int rows, int K, int ldx, const uint16_t* w, float eps,
                                 uint16_t* y, int ldy, cudaStream_t s, int use_pdl);
 cudaError_t w4_pack_gptq(const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
@@ -258,9 +260,6 @@ int mtl_attn_decode(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_
     return fail(MTL_E_UNSUPPORTED, "n_heads=%d n_kv=%d (n_heads/n_kv must divide and be <= 8)", n_heads, n_kv);
   if (streams < 1 || max_seq < 1 || splits < 1 || splits > 64)
     return fail(MTL_E_INVALID, "streams=%d max_seq=%d splits=%d", streams, max_seq, splits);
-  if ((long long)splits * mtl::kAttnMaxChunk < max_seq)
-    return fail(MTL_E_INVALID, "splits=%d too few for max_seq=%d (need >= %d)", splits, max_seq,
-                (max_seq + mtl::kAttnMaxChunk - 1) / mtl::kAttnMaxChunk);
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || cache_stream_stride % 8)
     return fail(MTL_E_ALIGN, "KV cache must be 16-byte aligned");
   size_t need = 0;
@@ -333,6 +332,14 @@ int mtl_argmax_masked(const uint16_t* x, int cols, const int32_t* excluded, int 
     return fail(MTL_E_INVALID, "mtl_argmax_masked: bad arguments");
   cudaError_t e = mtl::launch_argmax_masked(x, cols, excluded, n_excluded, out, stream, use_pdl());
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_argmax_masked");
+}
+
+int mtl_greedy_feed(const uint16_t* audio_logits, const uint16_t* two_logits, int64_t* ids_row, int64_t* pos,
+                    int gen_slot_id, int delay_slot_id, mtl_stream_t stream) {
+  if (!audio_logits || !two_logits || !ids_row || !pos) return fail(MTL_E_INVALID, "mtl_greedy_feed: NULL pointer");
+  cudaError_t e = mtl::launch_greedy_feed(audio_logits, two_logits, ids_row, pos, gen_slot_id, delay_slot_id, stream,
+                                          use_pdl());
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_greedy_feed");
 }
 
 int mtl_rmsnorm(const uint16_t* x, int rows, int K, int ldx, const uint16_t* weight, float eps, uint16_t* y,

@@ -34,23 +34,30 @@ __global__ void __launch_bounds__(256) embed_sum_kernel(const int64_t* __restric
     flag_error(kDevBadIndex);
     t0 = 0;
   }
-  const uint4 v = __ldg(reinterpret_cast<const uint4*>(emb_text + (size_t)t0 * H) + c);
-  float acc[8];
-  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+  // all 33 row loads are independent: issue them before the ordered sum
+  uint4 rows[kNVQ + 1];
+  rows[0] = __ldg(reinterpret_cast<const uint4*>(emb_text + (size_t)t0 * H) + c);
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    acc[2 * q] = __uint_as_float(u[q] << 16);
-    acc[2 * q + 1] = __uint_as_float(u[q] & 0xFFFF0000u);
-  }
-#pragma unroll 4
   for (int i = 0; i < kNVQ; ++i) {
     int64_t a = row[i + 1];
     if (a < 0 || a >= kAudioVocab) {
       flag_error(kDevBadIndex);
       a = 0;
     }
-    const uint4 e = __ldg(reinterpret_cast<const uint4*>(emb_audio + ((size_t)i * kAudioVocab + a) * H) + c);
-    const uint32_t w[4] = {e.x, e.y, e.z, e.w};
+    rows[i + 1] = __ldg(reinterpret_cast<const uint4*>(emb_audio + ((size_t)i * kAudioVocab + a) * H) + c);
+  }
+  float acc[8];
+  {
+    const uint32_t u[4] = {rows[0].x, rows[0].y, rows[0].z, rows[0].w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      acc[2 * q] = __uint_as_float(u[q] << 16);
+      acc[2 * q + 1] = __uint_as_float(u[q] & 0xFFFF0000u);
+    }
+  }
+#pragma unroll
+  for (int i = 1; i <= kNVQ; ++i) {
+    const uint32_t w[4] = {rows[i].x, rows[i].y, rows[i].z, rows[i].w};
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       acc[2 * q] = round_bf16(acc[2 * q] + __uint_as_float(w[q] << 16));
@@ -96,19 +103,43 @@ struct AttnArgs {
 
 constexpr int kAttnThreads = 128;
 constexpr int kAttnMaxRep = 8;
-constexpr int kAttnMaxChunk = 512;  // positions per split held in shared memory
-constexpr int kAttnMinChunk = 128;  // positions per split at least
+constexpr int kAttnTile = 32;       // positions per tile (4 warps x 8)
+constexpr int kAttnMinChunk = 32;   // positions per split at least
 
 __device__ __forceinline__ float rope_rot(const float* x, int d) {
   // rotate_half (model.py:42-44): [-x2, x1]
   return d < kHeadDim / 2 ? -x[d + kHeadDim / 2] : x[d - kHeadDim / 2];
 }
 
+// Registers of one tile: each lane holds 32 K dims of one position (scores)
+// and 4 V dims of 8 positions (P.V).
+struct KVTile {
+  uint4 k[4];
+  uint2 v[8];
+};
+
+__device__ __forceinline__ void load_tile(KVTile& t, const uint16_t* kc, const uint16_t* vc, int base, int hi,
+                                          int pos, int warp, int lane) {
+  const int ps = lane >> 2, dg = lane & 3;
+  const int sk = base + warp * 8 + ps;
+  if (sk < hi && sk != pos) {
+    const uint4* kp = reinterpret_cast<const uint4*>(kc + (size_t)sk * kHeadDim + dg * 32);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) t.k[j] = __ldg(kp + j);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int sv = base + warp * 8 + i;
+    if (sv < hi && sv != pos) t.v[i] = __ldg(reinterpret_cast<const uint2*>(vc + (size_t)sv * kHeadDim) + lane);
+  }
+}
+
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
   __shared__ float sq[kAttnMaxRep][kHeadDim];  // normed + roped q (bf16 values)
   __shared__ float sk[kHeadDim], sv[kHeadDim];
-  __shared__ float sc[kAttnMaxRep][kAttnMaxChunk];
-  __shared__ float red[4][kAttnMaxRep];
+  __shared__ float sc[kAttnMaxRep][kAttnTile];
+  __shared__ float so[4][kAttnMaxRep][kHeadDim];  // per-warp P.V partials
+  __shared__ float mrun_s[kAttnMaxRep], alpha_s[kAttnMaxRep];
   __shared__ int last_flag;
   const int h = blockIdx.x, sp = blockIdx.y, st = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -121,151 +152,168 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     return;
   }
   const int pos = (int)pos64, s1 = pos + 1;
-  // Slices of at least kAttnMinChunk positions: contexts up to that length
-  // are one block (one max, one bf16 rounding of exp(s - max)), as in the
-  // single-block softmax of PyTorch's SDPA for short sequences.
   const int chunk = max(kAttnMinChunk, (s1 + a.splits - 1) / a.splits);
   const int lo = min(sp * chunk, s1), hi = min(lo + chunk, s1);
-  const uint16_t* qkv = a.qkv + (size_t)st * (a.nh + 2 * a.nkv) * kHeadDim;
+  const int n = hi - lo;
   uint16_t* kc = a.k_cache + st * a.cache_stream_stride + (size_t)h * a.max_seq * kHeadDim;
   uint16_t* vc = a.v_cache + st * a.cache_stream_stride + (size_t)h * a.max_seq * kHeadDim;
-  const uint16_t* cs = a.rope_cos + (size_t)pos * kHeadDim;
-  const uint16_t* sn = a.rope_sin + (size_t)pos * kHeadDim;
-
-  // --- q/k RMSNorm over head_dim + RoPE; one warp per head (rep q heads + k)
-  for (int r = warp; r <= rep; r += 4) {
-    const uint16_t* src = (r < rep) ? qkv + (size_t)(h * rep + r) * kHeadDim
-                                    : qkv + (size_t)(a.nh + h) * kHeadDim;
-    const uint16_t* nw = (r < rep) ? a.q_norm_w : a.k_norm_w;
-    float x[4];
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      x[j] = bf16_bits_to_f32(src[lane + 32 * j]);
-      ss = fmaf(x[j], x[j], ss);
-    }
-    ss = warp_sum(ss);
-    const float rinv = rsqrtf(ss / (float)kHeadDim + 1e-6f);
-    float* dst = (r < rep) ? sq[r] : sk;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int d = lane + 32 * j;
-      dst[d] = round_bf16(bf16_bits_to_f32(nw[d]) * round_bf16(x[j] * rinv));
-    }
-    __syncwarp();
-    float y[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int d = lane + 32 * j;
-      const float t1 = round_bf16(dst[d] * bf16_bits_to_f32(cs[d]));
-      const float t2 = round_bf16(rope_rot(dst, d) * bf16_bits_to_f32(sn[d]));
-      y[j] = round_bf16(t1 + t2);
-    }
-    __syncwarp();
-#pragma unroll
-    for (int j = 0; j < 4; ++j) dst[lane + 32 * j] = y[j];
-  }
-  // v is used as is (fast.py:137,140)
-  for (int d = tid; d < kHeadDim; d += kAttnThreads)
-    sv[d] = bf16_bits_to_f32(qkv[(size_t)(a.nh + a.nkv + h) * kHeadDim + d]);
-  __syncthreads();
-  // K/V append at pos (fast.py:145-146): the split holding pos owns the write;
-  // every split uses sk/sv for position pos instead of re-reading the cache.
-  if (hi == s1 && lo < hi) {
-    for (int d = tid; d < kHeadDim; d += kAttnThreads) {
-      kc[(size_t)pos * kHeadDim + d] = f32_to_bf16_bits(sk[d]);
-      vc[(size_t)pos * kHeadDim + d] = f32_to_bf16_bits(sv[d]);
-    }
-  }
-
-  const int n = hi - lo;
   float* part = a.partials + ((((size_t)st * a.nkv + h) * a.splits + sp) * rep) * (2 + kHeadDim);
+
   if (n > 0) {
-    // --- scores: lane = (position sub-index ps in 0..7, dim group dg in 0..3)
+    // first tile's loads go out before the q/k prologue (they do not depend on it)
+    KVTile cur;
+    load_tile(cur, kc, vc, lo, hi, pos, warp, lane);
+    const uint16_t* qkv = a.qkv + (size_t)st * (a.nh + 2 * a.nkv) * kHeadDim;
+    const uint16_t* cs = a.rope_cos + (size_t)pos * kHeadDim;
+    const uint16_t* sn = a.rope_sin + (size_t)pos * kHeadDim;
+    // --- q/k RMSNorm over head_dim + RoPE; one warp per head (rep q heads + k)
+    for (int r = warp; r <= rep; r += 4) {
+      const uint16_t* src = (r < rep) ? qkv + (size_t)(h * rep + r) * kHeadDim : qkv + (size_t)(a.nh + h) * kHeadDim;
+      const uint16_t* nw = (r < rep) ? a.q_norm_w : a.k_norm_w;
+      float x[4];
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        x[j] = bf16_bits_to_f32(src[lane + 32 * j]);
+        ss = fmaf(x[j], x[j], ss);
+      }
+      ss = warp_sum(ss);
+      const float rinv = rsqrtf(ss / (float)kHeadDim + 1e-6f);
+      float* dst = (r < rep) ? sq[r] : sk;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int d = lane + 32 * j;
+        dst[d] = round_bf16(bf16_bits_to_f32(nw[d]) * round_bf16(x[j] * rinv));
+      }
+      __syncwarp();
+      float y[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int d = lane + 32 * j;
+        const float t1 = round_bf16(dst[d] * bf16_bits_to_f32(cs[d]));
+        const float t2 = round_bf16(rope_rot(dst, d) * bf16_bits_to_f32(sn[d]));
+        y[j] = round_bf16(t1 + t2);
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dst[lane + 32 * j] = y[j];
+    }
+    // v is used as is (fast.py:137,140)
+    sv[tid] = bf16_bits_to_f32(qkv[(size_t)(a.nh + a.nkv + h) * kHeadDim + tid]);
+    if (tid < kAttnMaxRep) mrun_s[tid] = -INFINITY;
+    __syncthreads();
+    // K/V append at pos (fast.py:145-146) by the split holding pos; every split
+    // uses sk / sv for position pos instead of re-reading the cache.
+    if (hi == s1) {
+      kc[(size_t)pos * kHeadDim + tid] = f32_to_bf16_bits(sk[tid]);
+      vc[(size_t)pos * kHeadDim + tid] = f32_to_bf16_bits(sv[tid]);
+    }
+
     const int ps = lane >> 2, dg = lane & 3;
-    for (int base = lo + warp * 8; base < hi; base += 32) {
-      const int s = base + ps;
-      float dot[kAttnMaxRep];
+    float o[kAttnMaxRep][4];
 #pragma unroll
-      for (int r = 0; r < kAttnMaxRep; ++r) dot[r] = 0.f;
-      if (s < hi) {
-        float kv[32];
-        if (s == pos) {
+    for (int r = 0; r < kAttnMaxRep; ++r)
 #pragma unroll
-          for (int j = 0; j < 32; ++j) kv[j] = sk[dg * 32 + j];
-        } else {
-          const uint4* kp = reinterpret_cast<const uint4*>(kc + (size_t)s * kHeadDim + dg * 32);
+      for (int c = 0; c < 4; ++c) o[r][c] = 0.f;
+    float lsum[kAttnMaxRep];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint4 v = __ldg(kp + j);
-            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    for (int r = 0; r < kAttnMaxRep; ++r) lsum[r] = 0.f;
+
+    for (int base = lo; base < hi; base += kAttnTile) {
+      KVTile nxt;
+      if (base + kAttnTile < hi) load_tile(nxt, kc, vc, base + kAttnTile, hi, pos, warp, lane);
+      // --- scores of this tile: lane = (position ps, dim group dg)
+      const int s = base + warp * 8 + ps;
+      float kv[32];
+      if (s == pos) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              kv[8 * j + 2 * q] = __uint_as_float(u[q] << 16);
-              kv[8 * j + 2 * q + 1] = __uint_as_float(u[q] & 0xFFFF0000u);
-            }
-          }
-        }
+        for (int j = 0; j < 32; ++j) kv[j] = sk[dg * 32 + j];
+      } else {
 #pragma unroll
-        for (int r = 0; r < kAttnMaxRep; ++r) {
-          if (r < rep) {
-            float acc = 0.f;
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t u[4] = {cur.k[j].x, cur.k[j].y, cur.k[j].z, cur.k[j].w};
 #pragma unroll
-            for (int j = 0; j < 32; ++j) acc = fmaf(sq[r][dg * 32 + j], kv[j], acc);
-            dot[r] = acc;
+          for (int q = 0; q < 4; ++q) {
+            kv[8 * j + 2 * q] = __uint_as_float(u[q] << 16);
+            kv[8 * j + 2 * q + 1] = __uint_as_float(u[q] & 0xFFFF0000u);
           }
         }
       }
 #pragma unroll
       for (int r = 0; r < kAttnMaxRep; ++r) {
         if (r < rep) {
-          float v = dot[r];
-          v += __shfl_xor_sync(0xffffffffu, v, 1);
-          v += __shfl_xor_sync(0xffffffffu, v, 2);
-          if (dg == 0 && s < hi) sc[r][s - lo] = v * a.scale;
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc = fmaf(sq[r][dg * 32 + j], kv[j], acc);
+          acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+          acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+          if (dg == 0) sc[r][warp * 8 + ps] = (s < hi) ? acc * a.scale : -INFINITY;
         }
       }
-    }
-    __syncthreads();
-    // --- split max, probabilities (bf16-rounded) and fp32 row sums
-    for (int r = 0; r < rep; ++r) {
-      float mx = -INFINITY;
-      for (int i = tid; i < n; i += kAttnThreads) mx = fmaxf(mx, sc[r][i]);
-      mx = warp_max(mx);
-      if (lane == 0) red[warp][r] = mx;
-    }
-    __syncthreads();
-    float mrow[kAttnMaxRep];
-    for (int r = 0; r < rep; ++r) mrow[r] = fmaxf(fmaxf(red[0][r], red[1][r]), fmaxf(red[2][r], red[3][r]));
-    __syncthreads();
-    for (int r = 0; r < rep; ++r) {
-      float l = 0.f;
-      for (int i = tid; i < n; i += kAttnThreads) {
-        const float pf = expf(sc[r][i] - mrow[r]);
-        l += pf;
-        sc[r][i] = round_bf16(pf);
+      __syncthreads();
+      // --- running max per head (warp r owns head r..), rescale factor
+      for (int r = warp; r < rep; r += 4) {
+        const float tmx = warp_max(sc[r][lane]);
+        if (lane == 0) {
+          const float mnew = fmaxf(mrun_s[r], tmx);
+          alpha_s[r] = (mrun_s[r] == -INFINITY) ? 0.f : expf(mrun_s[r] - mnew);
+          mrun_s[r] = mnew;
+        }
       }
-      l = warp_sum(l);
-      if (lane == 0) red[warp][r] = l;
+      __syncthreads();
+      // --- probabilities exp(s - m) rounded to bf16 (flash-style), P.V over
+      //     this warp's 8 positions for 4 dims per lane
+      const int dbase = lane * 4;
+#pragma unroll
+      for (int r = 0; r < kAttnMaxRep; ++r) {
+        if (r < rep) {
+          const float al = alpha_s[r], m = mrun_s[r];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) o[r][c] *= al;
+          lsum[r] *= al;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int sp2 = base + warp * 8 + i;
+            if (sp2 < hi) {
+              const float pf = expf(sc[r][warp * 8 + i] - m);
+              lsum[r] += pf;
+              const float pb = round_bf16(pf);
+              float vv[4];
+              if (sp2 == pos) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) vv[c] = sv[dbase + c];
+              } else {
+                vv[0] = __uint_as_float(cur.v[i].x << 16);
+                vv[1] = __uint_as_float(cur.v[i].x & 0xFFFF0000u);
+                vv[2] = __uint_as_float(cur.v[i].y << 16);
+                vv[3] = __uint_as_float(cur.v[i].y & 0xFFFF0000u);
+              }
+#pragma unroll
+              for (int c = 0; c < 4; ++c) o[r][c] = fmaf(pb, vv[c], o[r][c]);
+            }
+          }
+        }
+      }
+      __syncthreads();  // sc / alpha reuse
+      if (base + kAttnTile < hi) cur = nxt;
+    }
+    // --- combine the 4 warps' partials (same running max) and publish
+    for (int r = 0; r < rep; ++r) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) so[warp][r][lane * 4 + c] = o[r][c];
+    }
+    float* lred = &sc[0][0];  // reuse: [4 warps][rep] row sums
+    for (int r = 0; r < rep; ++r) {
+      // lsum is identical across lanes of a warp (every lane saw the same p's)
+      if (lane == 0) lred[warp * kAttnMaxRep + r] = lsum[r];
     }
     __syncthreads();
-    // --- P.V: thread d accumulates o[r][d] over the slice
-    const int d = tid;
-    float o[kAttnMaxRep];
-#pragma unroll
-    for (int r = 0; r < kAttnMaxRep; ++r) o[r] = 0.f;
-    for (int i = 0; i < n; ++i) {
-      const int s = lo + i;
-      const float vv = (s == pos) ? sv[d] : bf16_bits_to_f32(vc[(size_t)s * kHeadDim + d]);
-#pragma unroll
-      for (int r = 0; r < kAttnMaxRep; ++r)
-        if (r < rep) o[r] = fmaf(sc[r][i], vv, o[r]);
-    }
     for (int r = 0; r < rep; ++r) {
-      part[(size_t)r * (2 + kHeadDim) + 2 + d] = o[r];
+      part[(size_t)r * (2 + kHeadDim) + 2 + tid] = so[0][r][tid] + so[1][r][tid] + so[2][r][tid] + so[3][r][tid];
       if (tid == 0) {
-        part[(size_t)r * (2 + kHeadDim) + 0] = mrow[r];
-        part[(size_t)r * (2 + kHeadDim) + 1] = red[0][r] + red[1][r] + red[2][r] + red[3][r];
+        part[(size_t)r * (2 + kHeadDim) + 0] = mrun_s[r];
+        part[(size_t)r * (2 + kHeadDim) + 1] = lred[0 * kAttnMaxRep + r] + lred[1 * kAttnMaxRep + r] +
+                                                lred[2 * kAttnMaxRep + r] + lred[3 * kAttnMaxRep + r];
       }
     }
   } else if (tid < rep) {
@@ -286,20 +334,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   }
   __syncthreads();
   if (!last_flag) return;
-  const float* base = a.partials + (((size_t)st * a.nkv + h) * a.splits * rep) * (2 + kHeadDim);
+  const float* basep = a.partials + (((size_t)st * a.nkv + h) * a.splits * rep) * (2 + kHeadDim);
   for (int r = 0; r < rep; ++r) {
     float m = -INFINITY;
-    for (int j = 0; j < a.splits; ++j) m = fmaxf(m, __ldcg(base + ((size_t)j * rep + r) * (2 + kHeadDim)));
-    float l = 0.f, o = 0.f;
+    for (int j = 0; j < a.splits; ++j) m = fmaxf(m, __ldcg(basep + ((size_t)j * rep + r) * (2 + kHeadDim)));
+    float l = 0.f, acc = 0.f;
     for (int j = 0; j < a.splits; ++j) {
-      const float* pj = base + ((size_t)j * rep + r) * (2 + kHeadDim);
+      const float* pj = basep + ((size_t)j * rep + r) * (2 + kHeadDim);
       const float mj = __ldcg(pj);
       if (mj == -INFINITY) continue;
       const float f = expf(mj - m);
       l = fmaf(__ldcg(pj + 1), f, l);
-      o = fmaf(__ldcg(pj + 2 + tid), f, o);
+      acc = fmaf(__ldcg(pj + 2 + tid), f, acc);
     }
-    a.out[(size_t)st * a.nh * kHeadDim + (size_t)(h * rep + r) * kHeadDim + tid] = f32_to_bf16_bits(o / l);
+    a.out[(size_t)st * a.nh * kHeadDim + (size_t)(h * rep + r) * kHeadDim + tid] = f32_to_bf16_bits(acc / l);
   }
 }
 
@@ -538,6 +586,46 @@ __global__ void __launch_bounds__(256) argmax_masked_kernel(const uint16_t* __re
   }
 }
 
+// ---------------------------------------------------------- greedy feed
+// Device-side greedy feedback for an autoregressive audio-phase decode loop
+// without host round trips: next row = [GEN_SLOT or DELAY_SLOT by the 2-way
+// argmax (fast.py:481-490), argmax of each of the 32 audio rows] and
+// pos += 1.  One warp per audio row; warp 0 also takes the text decision.
+__global__ void __launch_bounds__(1024) greedy_feed_kernel(const uint16_t* __restrict__ la,
+                                                           const uint16_t* __restrict__ two, int64_t* ids,
+                                                           int64_t* pos, int gen_slot, int delay_slot) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp < kNVQ) {
+    const uint16_t* r = la + (size_t)warp * kAudioVocab;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = lane; c < kAudioVocab; c += 32) {
+      const float v = bf16_bits_to_f32(r[c]);
+      if (v > best) {
+        best = v;
+        bi = c;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) ids[1 + warp] = (bi == 0x7fffffff) ? 0 : bi;
+  }
+  if (threadIdx.x == 0) {
+    const float a = bf16_bits_to_f32(two[0]), b = bf16_bits_to_f32(two[1]);
+    ids[0] = (b > a) ? delay_slot : gen_slot;
+    pos[0] += 1;
+  }
+}
+
 // -------------------------------------------------------- RTN quantisation
 // fast.py:85-96 / gptq.py:35-64: per (row n, group G) of a bf16 weight
 // [N, K]: mx/mn over the group, s = clamp((mx - mn) * (1/15), min=1e-6),
@@ -643,6 +731,13 @@ cudaError_t launch_argmax_masked(const uint16_t* x, int cols, const int* excl, i
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_cfg(dim3(1), dim3(256), 0, s, attr, use_pdl);
   return cudaLaunchKernelEx(&cfg, argmax_masked_kernel, x, cols, ex, out);
+}
+
+cudaError_t launch_greedy_feed(const uint16_t* la, const uint16_t* two, int64_t* ids, int64_t* pos, int gen_slot,
+                               int delay_slot, cudaStream_t s, int use_pdl) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_cfg(dim3(1), dim3(kNVQ * 32), 0, s, attr, use_pdl);
+  return cudaLaunchKernelEx(&cfg, greedy_feed_kernel, la, two, ids, pos, gen_slot, delay_slot);
 }
 
 cudaError_t launch_rtn_quantize(const uint16_t* w, int N, int K, int g, uint8_t* q, uint16_t* qsz, cudaStream_t s) {

@@ -18,6 +18,7 @@ buffers, plus ``generate_fast``.  What changes is the step itself:
 from __future__ import annotations
 
 import math
+import time
 from dataclasses import dataclass, field
 
 import torch
@@ -129,9 +130,9 @@ class _StepEngine:
         self.attn = torch.zeros(1, nq, dtype=bf, device=dev)
         inter = lins[0]["gu"].N // 2
         self.act = torch.zeros(1, inter, dtype=bf, device=dev)
-        self.splits = max(16, math.ceil(m.max_seq_len / 512))
-        if self.splits > 64:
-            raise ValueError(f"max_seq_len {m.max_seq_len} > 32768 is not served by the decode attention")
+        # KV splits per head: 8 heads x 16 splits covers the SMs once the cache
+        # is long; short caches use fewer (each split holds >= 32 positions)
+        self.splits = 16
         from . import _lib
         nbytes = _lib.attn_scratch_bytes(1, m.n_heads, m.n_kv_heads, self.splits)
         self.attn_scratch = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
@@ -313,6 +314,23 @@ class FastMossTTS:
                 self._run_eager(audio2)
             self.graphs.append(g)
         torch.cuda.synchronize()
+
+    def capture_greedy_loop(self) -> torch.cuda.CUDAGraph:
+        """Graph of one autoregressive audio-phase step with device-side
+        greedy feedback (next row and position written by the feed kernel):
+        replaying it repeatedly decodes with no host round trip."""
+        from .model import AUDIO_DELAY_SLOT_TOKEN_ID as _DELAY, AUDIO_GEN_SLOT_TOKEN_ID as _GEN
+        self.capture()
+
+        def body():
+            self._run_eager(True)
+            kernels.greedy_feed(self.la_static, self.two_static, self.ids_row, self.pos_dev, _GEN, _DELAY)
+
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=self.capture_stream):
+            body()
+        torch.cuda.synchronize()
+        return g
 
     def step(self, row: torch.Tensor | None, pos: int, audio2: bool = False):
         """Replay one decode step (fast.py:308-325); outputs alias static buffers."""
@@ -574,6 +592,8 @@ def generate_fast(
         # pageable source: the copy is staged before copy_ returns
         fast.ids_row.view(-1).copy_(torch.tensor([next_text] + next_audio, dtype=torch.long))
         prev_audio.append(next_audio)
+        if _stats is not None:
+            _stats.setdefault("step_wall_s", []).append(time.perf_counter())
         text_steps.append(next_text)
         audio_steps.append(next_audio)
         n_steps += 1

@@ -86,6 +86,13 @@ def argmax_masked(x: torch.Tensor, out: torch.Tensor, excluded=()) -> torch.Tens
     return out
 
 
+def greedy_feed(la: torch.Tensor, two: torch.Tensor, ids_row: torch.Tensor, pos_dev: torch.Tensor,
+                gen_slot: int, delay_slot: int) -> None:
+    """Next row and position of a device-side greedy audio-phase loop."""
+    _lib.call("mtl_greedy_feed", la.data_ptr(), two.data_ptr(), ids_row.data_ptr(), pos_dev.data_ptr(),
+              gen_slot, delay_slot, _s())
+
+
 def rtn_quantize(w: torch.Tensor, group_size: int = 128) -> tuple[torch.Tensor, torch.Tensor]:
     """Reference RTN W4 (fast.py:85-96): bf16 [N, K] -> (q uint8 [N, K], qsz bf16 [K/g, N, 2])."""
     _bf16(w, "w")

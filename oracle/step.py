@@ -114,7 +114,7 @@ class OracleModel:
     """numpy MossTTSModel. ``weights`` maps reference checkpoint key names
     (tests/test_quant.py:299-327 layout) to bf16 bit arrays."""
 
-    def __init__(self, weights: dict, max_seq_len: int = 256):
+    def __init__(self, weights: dict, max_seq_len: int = 256, fp32_linears: bool = False):
         layer_ids = sorted({int(k.split(".")[2]) for k in weights
                             if k.startswith("language_model.layers.")})
         self.n_layers = len(layer_ids)
@@ -126,6 +126,9 @@ class OracleModel:
         self.n_kv = int(weights["language_model.layers.0.self_attn.k_proj.weight"].shape[0]) // self.head_dim
         self.n_rep = self.n_heads // self.n_kv
         self.max_seq_len = max_seq_len
+        # fp32_linears: BLAS fp32 products instead of fp64 (the CPU-baseline
+        # timing mode; parity tests keep the fp64 default)
+        self.fp32_linears = fp32_linears
         self.embed = weights["language_model.embed_tokens.weight"]
         self.final_norm = weights["language_model.norm.weight"]
         names = {"q": "self_attn.q_proj", "k": "self_attn.k_proj", "v": "self_attn.v_proj",
@@ -160,6 +163,8 @@ class OracleModel:
 
     def linear(self, x_bits: np.ndarray, li: int, name: str) -> np.ndarray:
         w = self._w_eff[li][name]                   # [N, K] fp32
+        if self.fp32_linears:
+            return f32_to_bf16(bf16_to_f32(x_bits) @ w.T)
         x = bf16_to_f32(x_bits).astype(np.float64)
         return f32_to_bf16((x @ w.astype(np.float64).T).astype(np.float32))
 
