@@ -104,6 +104,22 @@ int mtl_w4a16_linear(const uint16_t* x, int ldx, int M, int K, int N, int group_
                      float norm_eps, int epilogue, const uint16_t* residual, uint16_t* y, int ldy,
                      void* scratch, size_t scratch_bytes, mtl_stream_t stream);
 
+/* mtl_w4a16_linear for callers that cannot allocate device memory (a host
+ * that owns all device memory in its own pool and gives this library no
+ * allocator, or a serving loop recording its step under stream capture,
+ * where cudaMalloc is not permitted).  No counterpart in the reference: it
+ * exists for such embedders only.  Same arguments and results as
+ * mtl_w4a16_linear minus the scratch buffer: the split-K scratch is a fixed
+ * 1 MiB device array inside the library (held on every GPU that loads the
+ * library until exit); shapes needing more (mtl_w4_plan) fail with
+ * MTL_E_SCRATCH.  All calls share that array: calls that can overlap on the
+ * GPU (unordered streams) race, calls ordered on one stream are fine.  The
+ * first call on each device resolves the array's address (with that device
+ * current); make it before any stream capture.  Allocates nothing. */
+int mtl_w4a16_linear_noalloc(const uint16_t* x, int ldx, int M, int K, int N, int group_size, int param_fmt,
+                             const void* tiles, int zero_offset, const int32_t* k_perm, const uint16_t* norm_w,
+                             float norm_eps, int epilogue, const uint16_t* residual, uint16_t* y, int ldy,
+                             mtl_stream_t stream);
 
 /* ------------------------------------------------------ decoder step ops */
 

@@ -3,3 +3,4 @@
 #include "w4_gemv.cu"
 #include "step_kernels.cu"
 #include "capi.cu"
+#include "noalloc.cu"
