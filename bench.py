@@ -366,17 +366,121 @@ def run_reference_arm(args, ctx):
     print(json.dumps(line), flush=True)
 
 
+def profile_gemv(launches: int = 6):
+    """Small case for ncu: config 0 (AutoGPTQ W4 linear 4096 -> 12288, g128,
+    seeded synthetic tensors) on cuda:0, `launches` launches over 4 weight
+    copies (105 MB, > L2)."""
+    import numpy as np
+    import torch
+    from moss_tts_lite_b200 import _lib
+    from moss_tts_lite_b200.quant import QuantLinear
+    from oracle import w4 as ow
+    dev = torch.device("cuda", 0)
+    K, N, g = 4096, 12288, 128
+    d = ow.synth_gptq_linear(K, N, g, seed=0)
+
+    def t(a, dtype=None):
+        x = torch.from_numpy(np.ascontiguousarray(a))
+        return (x.view(dtype) if dtype is not None else x).to(dev)
+    lins = [QuantLinear.from_tensors(t(d["qweight"]), t(d["qzeros"]), t(d["scales"], torch.float16),
+                                     t(d["g_idx"]), group_size=g) for _ in range(4)]
+    x = t(d["x"], torch.bfloat16)
+    out = torch.empty(1, N, dtype=torch.bfloat16, device=dev)
+    for i in range(launches):
+        lins[i % 4].w.linear(x, out=out)
+    torch.cuda.synchronize()
+    st = _lib.device_status()
+    print(json.dumps({"profile": "w4_gemv cfg0", "launches": launches, "bytes_per_launch": lins[0].w.tiles.numel()
+                      + 2 * K + 2 * N, "device_status": st}))
+    if st != 0:
+        raise SystemExit(1)
+
+
+def run_reference_gpu(args, ctx):
+    """--impl reference-gpu (informational, rank 0): the unmodified reference
+    W4 fast path on this GPU through its public API - moss_tts_lite.model.
+    MossTTSModel + moss_tts_lite.fast.FastMossTTS(quant='w4', g128, tinygemm)
+    + generate_fast(greedy) - on the same synthetic model and prompt; decode
+    steps/s from generate_fast's own per-step CUDA-event stats, skipping the
+    warm-up steps.  Needs the reference package under baseline/_ref."""
+    import torch
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if ref_dir not in sys.path:
+        sys.path.append(ref_dir)
+    try:
+        from moss_tts_lite.fast import FastMossTTS as RefFast
+        from moss_tts_lite.fast import generate_fast as ref_generate_fast
+        from moss_tts_lite.model import MossTTSModel as RefModel
+    except Exception as e:  # noqa: BLE001
+        print(json.dumps({"impl": "reference-gpu", "unavailable": f"reference package not importable: {e}"}))
+        return
+    if ctx.rank != 0:
+        return
+    dev = torch.device("cuda", ctx.local)
+    torch.cuda.set_device(dev)
+    c = CFG
+    H, D = c["hidden"], c["head_dim"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(c["seed"])
+
+    def r(*shape):
+        return (torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * c["std"]).to(torch.bfloat16)
+
+    ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=dev)  # noqa: E731
+    w = {"language_model.embed_tokens.weight": r(c["vocab"], H), "language_model.norm.weight": ones(H)}
+    for li in range(c["n_layers"]):
+        p = f"language_model.layers.{li}"
+        w[f"{p}.input_layernorm.weight"] = ones(H)
+        w[f"{p}.post_attention_layernorm.weight"] = ones(H)
+        w[f"{p}.self_attn.q_proj.weight"] = r(c["n_heads"] * D, H)
+        w[f"{p}.self_attn.k_proj.weight"] = r(c["n_kv"] * D, H)
+        w[f"{p}.self_attn.v_proj.weight"] = r(c["n_kv"] * D, H)
+        w[f"{p}.self_attn.o_proj.weight"] = r(H, c["n_heads"] * D)
+        w[f"{p}.self_attn.q_norm.weight"] = ones(D)
+        w[f"{p}.self_attn.k_norm.weight"] = ones(D)
+        w[f"{p}.mlp.gate_proj.weight"] = r(c["inter"], H)
+        w[f"{p}.mlp.up_proj.weight"] = r(c["inter"], H)
+        w[f"{p}.mlp.down_proj.weight"] = r(H, c["inter"])
+    for i in range(32):
+        w[f"emb_ext.{i}.weight"] = r(1025, H)
+    w["lm_heads.0.weight"] = r(c["vocab"], H)
+    for i in range(32):
+        w[f"lm_heads.{i + 1}.weight"] = r(1025, H)
+    model = RefModel(w, device=dev, dtype=torch.bfloat16, max_seq_len=MAX_SEQ)
+    del w
+    fast = RefFast(model, quant="w4", w4_group_size=c["group_size"])
+    prompt = make_prompt(c["seed"]).to(dev)
+    st = {}
+    n = args.warmup + args.steps + 1
+    res = ref_generate_fast(fast, {"input_ids": prompt}, max_new_tokens=n, greedy=True, watchdog=False, stats=st)
+    ms = st["step_ms"][args.warmup:args.warmup + args.steps]
+    v = 1000.0 / (sum(ms) / len(ms))
+    print(json.dumps({"metric": METRIC, "impl": "reference-gpu", "value": v, "unit": "steps/s",
+                      "ms_per_step": 1000.0 / v, "steps": len(ms), "warmup": args.warmup,
+                      "steps_generated": res.n_steps,
+                      "what": "moss_tts_lite FastMossTTS(quant='w4', g128) + generate_fast(greedy), same "
+                              "synthetic model and prompt, per-step CUDA-event stats of the reference"}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--impl", default="mtl", choices=["mtl", "reference"])
+    ap.add_argument("--impl", default="mtl", choices=["mtl", "reference", "reference-gpu"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-gemv", action="store_true", help="small config-0 GEMV case for ncu")
     args = ap.parse_args()
+    if args.profile_gemv:
+        profile_gemv()
+        return
     ctx = _Dist()
     if args.impl == "reference":
         run_reference_arm(args, ctx)
+        return
+    if args.impl == "reference-gpu":
+        run_reference_gpu(args, ctx)
         return
     import torch
     torch.cuda.set_device(ctx.local)
@@ -422,7 +526,10 @@ def main():
                     "steps_generated": e2e_steps},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": (traffic or {}).get("dram_bytes_per_launch"),
+                         # ncu DRAM bytes of the config-0 capture, scaled by its
+                         # traffic/algorithmic ratio to the average step launch
+                         "traffic": (bytes_per_launch * traffic["traffic_over_algorithmic"]
+                                     if traffic else None),
                          "kernel": "w4_gemv_kernel (144 launches per step: q|k|v, o, gate|up, down x 36)",
                          "bytes_per_launch": bytes_per_launch, "us_per_launch": s_per_launch * 1e6},
             "gpu_launches": steps * (1 + 5 * CFG["n_layers"] + 2 + 1),

@@ -196,6 +196,28 @@ int mtl_argmax_masked(const uint16_t* x, int cols, const int32_t* excluded, int 
 int mtl_greedy_feed(const uint16_t* audio_logits, const uint16_t* two_logits, int64_t* ids_row, int64_t* pos,
                     int gen_slot_id, int delay_slot_id, mtl_stream_t stream);
 
+/* Fused sample_token (sampling.py:70-98) for up to 40 logits rows of one
+ * decode step (fast.py:491-545), one draw per row:
+ *   row r = logits + row_index[r] * ld (bf16, `cols` values; row_index host
+ *   array); x = bf16(x * (1/temperature)); ids in HOST array `excluded`
+ *   (<= 8) -> -inf; repetition penalty (sampling.py:36-67) on the ids set in
+ *   device bitmap seen_bits[seen_set_of_row[r]] (words_per_set uint32 words;
+ *   penalty 1 or seen_bits NULL = off); top-k (top_k <= 0 = off, at most 2048
+ *   candidates); top-p on bf16 softmax/cumsum (top_p >= 1 = off); one
+ *   categorical draw from Philox4x32-10 keyed by (seed, offset, r).
+ *   scan_rows (host array, NULL = all 1): how many rows the reference's
+ *   sample_token call held together with row r; PyTorch's CUDA cumsum of
+ *   bf16 groups its roundings differently for one-row and multi-row
+ *   tensors, and the top-p cut-off follows the same grouping.
+ *   out[r] (device int64) = sampled column + out_add.
+ * Candidate sets and probabilities follow the reference's arithmetic; the
+ * random stream is this library's own (not torch.multinomial's). */
+int mtl_sample_rows(const uint16_t* logits, int ld, int cols, int n_rows, const int32_t* row_index,
+                    float temperature, int top_k, float top_p, float repetition_penalty, const uint32_t* seen_bits,
+                    int words_per_set, const int32_t* seen_set_of_row, const int32_t* excluded, int n_excluded,
+                    const int32_t* scan_rows, uint64_t seed, uint64_t offset, int64_t out_add, int64_t* out,
+                    mtl_stream_t stream);
+
 /* Round-to-nearest W4 quantisation of a bf16 weight [N, K] exactly as
  * FastMossTTS._quantize (fast.py:85-96) / gptq.rtn_quantize (gptq.py:54-64):
  * q uint8 [N, K] codes and qsz bf16 [K/g, N, 2] = (scale, min + 8 scale). */

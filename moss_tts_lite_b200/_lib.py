@@ -55,6 +55,10 @@ SIGNATURES = {
     "mtl_argmax_masked": (_c_int, [_c_void_p, _c_int, ctypes.POINTER(ctypes.c_int32), _c_int, _c_void_p,
                                    _c_void_p]),
     "mtl_greedy_feed": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p]),
+    "mtl_sample_rows": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int32), _c_float,
+                                 _c_int, _c_float, _c_float, _c_void_p, _c_int, ctypes.POINTER(ctypes.c_int32),
+                                 ctypes.POINTER(ctypes.c_int32), _c_int, ctypes.POINTER(ctypes.c_int32),
+                                 ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64, _c_void_p, _c_void_p]),
     "mtl_rmsnorm": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_float, _c_void_p, _c_int,
                              _c_void_p]),
     "mtl_w4_rtn_quantize": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p]),

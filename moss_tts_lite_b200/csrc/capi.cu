@@ -27,6 +27,7 @@ cudaError_t launch_greedy_feed(const uint16_t* la, const uint16_t* two, int64_t*
                                int delay_slot, cudaStream_t s, int use_pdl);
 cudaError_t launch_rmsnorm_rows(const uint16_t* x, int rows, int K, int ldx, const uint16_t* w, float eps,
                                 uint16_t* y, int ldy, cudaStream_t s, int use_pdl);
+cudaError_t launch_sample_rows(const SampleArgs& a, cudaStream_t s);
 cudaError_t w4_pack_gptq(const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
                          const int32_t* perm, int K, int N, int g, uint8_t* tiles, cudaStream_t s);
 cudaError_t w4_pack_ref(const uint8_t* q, const uint16_t* qsz, int K, int N, int g, uint8_t* tiles,
@@ -340,6 +341,69 @@ int mtl_greedy_feed(const uint16_t* audio_logits, const uint16_t* two_logits, in
   cudaError_t e = mtl::launch_greedy_feed(audio_logits, two_logits, ids_row, pos, gen_slot_id, delay_slot_id, stream,
                                           use_pdl());
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_greedy_feed");
+}
+
+// Threads per row (log2) of PyTorch's shared-memory cumsum of a [num_rows,
+// row_size] tensor (get_log_num_threads_x_inner_scan, ATen ScanUtils.cuh):
+// about 512 threads per block split in the ratio of row_size to num_rows,
+// clamped to [2^4, 2^9].
+static int inner_scan_log_threads_x(int num_rows, int row_size) {
+  int lx = 0, ly = 0;
+  while ((1 << lx) < row_size) ++lx;
+  while ((1 << ly) < num_rows) ++ly;
+  int l = (9 + lx - ly) / 2;
+  return l < 4 ? 4 : (l > 9 ? 9 : l);
+}
+
+int mtl_sample_rows(const uint16_t* logits, int ld, int cols, int n_rows, const int32_t* row_index,
+                    float temperature, int top_k, float top_p, float repetition_penalty, const uint32_t* seen_bits,
+                    int words_per_set, const int32_t* seen_set_of_row, const int32_t* excluded, int n_excluded,
+                    const int32_t* scan_rows, uint64_t seed, uint64_t offset, int64_t out_add, int64_t* out,
+                    mtl_stream_t stream) {
+  if (!logits || !out || !row_index) return fail(MTL_E_INVALID, "mtl_sample_rows: NULL pointer");
+  if (n_rows < 1 || n_rows > mtl::kSampleMaxRows || cols < 1 || ld < cols)
+    return fail(MTL_E_INVALID, "mtl_sample_rows: n_rows=%d (1..%d) cols=%d ld=%d", n_rows, mtl::kSampleMaxRows, cols, ld);
+  if (!(temperature > 0.f)) return fail(MTL_E_INVALID, "mtl_sample_rows: temperature must be > 0");
+  if (n_excluded < 0 || n_excluded > mtl::kSampleMaxExcl || (n_excluded && !excluded))
+    return fail(MTL_E_INVALID, "mtl_sample_rows: n_excluded=%d (<= %d)", n_excluded, mtl::kSampleMaxExcl);
+  const int k = (top_k > 0 && top_k < cols) ? top_k : cols;
+  if (k > mtl::kSampleMaxCand)
+    return fail(MTL_E_UNSUPPORTED, "mtl_sample_rows: %d candidates (top_k=%d, cols=%d) exceed %d", k, top_k, cols,
+                mtl::kSampleMaxCand);
+  if (repetition_penalty != 1.0f && seen_bits && (!seen_set_of_row || words_per_set < (cols + 31) / 32))
+    return fail(MTL_E_INVALID, "mtl_sample_rows: seen bitmap needs words_per_set >= %d", (cols + 31) / 32);
+  mtl::SampleArgs a{};
+  a.logits = logits;
+  a.ld = ld;
+  a.cols = cols;
+  a.n_rows = n_rows;
+  const bool pen = repetition_penalty != 1.0f && seen_bits != nullptr;
+  for (int r = 0; r < n_rows; ++r) {
+    a.row_index[r] = row_index[r];
+    a.seen_set[r] = pen ? seen_set_of_row[r] : -1;
+    const int sr = scan_rows ? scan_rows[r] : 1;
+    if (sr < 1) return fail(MTL_E_INVALID, "mtl_sample_rows: scan_rows[%d]=%d (>= 1)", r, sr);
+    a.scan_lognx[r] = sr == 1 ? 0 : inner_scan_log_threads_x(sr, cols);
+  }
+  a.seen_bits = pen ? seen_bits : nullptr;
+  a.words_per_set = words_per_set;
+  // PyTorch on CUDA divides by a Python scalar as a multiply by its float reciprocal
+  a.inv_temp = 1.0f / temperature;
+  a.penalty = repetition_penalty;
+  a.inv_penalty = 1.0f / repetition_penalty;
+  a.top_k = top_k;
+  // `cumulative_probs > top_p` compares bf16 against the scalar rounded to bf16
+  a.top_p_bf = top_p >= 1.0f ? 2.0f : __bfloat162float(__float2bfloat16_rn(top_p));
+  a.n_excl = n_excluded;
+  for (int e = 0; e < n_excluded; ++e) a.excl[e] = excluded[e];
+  a.seed_lo = (uint32_t)seed;
+  a.seed_hi = (uint32_t)(seed >> 32);
+  a.off_lo = (uint32_t)offset;
+  a.off_hi = (uint32_t)(offset >> 32);
+  a.out = out;
+  a.out_add = out_add;
+  cudaError_t e = mtl::launch_sample_rows(a, stream);
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_sample_rows");
 }
 
 int mtl_rmsnorm(const uint16_t* x, int rows, int K, int ldx, const uint16_t* weight, float eps, uint16_t* y,

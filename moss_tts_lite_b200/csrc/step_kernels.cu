@@ -334,20 +334,40 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   }
   __syncthreads();
   if (!last_flag) return;
+  // --- merge: all (max, sum) pairs in one round of independent loads, the
+  //     rescale factors per split, then each thread's 128-dim slice with its
+  //     partial loads issued back to back.  Only splits that held positions.
+  __shared__ float mg_m[kAttnMaxRep * 64], mg_l[kAttnMaxRep * 64], mg_lsum[kAttnMaxRep];
+  const int nact = min(a.splits, (s1 + chunk - 1) / chunk);
   const float* basep = a.partials + (((size_t)st * a.nkv + h) * a.splits * rep) * (2 + kHeadDim);
-  for (int r = 0; r < rep; ++r) {
+  for (int i = tid; i < rep * nact; i += kAttnThreads) {
+    const int r = i / nact, j = i - r * nact;
+    const float* pj = basep + ((size_t)j * rep + r) * (2 + kHeadDim);
+    mg_m[r * 64 + j] = __ldcg(pj);
+    mg_l[r * 64 + j] = __ldcg(pj + 1);
+  }
+  __syncthreads();
+  for (int r = warp; r < rep; r += 4) {
     float m = -INFINITY;
-    for (int j = 0; j < a.splits; ++j) m = fmaxf(m, __ldcg(basep + ((size_t)j * rep + r) * (2 + kHeadDim)));
-    float l = 0.f, acc = 0.f;
-    for (int j = 0; j < a.splits; ++j) {
-      const float* pj = basep + ((size_t)j * rep + r) * (2 + kHeadDim);
-      const float mj = __ldcg(pj);
-      if (mj == -INFINITY) continue;
-      const float f = expf(mj - m);
-      l = fmaf(__ldcg(pj + 1), f, l);
-      acc = fmaf(__ldcg(pj + 2 + tid), f, acc);
+    for (int j = lane; j < nact; j += 32) m = fmaxf(m, mg_m[r * 64 + j]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int j = lane; j < nact; j += 32) {
+      const float mj = mg_m[r * 64 + j];
+      const float f = (mj == -INFINITY) ? 0.f : expf(mj - m);
+      mg_m[r * 64 + j] = f;  // becomes the rescale factor of split j
+      l = fmaf(mg_l[r * 64 + j], f, l);
     }
-    a.out[(size_t)st * a.nh * kHeadDim + (size_t)(h * rep + r) * kHeadDim + tid] = f32_to_bf16_bits(acc / l);
+    l = warp_sum(l);
+    if (lane == 0) mg_lsum[r] = l;
+  }
+  __syncthreads();
+  for (int r = 0; r < rep; ++r) {
+    float acc = 0.f;
+#pragma unroll 8
+    for (int j = 0; j < nact; ++j)
+      acc = fmaf(__ldcg(basep + ((size_t)j * rep + r) * (2 + kHeadDim) + 2 + tid), mg_m[r * 64 + j], acc);
+    a.out[(size_t)st * a.nh * kHeadDim + (size_t)(h * rep + r) * kHeadDim + tid] = f32_to_bf16_bits(acc / mg_lsum[r]);
   }
 }
 

@@ -378,6 +378,10 @@ class _Decider:
             kernels.argmax_rows(la, self.dev_out[1:])
         if need_text:
             kernels.argmax_masked(text_src, self.dev_out[0:1], text_excluded)
+        return self.fetch()
+
+    def fetch(self):
+        """One device->host copy of the step's decisions."""
         self.host.copy_(self.dev_out, non_blocking=True)
         torch.cuda.current_stream().synchronize()
         return self.host.tolist()
@@ -455,8 +459,7 @@ def generate_fast(
     audio_do_sample = audio_temperature > 0
     if not audio_do_sample:
         audio_temperature = 1
-    gen = torch.Generator(device=device)
-    gen.manual_seed(seed)
+    step_offset = 0      # Philox stream offset of the sampled decisions
 
     col0 = input_ids[0, :, 0].tolist()
     last0 = col0[-1]
@@ -469,7 +472,9 @@ def generate_fast(
     is_stopping = False
     pre_exclude0 = (PAD_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_DELAY_SLOT_TOKEN_ID, AUDIO_END_TOKEN_ID)
 
-    prev_audio = input_ids[0, :, 1:].tolist()        # generation_ids[:, :, 1:] rows
+    prompt_audio = input_ids[0, :, 1:].tolist()
+    seen_ch0 = {r[0] for r in prompt_audio}                      # generation_ids[:, :, 1]
+    seen_rest = {t for r in prompt_audio for t in r[1:]}         # generation_ids[:, :, 2:]
     text_steps: list = []
     audio_steps: list = []
     n_steps = 0
@@ -534,15 +539,30 @@ def generate_fast(
         else:
             dec = None
 
+        sampled = None
+        if (sampling_text and text_do_sample) or (need_audio and audio_do_sample):
+            step_offset += 1
+            if sampling_text and text_do_sample:
+                sample_rows.text(fast, is_audio, time_step, text_temperature, text_top_k, text_top_p,
+                                 seed, 2 * step_offset, decider.dev_out[0:1])
+            rows = []
+            if need_audio and audio_do_sample:
+                rows = sample_rows.audio(fast, smask, audio_temperature, audio_top_k, audio_top_p,
+                                         audio_repetition_penalty, seen_ch0, seen_rest, seed,
+                                         2 * step_offset + 1, decider.dev_out[1:])
+            host = decider.fetch()
+            sampled = (host[0], {j: host[1 + i] for i, j in enumerate(rows)})
+
         if sampling_text:
             if not text_do_sample:
                 if is_audio:
                     next_text = AUDIO_GEN_SLOT_TOKEN_ID if dec[0] == 0 else AUDIO_DELAY_SLOT_TOKEN_ID
                 else:
                     next_text = int(dec[0])
+            elif is_audio:
+                next_text = AUDIO_GEN_SLOT_TOKEN_ID if sampled[0] == 0 else AUDIO_DELAY_SLOT_TOKEN_ID
             else:
-                next_text = sample_rows.text(fast, is_audio, time_step, text_temperature, text_top_k,
-                                             text_top_p, gen)
+                next_text = int(sampled[0])
         if next_text == AUDIO_START_TOKEN_ID:
             is_audio = True
         if next_text == IM_END_TOKEN_ID:
@@ -550,14 +570,9 @@ def generate_fast(
 
         next_audio = [AUDIO_PAD_CODE] * N_VQ
         if need_audio:
-            if not audio_do_sample:
-                toks = dec[1:]
-            else:
-                toks = sample_rows.audio(fast, smask, audio_temperature, audio_top_k, audio_top_p,
-                                         audio_repetition_penalty, prev_audio, gen)
             for j in range(N_VQ):
                 if smask[j]:
-                    next_audio[j] = int(toks[j])
+                    next_audio[j] = int(dec[1 + j]) if not audio_do_sample else int(sampled[1][j])
 
         ch0_val = next_audio[0]
         if watchdog and not wd_stop and is_audio and dl == _INT64_MAX:
@@ -591,7 +606,8 @@ def generate_fast(
 
         # pageable source: the copy is staged before copy_ returns
         fast.ids_row.view(-1).copy_(torch.tensor([next_text] + next_audio, dtype=torch.long))
-        prev_audio.append(next_audio)
+        seen_ch0.add(next_audio[0])
+        seen_rest.update(next_audio[1:])
         if _stats is not None:
             _stats.setdefault("step_wall_s", []).append(time.perf_counter())
         text_steps.append(next_text)

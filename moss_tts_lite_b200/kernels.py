@@ -93,6 +93,29 @@ def greedy_feed(la: torch.Tensor, two: torch.Tensor, ids_row: torch.Tensor, pos_
               gen_slot, delay_slot, _s())
 
 
+def sample_rows(logits: torch.Tensor, rows, *, temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0,
+                penalty: float = 1.0, seen_bits: torch.Tensor | None = None, seen_set=None, excluded=(),
+                seed: int = 0, offset: int = 0, out: torch.Tensor, out_add: int = 0, scan_rows=None) -> torch.Tensor:
+    """One sampled token per listed row of bf16 ``logits`` [R, V] into out[0:len(rows)] (int64).
+    ``scan_rows[i]``: rows of the reference's sample_token call that held
+    row i (1 = a one-row call; default all 1), which fixes how its CUDA
+    cumsum rounds the top-p partial sums."""
+    _bf16(logits, "logits")
+    V = logits.shape[-1]
+    rows = list(rows)
+    idx = (ctypes.c_int32 * len(rows))(*rows)
+    sets = (ctypes.c_int32 * len(rows))(*(seen_set if seen_set is not None else [0] * len(rows)))
+    ex = list(excluded)
+    exa = (ctypes.c_int32 * max(1, len(ex)))(*ex)
+    words = seen_bits.shape[-1] if seen_bits is not None else 0
+    sr = (ctypes.c_int32 * len(rows))(*(scan_rows if scan_rows is not None else [1] * len(rows)))
+    _lib.call("mtl_sample_rows", logits.data_ptr(), V, V, len(rows), idx, ctypes.c_float(temperature), int(top_k),
+              ctypes.c_float(top_p), ctypes.c_float(penalty), _p(seen_bits), words, sets, exa, len(ex), sr,
+              ctypes.c_uint64(seed & 0xFFFFFFFFFFFFFFFF), ctypes.c_uint64(offset), ctypes.c_int64(out_add),
+              out.data_ptr(), _s())
+    return out
+
+
 def rtn_quantize(w: torch.Tensor, group_size: int = 128) -> tuple[torch.Tensor, torch.Tensor]:
     """Reference RTN W4 (fast.py:85-96): bf16 [N, K] -> (q uint8 [N, K], qsz bf16 [K/g, N, 2])."""
     _bf16(w, "w")

@@ -138,3 +138,77 @@ def test_mini_model_step_vs_reference():
         lt = bf16_to_f32(m.text_logits(h))
         assert np.array_equal(lt[z[f"text_top_idx{t}"]], z[f"text_top_val{t}"])
         assert np.array_equal(np.sort(lt)[::-1][:16], z[f"text_top_val{t}"])
+
+
+def test_philox4x32_10_known_answers():
+    """Published known-answer vectors of Philox4x32-10 (Salmon et al. 2011,
+    Random123 kat_vectors): the generator behind the sampling draws."""
+    assert osmp.philox4x32_10([0, 0, 0, 0], [0, 0]) == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]
+    assert osmp.philox4x32_10([0xFFFFFFFF] * 4, [0xFFFFFFFF] * 2) == [0x408F276D, 0x41C83B0E, 0xA20BC7C6,
+                                                                        0x6D5451FD]
+    assert osmp.philox4x32_10([0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344], [0xA4093822, 0x299F31D0]) == \
+        [0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1]
+
+
+def test_oracle_sample_row_candidates_follow_reference_ops():
+    """The oracle's candidate set (top-k then top-p) equals the reference's
+    apply_top_k / apply_top_p_optimized on the same bf16 logits (CPU torch,
+    so with the CPU cumsum; tests/test_sampling_gpu.py checks CUDA)."""
+    import torch
+    import sys
+    sys.path.insert(0, "/nonexistent")
+    from oracle.bf16 import f32_to_bf16
+    rng = np.random.default_rng(3)
+    for trial in range(20):
+        x = f32_to_bf16(rng.standard_normal(1025).astype(np.float32) * 2)
+        k, p = [(25, 0.8), (50, 0.95), (0, 0.8), (25, 1.0)][trial % 4]
+        cand, probs = osmp.sample_row(x, top_k=k, top_p=p, return_probs=True, device="cpu")
+        mine = set(int(c) for c, pr in zip(cand, probs) if pr > 0)
+        t = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).view(1, -1)
+        ref = t.clone()
+        if k:
+            ref = torch.full_like(t, float("-inf")).scatter(1, torch.topk(t, k).indices, torch.topk(t, k).values)
+        if p < 1:
+            probs_t = torch.softmax(ref, -1)
+            sp, si = torch.sort(probs_t, descending=True)
+            cum = torch.cumsum(sp, -1)
+            rem = cum > p
+            rem[..., 1:] = rem[..., :-1].clone()
+            rem[..., 0] = False
+            mask = torch.zeros_like(ref, dtype=torch.bool).scatter(1, si, rem)
+            ref = ref.masked_fill(mask, float("-inf"))
+        theirs = set(torch.nonzero(torch.isfinite(ref[0])).view(-1).tolist())
+        # tie-robust: torch.topk breaks ties at the cut-off in an unspecified
+        # order, the oracle keeps the lowest ids; the kept values must agree
+        vals = bf16_to_f32(x)
+        assert sorted(vals[list(mine)]) == sorted(vals[list(theirs)]), (trial, sorted(mine ^ theirs))
+
+
+def test_cuda_cumsum_grouping_vs_golden():
+    """oracle.sampling.cumsum_bf16_cuda reproduces torch.cumsum of bf16 on a
+    B200 bit for bit, for one-row tensors (device-wide scan, up to 8000
+    items: several scan tiles) and multi-row tensors (per-row shared-memory
+    scan with 2..31 rows); fixtures from tests/golden/make_golden_cumsum_cuda.py."""
+    import sys
+    sys.path.insert(0, GOLD)
+    from make_golden_cumsum_cuda import SHAPES
+    z = _load("cumsum_bf16_cuda.npz")
+    for i, (r, n) in enumerate(SHAPES):
+        p = bf16_to_f32(z[f"in{i}"]).reshape(r, n)
+        want = bf16_to_f32(z[f"out{i}"]).reshape(r, n)
+        got = np.stack([osmp.cumsum_bf16_cuda(p[j], r, n) for j in range(r)])
+        assert np.array_equal(got, want), (i, r, n, int((got != want).sum()))
+    # the plain bf16 running sum is not what the device computes past 30 items
+    p = bf16_to_f32(z["in2"]).reshape(-1)
+    run, seq = np.float32(0), []
+    for v in p:
+        run = np.float32(osmp._bf(np.float32(run + v)).item())
+        seq.append(run)
+    assert not np.array_equal(np.asarray(seq, np.float32), bf16_to_f32(z["out2"]).reshape(-1))
+
+
+def test_inner_scan_thread_split():
+    """get_log_num_threads_x_inner_scan for the audio row shapes the
+    reference scans: [R, 1025] for R = 2..31 sampled channels."""
+    assert [osmp.inner_scan_log_threads_x(r, 1025) for r in (2, 4, 5, 8, 9, 16, 17, 31)] == [9, 9, 8, 8, 8, 8, 7, 7]
+    assert osmp.inner_scan_log_threads_x(1024, 16) == 4
