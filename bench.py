@@ -396,6 +396,64 @@ def profile_gemv(launches: int = 6):
         raise SystemExit(1)
 
 
+def profile_attn(timed: bool = True, launches: int = 4, lengths=(136, 1024, 4096, 8191)):
+    """Decode attention of configuration 2 alone (32 query / 8 KV heads x 128,
+    KV cache [8, 8192, 128] for one layer, seeded synthetic values): per cache
+    length, the device time of 50 launches chained in a CUDA graph (if
+    `timed`), then `launches` plain launches at the first length (the ncu
+    capture case)."""
+    import torch
+    from moss_tts_lite_b200 import _lib, kernels
+    from moss_tts_lite_b200.model import rope_tables
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device="cpu").manual_seed(0)
+    nh, nkv, hd, max_seq = CFG["n_heads"], CFG["n_kv"], CFG["head_dim"], MAX_SEQ
+    splits = 16
+
+    def r(*shape, s=1.0):
+        return (torch.randn(*shape, generator=g) * s).to(torch.bfloat16).to(dev)
+    qkv = r(1, (nh + 2 * nkv) * hd)
+    qn, kn = r(hd, s=0.1) + 1, r(hd, s=0.1) + 1
+    cos, sin = rope_tables(max_seq, dev, torch.bfloat16, hd)
+    kc, vc = r(nkv, max_seq, hd), r(nkv, max_seq, hd)
+    out = torch.empty(1, nh * hd, dtype=torch.bfloat16, device=dev)
+    scratch = torch.zeros(_lib.attn_scratch_bytes(1, nh, nkv, splits), dtype=torch.uint8, device=dev)
+    pos = torch.zeros(1, dtype=torch.int64, device=dev)
+
+    def launch(stable=False):
+        kernels.attn_decode(qkv, qn, kn, cos, sin, kc, vc, pos, nh, nkv, splits, out, scratch, kv_stable=stable)
+    res = {}
+    s = torch.cuda.Stream(device=dev)
+    for L in (lengths if timed else ()):
+        pos.fill_(L - 1)
+        with torch.cuda.stream(s):
+            launch()
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=s):
+                for _ in range(50):
+                    launch(stable=True)
+            for _ in range(3):
+                gr.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(10):
+                gr.replay()
+            e1.record(s)
+            e1.synchronize()
+            res[L] = e0.elapsed_time(e1) * 1e3 / 500
+            del gr
+    pos.fill_(lengths[0] - 1)
+    for _ in range(launches):
+        launch()
+    torch.cuda.synchronize()
+    st = _lib.device_status()
+    print(json.dumps({"profile": "attn_decode cfg2", "us_per_launch_in_graph": res, "launches": launches,
+                      "device_status": st}))
+    if st != 0:
+        raise SystemExit(1)
+
+
 def run_reference_gpu(args, ctx):
     """--impl reference-gpu (informational, rank 0): the unmodified reference
     W4 fast path on this GPU through its public API - moss_tts_lite.model.
@@ -471,9 +529,14 @@ def main():
     ap.add_argument("--impl", default="mtl", choices=["mtl", "reference", "reference-gpu"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-gemv", action="store_true", help="small config-0 GEMV case for ncu")
+    ap.add_argument("--profile-attn", action="store_true", help="decode attention alone (config 2 heads)")
+    ap.add_argument("--profile-attn-launches", action="store_true", help="4 plain attention launches (ncu case)")
     args = ap.parse_args()
     if args.profile_gemv:
         profile_gemv()
+        return
+    if args.profile_attn or args.profile_attn_launches:
+        profile_attn(timed=args.profile_attn)
         return
     ctx = _Dist()
     if args.impl == "reference":

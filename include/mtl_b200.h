@@ -147,14 +147,21 @@ int mtl_attn_scratch_bytes(int streams, int n_heads, int n_kv, int splits, size_
  *   k_cache, v_cache    bf16 [n_kv, max_seq, 128] of this layer for stream 0;
  *              stream s starts cache_stream_stride elements later
  *   pos        int64 [streams] (device): position being decoded
- *   splits     KV splits per head (1..64); each covers >= 32 positions
+ *   splits     KV splits per head (1..64); each covers >= 64 positions
+ *   flags      0 or MTL_ATTN_KV_STABLE: pos and cache rows [0, pos) were
+ *              written by work that completed before the preceding kernel
+ *              started (e.g. the call is one step of a CUDA graph whose
+ *              replays follow the steps that wrote them); the kernel then
+ *              starts streaming the cache before waiting on the preceding
+ *              kernel (programmatic dependent launch)
  *   out        bf16 [streams, n_heads * 128]
  * head_dim must be 128 and n_heads / n_kv <= 8. */
+#define MTL_ATTN_KV_STABLE 1
 int mtl_attn_decode(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_t* k_norm_w,
                     const uint16_t* rope_cos, const uint16_t* rope_sin, uint16_t* k_cache, uint16_t* v_cache,
                     long long cache_stream_stride, int max_seq, const int64_t* pos, int streams, int n_heads,
-                    int n_kv, int head_dim, int splits, uint16_t* out, void* scratch, size_t scratch_bytes,
-                    mtl_stream_t stream);
+                    int n_kv, int head_dim, int splits, int flags, uint16_t* out, void* scratch,
+                    size_t scratch_bytes, mtl_stream_t stream);
 
 /* y = epilogue(x . W^T) for bf16 weights W [N, K] (the lm heads,
  * model.py:240-295, fast.py:174-194, and bf16 backbone linears: F.linear at

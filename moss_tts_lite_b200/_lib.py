@@ -18,6 +18,7 @@ MTL_FMT_GPTQ = 1
 MTL_EPI_STORE = 0
 MTL_EPI_RESIDUAL = 1
 MTL_EPI_SWIGLU = 2
+MTL_ATTN_KV_STABLE = 1
 
 ABI_VERSION = 1
 
@@ -48,7 +49,7 @@ SIGNATURES = {
     "mtl_attn_scratch_bytes": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_size_p]),
     "mtl_attn_decode": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                  ctypes.c_longlong, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int,
-                                 _c_void_p, _c_void_p, _c_size_t, _c_void_p]),
+                                 _c_int, _c_void_p, _c_void_p, _c_size_t, _c_void_p]),
     "mtl_bf16_linear": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_float, _c_void_p,
                                  _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_int, _c_void_p]),
     "mtl_argmax_rows": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),

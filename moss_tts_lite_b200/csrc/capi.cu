@@ -238,7 +238,7 @@ int mtl_embed_sum(const int64_t* ids, int M, const uint16_t* emb_text, int text_
 }
 
 static size_t attn_partial_floats(int streams, int n_heads, int n_kv, int splits) {
-  return (size_t)streams * n_kv * splits * (n_heads / n_kv) * (2 + mtl::kHeadDim);
+  return (size_t)streams * n_kv * splits * (n_heads / n_kv) * mtl::kAttnRec;
 }
 static size_t attn_counter_bytes(int streams, int n_kv) { return ((size_t)streams * n_kv * 4 + 255) / 256 * 256; }
 
@@ -252,8 +252,8 @@ int mtl_attn_scratch_bytes(int streams, int n_heads, int n_kv, int splits, size_
 int mtl_attn_decode(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_t* k_norm_w,
                     const uint16_t* rope_cos, const uint16_t* rope_sin, uint16_t* k_cache, uint16_t* v_cache,
                     long long cache_stream_stride, int max_seq, const int64_t* pos, int streams, int n_heads,
-                    int n_kv, int head_dim, int splits, uint16_t* out, void* scratch, size_t scratch_bytes,
-                    mtl_stream_t stream) {
+                    int n_kv, int head_dim, int splits, int flags, uint16_t* out, void* scratch,
+                    size_t scratch_bytes, mtl_stream_t stream) {
   if (!qkv || !q_norm_w || !k_norm_w || !rope_cos || !rope_sin || !k_cache || !v_cache || !pos || !out || !scratch)
     return fail(MTL_E_INVALID, "mtl_attn_decode: NULL pointer");
   if (head_dim != mtl::kHeadDim) return fail(MTL_E_UNSUPPORTED, "head_dim %d (only 128)", head_dim);
@@ -263,6 +263,7 @@ int mtl_attn_decode(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_
     return fail(MTL_E_INVALID, "streams=%d max_seq=%d splits=%d", streams, max_seq, splits);
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || cache_stream_stride % 8)
     return fail(MTL_E_ALIGN, "KV cache must be 16-byte aligned");
+  if (flags & ~MTL_ATTN_KV_STABLE) return fail(MTL_E_INVALID, "mtl_attn_decode: unknown flags 0x%x", flags);
   size_t need = 0;
   mtl_attn_scratch_bytes(streams, n_heads, n_kv, splits, &need);
   if (scratch_bytes < need) return fail(MTL_E_SCRATCH, "attention scratch %zu < %zu", scratch_bytes, need);
@@ -281,6 +282,7 @@ int mtl_attn_decode(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_
   a.nh = n_heads;
   a.nkv = n_kv;
   a.splits = splits;
+  a.flags = (flags & MTL_ATTN_KV_STABLE) ? mtl::kAttnKvStable : 0u;
   a.out = out;
   a.counters = static_cast<int*>(scratch);
   a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + attn_counter_bytes(streams, n_kv));

@@ -2,6 +2,7 @@
 // error word are shared by every kernel without relocatable device code).
 #include "w4_gemv.cu"
 #include "step_kernels.cu"
+#include "attn_decode.cu"
 #include "sampling.cu"
 #include "capi.cu"
 #include "noalloc.cu"

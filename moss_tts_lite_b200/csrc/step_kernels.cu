@@ -71,306 +71,6 @@ __global__ void __launch_bounds__(256) embed_sum_kernel(const int64_t* __restric
   reinterpret_cast<uint4*>(out + (size_t)m * H)[c] = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// ----------------------------------------------------- decode attention
-// Fused _p_pre tail + _p_attn (fast.py:138-162, model.py:175-190) for one
-// layer and one decode position per stream:
-//   q/k head RMSNorm (model.py:34-40 over head_dim), RoPE
-//   bf16(bf16(x*cos) + bf16(rotate_half(x)*sin)) at position pos, K/V append
-//   at pos, then softmax(q k^T / sqrt(128)) v over positions [0, pos] for
-//   the n_rep query heads sharing each KV head (GQA).
-// Grid: (n_kv, splits, streams).  Split p covers a contiguous slice of
-// [0, pos]; each writes (max, sum, o[128]) per query head to scratch and the
-// last split to finish (atomic counter per KV head) merges them in split
-// order.  Probabilities exp(s - split_max) are rounded to bf16 before P.V
-// with fp32 accumulation (the rounding point of PyTorch's flash-style SDPA).
-struct AttnArgs {
-  const uint16_t* qkv;  // bf16 [streams, (nh + 2 nkv) * 128]
-  const uint16_t* q_norm_w;
-  const uint16_t* k_norm_w;
-  const uint16_t* rope_cos;  // bf16 [max_seq, 128]
-  const uint16_t* rope_sin;
-  uint16_t* k_cache;  // bf16 [streams][nkv][max_seq][128] for this layer (stream stride given)
-  uint16_t* v_cache;
-  long long cache_stream_stride;  // elements between streams (0 for one stream)
-  int max_seq;
-  const int64_t* pos;  // [streams] decode position of each stream
-  int nh, nkv, splits;
-  uint16_t* out;  // bf16 [streams, nh * 128]
-  float* partials;  // [streams][nkv][splits][n_rep][2 + 128]
-  int* counters;    // [streams][nkv]
-  float scale;
-};
-
-constexpr int kAttnThreads = 128;
-constexpr int kAttnMaxRep = 8;
-constexpr int kAttnTile = 32;       // positions per tile (4 warps x 8)
-constexpr int kAttnMinChunk = 32;   // positions per split at least
-
-__device__ __forceinline__ float rope_rot(const float* x, int d) {
-  // rotate_half (model.py:42-44): [-x2, x1]
-  return d < kHeadDim / 2 ? -x[d + kHeadDim / 2] : x[d - kHeadDim / 2];
-}
-
-// Registers of one tile: each lane holds 32 K dims of one position (scores)
-// and 4 V dims of 8 positions (P.V).
-struct KVTile {
-  uint4 k[4];
-  uint2 v[8];
-};
-
-__device__ __forceinline__ void load_tile(KVTile& t, const uint16_t* kc, const uint16_t* vc, int base, int hi,
-                                          int pos, int warp, int lane) {
-  const int ps = lane >> 2, dg = lane & 3;
-  const int sk = base + warp * 8 + ps;
-  if (sk < hi && sk != pos) {
-    const uint4* kp = reinterpret_cast<const uint4*>(kc + (size_t)sk * kHeadDim + dg * 32);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) t.k[j] = __ldg(kp + j);
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int sv = base + warp * 8 + i;
-    if (sv < hi && sv != pos) t.v[i] = __ldg(reinterpret_cast<const uint2*>(vc + (size_t)sv * kHeadDim) + lane);
-  }
-}
-
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
-  __shared__ float sq[kAttnMaxRep][kHeadDim];  // normed + roped q (bf16 values)
-  __shared__ float sk[kHeadDim], sv[kHeadDim];
-  __shared__ float sc[kAttnMaxRep][kAttnTile];
-  __shared__ float so[4][kAttnMaxRep][kHeadDim];  // per-warp P.V partials
-  __shared__ float mrun_s[kAttnMaxRep], alpha_s[kAttnMaxRep];
-  __shared__ int last_flag;
-  const int h = blockIdx.x, sp = blockIdx.y, st = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int rep = a.nh / a.nkv;
-  pdl_launch_dependents();
-  pdl_wait();
-  const int64_t pos64 = a.pos[st];
-  if (pos64 < 0 || pos64 >= a.max_seq) {
-    if (tid == 0) flag_error(kDevBadIndex);
-    return;
-  }
-  const int pos = (int)pos64, s1 = pos + 1;
-  const int chunk = max(kAttnMinChunk, (s1 + a.splits - 1) / a.splits);
-  const int lo = min(sp * chunk, s1), hi = min(lo + chunk, s1);
-  const int n = hi - lo;
-  uint16_t* kc = a.k_cache + st * a.cache_stream_stride + (size_t)h * a.max_seq * kHeadDim;
-  uint16_t* vc = a.v_cache + st * a.cache_stream_stride + (size_t)h * a.max_seq * kHeadDim;
-  float* part = a.partials + ((((size_t)st * a.nkv + h) * a.splits + sp) * rep) * (2 + kHeadDim);
-
-  if (n > 0) {
-    // first tile's loads go out before the q/k prologue (they do not depend on it)
-    KVTile cur;
-    load_tile(cur, kc, vc, lo, hi, pos, warp, lane);
-    const uint16_t* qkv = a.qkv + (size_t)st * (a.nh + 2 * a.nkv) * kHeadDim;
-    const uint16_t* cs = a.rope_cos + (size_t)pos * kHeadDim;
-    const uint16_t* sn = a.rope_sin + (size_t)pos * kHeadDim;
-    // --- q/k RMSNorm over head_dim + RoPE; one warp per head (rep q heads + k)
-    for (int r = warp; r <= rep; r += 4) {
-      const uint16_t* src = (r < rep) ? qkv + (size_t)(h * rep + r) * kHeadDim : qkv + (size_t)(a.nh + h) * kHeadDim;
-      const uint16_t* nw = (r < rep) ? a.q_norm_w : a.k_norm_w;
-      float x[4];
-      float ss = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        x[j] = bf16_bits_to_f32(src[lane + 32 * j]);
-        ss = fmaf(x[j], x[j], ss);
-      }
-      ss = warp_sum(ss);
-      const float rinv = rsqrtf(ss / (float)kHeadDim + 1e-6f);
-      float* dst = (r < rep) ? sq[r] : sk;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int d = lane + 32 * j;
-        dst[d] = round_bf16(bf16_bits_to_f32(nw[d]) * round_bf16(x[j] * rinv));
-      }
-      __syncwarp();
-      float y[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int d = lane + 32 * j;
-        const float t1 = round_bf16(dst[d] * bf16_bits_to_f32(cs[d]));
-        const float t2 = round_bf16(rope_rot(dst, d) * bf16_bits_to_f32(sn[d]));
-        y[j] = round_bf16(t1 + t2);
-      }
-      __syncwarp();
-#pragma unroll
-      for (int j = 0; j < 4; ++j) dst[lane + 32 * j] = y[j];
-    }
-    // v is used as is (fast.py:137,140)
-    sv[tid] = bf16_bits_to_f32(qkv[(size_t)(a.nh + a.nkv + h) * kHeadDim + tid]);
-    if (tid < kAttnMaxRep) mrun_s[tid] = -INFINITY;
-    __syncthreads();
-    // K/V append at pos (fast.py:145-146) by the split holding pos; every split
-    // uses sk / sv for position pos instead of re-reading the cache.
-    if (hi == s1) {
-      kc[(size_t)pos * kHeadDim + tid] = f32_to_bf16_bits(sk[tid]);
-      vc[(size_t)pos * kHeadDim + tid] = f32_to_bf16_bits(sv[tid]);
-    }
-
-    const int ps = lane >> 2, dg = lane & 3;
-    float o[kAttnMaxRep][4];
-#pragma unroll
-    for (int r = 0; r < kAttnMaxRep; ++r)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) o[r][c] = 0.f;
-    float lsum[kAttnMaxRep];
-#pragma unroll
-    for (int r = 0; r < kAttnMaxRep; ++r) lsum[r] = 0.f;
-
-    for (int base = lo; base < hi; base += kAttnTile) {
-      KVTile nxt;
-      if (base + kAttnTile < hi) load_tile(nxt, kc, vc, base + kAttnTile, hi, pos, warp, lane);
-      // --- scores of this tile: lane = (position ps, dim group dg)
-      const int s = base + warp * 8 + ps;
-      float kv[32];
-      if (s == pos) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) kv[j] = sk[dg * 32 + j];
-      } else {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t u[4] = {cur.k[j].x, cur.k[j].y, cur.k[j].z, cur.k[j].w};
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            kv[8 * j + 2 * q] = __uint_as_float(u[q] << 16);
-            kv[8 * j + 2 * q + 1] = __uint_as_float(u[q] & 0xFFFF0000u);
-          }
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < kAttnMaxRep; ++r) {
-        if (r < rep) {
-          float acc = 0.f;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc = fmaf(sq[r][dg * 32 + j], kv[j], acc);
-          acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-          acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-          if (dg == 0) sc[r][warp * 8 + ps] = (s < hi) ? acc * a.scale : -INFINITY;
-        }
-      }
-      __syncthreads();
-      // --- running max per head (warp r owns head r..), rescale factor
-      for (int r = warp; r < rep; r += 4) {
-        const float tmx = warp_max(sc[r][lane]);
-        if (lane == 0) {
-          const float mnew = fmaxf(mrun_s[r], tmx);
-          alpha_s[r] = (mrun_s[r] == -INFINITY) ? 0.f : expf(mrun_s[r] - mnew);
-          mrun_s[r] = mnew;
-        }
-      }
-      __syncthreads();
-      // --- probabilities exp(s - m) rounded to bf16 (flash-style), P.V over
-      //     this warp's 8 positions for 4 dims per lane
-      const int dbase = lane * 4;
-#pragma unroll
-      for (int r = 0; r < kAttnMaxRep; ++r) {
-        if (r < rep) {
-          const float al = alpha_s[r], m = mrun_s[r];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) o[r][c] *= al;
-          lsum[r] *= al;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int sp2 = base + warp * 8 + i;
-            if (sp2 < hi) {
-              const float pf = expf(sc[r][warp * 8 + i] - m);
-              lsum[r] += pf;
-              const float pb = round_bf16(pf);
-              float vv[4];
-              if (sp2 == pos) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c) vv[c] = sv[dbase + c];
-              } else {
-                vv[0] = __uint_as_float(cur.v[i].x << 16);
-                vv[1] = __uint_as_float(cur.v[i].x & 0xFFFF0000u);
-                vv[2] = __uint_as_float(cur.v[i].y << 16);
-                vv[3] = __uint_as_float(cur.v[i].y & 0xFFFF0000u);
-              }
-#pragma unroll
-              for (int c = 0; c < 4; ++c) o[r][c] = fmaf(pb, vv[c], o[r][c]);
-            }
-          }
-        }
-      }
-      __syncthreads();  // sc / alpha reuse
-      if (base + kAttnTile < hi) cur = nxt;
-    }
-    // --- combine the 4 warps' partials (same running max) and publish
-    for (int r = 0; r < rep; ++r) {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) so[warp][r][lane * 4 + c] = o[r][c];
-    }
-    float* lred = &sc[0][0];  // reuse: [4 warps][rep] row sums
-    for (int r = 0; r < rep; ++r) {
-      // lsum is identical across lanes of a warp (every lane saw the same p's)
-      if (lane == 0) lred[warp * kAttnMaxRep + r] = lsum[r];
-    }
-    __syncthreads();
-    for (int r = 0; r < rep; ++r) {
-      part[(size_t)r * (2 + kHeadDim) + 2 + tid] = so[0][r][tid] + so[1][r][tid] + so[2][r][tid] + so[3][r][tid];
-      if (tid == 0) {
-        part[(size_t)r * (2 + kHeadDim) + 0] = mrun_s[r];
-        part[(size_t)r * (2 + kHeadDim) + 1] = lred[0 * kAttnMaxRep + r] + lred[1 * kAttnMaxRep + r] +
-                                                lred[2 * kAttnMaxRep + r] + lred[3 * kAttnMaxRep + r];
-      }
-    }
-  } else if (tid < rep) {
-    part[(size_t)tid * (2 + kHeadDim) + 0] = -INFINITY;
-    part[(size_t)tid * (2 + kHeadDim) + 1] = 0.f;
-  }
-  // --- last split to finish merges all splits in order
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    int* ctr = a.counters + (size_t)st * a.nkv + h;
-    const int old = atomicAdd(ctr, 1);
-    last_flag = (old == a.splits - 1);
-    if (last_flag) {
-      __threadfence();
-      *ctr = 0;
-    }
-  }
-  __syncthreads();
-  if (!last_flag) return;
-  // --- merge: all (max, sum) pairs in one round of independent loads, the
-  //     rescale factors per split, then each thread's 128-dim slice with its
-  //     partial loads issued back to back.  Only splits that held positions.
-  __shared__ float mg_m[kAttnMaxRep * 64], mg_l[kAttnMaxRep * 64], mg_lsum[kAttnMaxRep];
-  const int nact = min(a.splits, (s1 + chunk - 1) / chunk);
-  const float* basep = a.partials + (((size_t)st * a.nkv + h) * a.splits * rep) * (2 + kHeadDim);
-  for (int i = tid; i < rep * nact; i += kAttnThreads) {
-    const int r = i / nact, j = i - r * nact;
-    const float* pj = basep + ((size_t)j * rep + r) * (2 + kHeadDim);
-    mg_m[r * 64 + j] = __ldcg(pj);
-    mg_l[r * 64 + j] = __ldcg(pj + 1);
-  }
-  __syncthreads();
-  for (int r = warp; r < rep; r += 4) {
-    float m = -INFINITY;
-    for (int j = lane; j < nact; j += 32) m = fmaxf(m, mg_m[r * 64 + j]);
-    m = warp_max(m);
-    float l = 0.f;
-    for (int j = lane; j < nact; j += 32) {
-      const float mj = mg_m[r * 64 + j];
-      const float f = (mj == -INFINITY) ? 0.f : expf(mj - m);
-      mg_m[r * 64 + j] = f;  // becomes the rescale factor of split j
-      l = fmaf(mg_l[r * 64 + j], f, l);
-    }
-    l = warp_sum(l);
-    if (lane == 0) mg_lsum[r] = l;
-  }
-  __syncthreads();
-  for (int r = 0; r < rep; ++r) {
-    float acc = 0.f;
-#pragma unroll 8
-    for (int j = 0; j < nact; ++j)
-      acc = fmaf(__ldcg(basep + ((size_t)j * rep + r) * (2 + kHeadDim) + 2 + tid), mg_m[r * 64 + j], acc);
-    a.out[(size_t)st * a.nh * kHeadDim + (size_t)(h * rep + r) * kHeadDim + tid] = f32_to_bf16_bits(acc / mg_lsum[r]);
-  }
-}
-
 // --------------------------------------------------------------- bf16 GEMV
 // y[m][n] = bf16(sum_k x[m][k] W[n][k]) for the lm heads (model.py:240-295,
 // fast.py:174-194), optionally with the final RMSNorm fused as prologue
@@ -705,12 +405,6 @@ cudaError_t launch_embed_sum(const int64_t* ids, int M, const uint16_t* emb_text
   const int total = M * (H / 8);
   cudaLaunchConfig_t cfg = pdl_cfg(dim3((total + 255) / 256), dim3(256), 0, s, attr, use_pdl);
   return cudaLaunchKernelEx(&cfg, embed_sum_kernel, ids, M, emb_text, text_vocab, emb_audio, H, out);
-}
-
-cudaError_t launch_attn_decode(const AttnArgs& a, int streams, cudaStream_t s, int use_pdl) {
-  cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.nkv, a.splits, streams), dim3(kAttnThreads), 0, s, attr, use_pdl);
-  return cudaLaunchKernelEx(&cfg, attn_decode_kernel, a);
 }
 
 cudaError_t launch_bf16_gemv(const Bf16GemvArgs& a, int num_sms, cudaStream_t s, int use_pdl) {

@@ -140,6 +140,9 @@ class _StepEngine:
         if self.emb_audio is None:   # reference MossTTSModel: stack its 32 tables once
             self.emb_audio = torch.stack(list(m.emb_ext), 0).contiguous()
         self.head_audio2d = m.head_audio.view(N_VQ * AUDIO_VOCAB, H)
+        # True while a step graph is captured: every replay follows the steps
+        # that wrote pos and the cache rows before it
+        self.kv_stable = False
 
     def backbone(self) -> None:
         m = self.m
@@ -149,7 +152,7 @@ class _StepEngine:
             L["qkv"](self.h, self.qkv, norm_weight=lyr["input_layernorm"])
             kernels.attn_decode(self.qkv, lyr["q_norm"], lyr["k_norm"], m.rope_cos, m.rope_sin,
                                 m.k_cache[li], m.v_cache[li], self.pos_dev, m.n_heads, m.n_kv_heads,
-                                self.splits, self.attn, self.attn_scratch)
+                                self.splits, self.attn, self.attn_scratch, kv_stable=self.kv_stable)
             L["o"](self.attn, self.h, residual=self.h)
             L["gu"](self.h, self.act, norm_weight=lyr["post_attention_layernorm"], swiglu=True)
             L["down"](self.act, self.h, residual=self.h)
@@ -308,11 +311,15 @@ class FastMossTTS:
         torch.cuda.synchronize()
         pool = torch.cuda.graph_pool_handle()
         self.graphs = []
-        for audio2 in (False, True):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, pool=pool, stream=self.capture_stream):
-                self._run_eager(audio2)
-            self.graphs.append(g)
+        self.engine.kv_stable = True
+        try:
+            for audio2 in (False, True):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, pool=pool, stream=self.capture_stream):
+                    self._run_eager(audio2)
+                self.graphs.append(g)
+        finally:
+            self.engine.kv_stable = False
         torch.cuda.synchronize()
 
     def capture_greedy_loop(self) -> torch.cuda.CUDAGraph:
@@ -327,8 +334,12 @@ class FastMossTTS:
             kernels.greedy_feed(self.la_static, self.two_static, self.ids_row, self.pos_dev, _GEN, _DELAY)
 
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=self.capture_stream):
-            body()
+        self.engine.kv_stable = True
+        try:
+            with torch.cuda.graph(g, stream=self.capture_stream):
+                body()
+        finally:
+            self.engine.kv_stable = False
         torch.cuda.synchronize()
         return g
 

@@ -46,12 +46,16 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, eps: float
 
 def attn_decode(qkv, q_norm_w, k_norm_w, rope_cos, rope_sin, k_cache_layer, v_cache_layer, pos_dev,
                 n_heads: int, n_kv: int, splits: int, out, scratch, streams: int = 1,
-                cache_stream_stride: int = 0) -> torch.Tensor:
+                cache_stream_stride: int = 0, kv_stable: bool = False) -> torch.Tensor:
+    """``kv_stable``: pos and cache rows [0, pos) are final before the
+    preceding kernel started (graph-captured steps), so the cache may be
+    streamed before the programmatic-dependent-launch wait."""
     max_seq = k_cache_layer.shape[-2]
     _lib.call("mtl_attn_decode", qkv.data_ptr(), q_norm_w.data_ptr(), k_norm_w.data_ptr(),
               rope_cos.data_ptr(), rope_sin.data_ptr(), k_cache_layer.data_ptr(), v_cache_layer.data_ptr(),
               ctypes.c_longlong(cache_stream_stride), max_seq, pos_dev.data_ptr(), streams, n_heads, n_kv,
-              k_cache_layer.shape[-1], splits, out.data_ptr(), scratch.data_ptr(), scratch.numel(), _s())
+              k_cache_layer.shape[-1], splits, _lib.MTL_ATTN_KV_STABLE if kv_stable else 0, out.data_ptr(),
+              scratch.data_ptr(), scratch.numel(), _s())
     return out
 
 

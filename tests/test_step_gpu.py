@@ -118,41 +118,56 @@ def test_rmsnorm_and_argmax():
     assert int(o1[0]) == 900
 
 
-@pytest.mark.parametrize("s1", [1, 7, 130, 641, 2000])
-def test_attention_decode_vs_oracle(s1):
+@pytest.mark.parametrize("s1,rep,streams,stable", [(1, 4, 1, False), (7, 4, 1, True), (64, 4, 1, False),
+                                                     (65, 8, 1, True), (130, 4, 1, False), (641, 4, 2, True),
+                                                     (2000, 4, 1, True), (4096, 2, 1, False), (3000, 8, 2, False)])
+def test_attention_decode_vs_oracle(s1, rep, streams, stable):
+    """Fused q/k-norm + RoPE + append + split-KV attention against the oracle,
+    at cache lengths around the 64-position tiles, GQA ratios 2-8, two
+    streams, with the cache rows past pos poisoned with NaN (masked rows must
+    contribute exactly nothing)."""
     dev = require_cuda()
     from moss_tts_lite_b200 import _lib, kernels
-    rng = np.random.default_rng(s1)
-    nh, nkv, D, max_seq = 8, 2, 128, 4096
+    rng = np.random.default_rng(s1 + rep)
+    nkv, D, max_seq = 2, 128, 4096
+    nh = nkv * rep
     pos = s1 - 1
-    kc = f32_to_bf16(rng.standard_normal((nkv, max_seq, D)).astype(np.float32))
-    vc = f32_to_bf16(rng.standard_normal((nkv, max_seq, D)).astype(np.float32))
-    qkv = f32_to_bf16((rng.standard_normal((1, (nh + 2 * nkv) * D)) * 2).astype(np.float32))
+    kc = f32_to_bf16(rng.standard_normal((streams, nkv, max_seq, D)).astype(np.float32))
+    vc = f32_to_bf16(rng.standard_normal((streams, nkv, max_seq, D)).astype(np.float32))
+    kc[:, :, s1:] = 0x7FC0   # NaN past the decoded position
+    vc[:, :, s1:] = 0x7FC0
+    qkv = f32_to_bf16((rng.standard_normal((streams, (nh + 2 * nkv) * D)) * 2).astype(np.float32))
     qn = f32_to_bf16((1 + 0.1 * rng.standard_normal(D)).astype(np.float32))
     kn = f32_to_bf16((1 + 0.1 * rng.standard_normal(D)).astype(np.float32))
     cos, sin = ost.rope_tables(max_seq, D)
     splits = 16
-    scratch = torch.zeros(_lib.attn_scratch_bytes(1, nh, nkv, splits), dtype=torch.uint8, device=dev)
+    scratch = torch.zeros(_lib.attn_scratch_bytes(streams, nh, nkv, splits), dtype=torch.uint8, device=dev)
     kct, vct = _t(kc, dev, torch.bfloat16), _t(vc, dev, torch.bfloat16)
-    out = torch.empty(1, nh * D, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(streams, nh * D, dtype=torch.bfloat16, device=dev)
     kernels.attn_decode(_t(qkv, dev, torch.bfloat16), _t(qn, dev, torch.bfloat16), _t(kn, dev, torch.bfloat16),
                         _t(cos, dev, torch.bfloat16), _t(sin, dev, torch.bfloat16), kct, vct,
-                        torch.tensor([pos], device=dev), nh, nkv, splits, out, scratch)
+                        torch.full((streams,), pos, device=dev), nh, nkv, splits, out, scratch, streams=streams,
+                        cache_stream_stride=nkv * max_seq * D, kv_stable=stable)
     torch.cuda.synchronize()
-    # oracle: norm + rope + append + attention
-    q = ost.apply_rope(ost.rms_norm(qkv[0, :nh * D].reshape(nh, D), qn), cos[pos], sin[pos])
-    k = ost.apply_rope(ost.rms_norm(qkv[0, nh * D:(nh + nkv) * D].reshape(nkv, D), kn), cos[pos], sin[pos])
-    v = qkv[0, (nh + nkv) * D:].reshape(nkv, D)
-    kc[:, pos], vc[:, pos] = k, v
-    assert np.array_equal(_bits(kct)[:, pos], k) and np.array_equal(_bits(vct)[:, pos], v)
-    ref = np.empty((nh, D))
-    for h in range(nh):
-        g = h // (nh // nkv)
-        ref[h] = ost.attend(bf16_to_f32(q[h:h + 1]).astype(np.float64), bf16_to_f32(kc[g, :s1]).astype(np.float64),
-                            bf16_to_f32(vc[g, :s1]).astype(np.float64), 1 / np.sqrt(D))[0]
-    y = bf16_to_f32(_bits(out)).reshape(nh, D)
-    # split-KV rounds exp(s - split max) instead of exp(s - row max): a few bf16 ulps
-    assert np.abs(y - ref).max() <= 2e-2 * max(1.0, np.abs(ref).max()), np.abs(y - ref).max()
+    y_all = bf16_to_f32(_bits(out)).reshape(streams, nh, D)
+    for st in range(streams):
+        # oracle: norm + rope + append + attention
+        q = ost.apply_rope(ost.rms_norm(qkv[st, :nh * D].reshape(nh, D), qn), cos[pos], sin[pos])
+        k = ost.apply_rope(ost.rms_norm(qkv[st, nh * D:(nh + nkv) * D].reshape(nkv, D), kn), cos[pos], sin[pos])
+        v = qkv[st, (nh + nkv) * D:].reshape(nkv, D)
+        kc[st, :, pos], vc[st, :, pos] = k, v
+        assert np.array_equal(_bits(kct)[st, :, pos], k) and np.array_equal(_bits(vct)[st, :, pos], v)
+        ref = np.empty((nh, D))
+        for h in range(nh):
+            g = h // rep
+            ref[h] = ost.attend(bf16_to_f32(q[h:h + 1]).astype(np.float64),
+                                bf16_to_f32(kc[st, g, :s1]).astype(np.float64),
+                                bf16_to_f32(vc[st, g, :s1]).astype(np.float64), 1 / np.sqrt(D))[0]
+        y = y_all[st]
+        assert np.isfinite(y).all()
+        # split-KV rounds exp(s - running max of its slice) instead of
+        # exp(s - row max) before P.V: a few bf16 ulps
+        assert np.abs(y - ref).max() <= 2e-2 * max(1.0, np.abs(ref).max()), (st, np.abs(y - ref).max())
     from moss_tts_lite_b200 import _lib as L
     assert L.device_status() == 0
 
