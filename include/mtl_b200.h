@@ -32,6 +32,12 @@ typedef struct CUstream_st* mtl_stream_t; /* == cudaStream_t */
 /* Parameter formats of a packed W4 weight. */
 #define MTL_FMT_REF 0  /* reference qsz: bf16 (scale, zero), w = (q-8)*scale+zero */
 #define MTL_FMT_GPTQ 1 /* AutoGPTQ: fp16 scale + 4-bit zero, w = (q-(z+off))*s   */
+#define MTL_FMT_TC 2   /* reference qsz in the tensor-core tile layout (128-row
+                          tiles, per-row (scale, zero)); mtl_w4a16_linear runs
+                          the tcgen05 kernel once per activation row.  N % 128
+                          == 0, group_size 32/64/128, K <= 16384; the SwiGLU
+                          epilogue expects gate and up rows interleaved one by
+                          one (row 2j = gate j, row 2j + 1 = up j) */
 
 /* Epilogues of mtl_w4a16_linear. */
 #define MTL_EPI_STORE 0    /* y = bf16(x W^T)                                   */
@@ -71,6 +77,12 @@ int mtl_w4_plan(int M, int K, int N, int group_size, int param_fmt, size_t* tile
  * and qsz bf16 [K/g, N, 2] = (scale, zero) (fast.py:94-96). */
 int mtl_w4_pack_ref(const uint8_t* q, const uint16_t* qsz, int K, int N, int group_size, void* tiles,
                     mtl_stream_t stream);
+
+/* The same reference weight (codes + qsz, as mtl_w4_pack_ref) packed into
+ * the tensor-core tile layout of MTL_FMT_TC (size from mtl_w4_plan with
+ * param_fmt = MTL_FMT_TC).  Same reference call sites as mtl_w4_pack_ref. */
+int mtl_w4_pack_tc(const uint8_t* q, const uint16_t* qsz, int K, int N, int group_size, void* tiles,
+                   mtl_stream_t stream);
 
 /* Pack an AutoGPTQ weight: qweight int32 [K/8, N] (LSB-first nibbles along
  * K), qzeros int32 [K/g, N/8] (LSB-first along N), scales fp16 [K/g, N].

@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(_HERE, "libmtl_b200.so")
 MTL_OK = 0
 MTL_FMT_REF = 0
 MTL_FMT_GPTQ = 1
+MTL_FMT_TC = 2
 MTL_EPI_STORE = 0
 MTL_EPI_RESIDUAL = 1
 MTL_EPI_SWIGLU = 2
@@ -36,6 +37,7 @@ SIGNATURES = {
     "mtl_device_status": (_c_int, [_c_u32_p, _c_int]),
     "mtl_w4_plan": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_size_p, _c_size_p]),
     "mtl_w4_pack_ref": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
+    "mtl_w4_pack_tc": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
     "mtl_w4_pack_gptq": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_int,
                                   _c_void_p, _c_void_p]),
     "mtl_w4_unpack_codes": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),

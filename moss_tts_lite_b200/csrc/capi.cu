@@ -33,6 +33,10 @@ cudaError_t w4_pack_gptq(const int32_t* qweight, const int32_t* qzeros, const ui
 cudaError_t w4_pack_ref(const uint8_t* q, const uint16_t* qsz, int K, int N, int g, uint8_t* tiles,
                         cudaStream_t s);
 cudaError_t w4_unpack_codes(const uint8_t* tiles, int K, int N, int g, int fmt, uint8_t* codes, cudaStream_t s);
+int w4_tc_plan(int K, int N, int g, int num_sms, TcPlan* out);
+cudaError_t w4_tc_launch(const TcArgs& a, cudaStream_t stream, int use_pdl);
+cudaError_t w4_tc_pack(const uint8_t* q, const uint16_t* qsz, int K, int N, int g, uint8_t* tiles, cudaStream_t s);
+cudaError_t w4_tc_unpack_codes(const uint8_t* tiles, int K, int N, int g, uint8_t* codes, cudaStream_t s);
 }  // namespace mtl
 
 namespace {
@@ -99,16 +103,46 @@ int get_plan(int M, int K, int N, int g, int fmt, mtl::W4Plan* out) {
   return 0;
 }
 
+int get_tc_plan(int K, int N, int g, mtl::TcPlan* out) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int>, mtl::TcPlan> cache;
+  const int sms = num_sms();
+  auto key = std::make_tuple(K, N, g, sms);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return 0;
+    }
+  }
+  mtl::TcPlan p;
+  int r = mtl::w4_tc_plan(K, N, g, sms, &p);
+  if (r != 0) return r;
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = p;
+  *out = p;
+  return 0;
+}
+
 int check_w4_shape(int K, int N, int g, int fmt) {
   if (!valid_group(g)) return fail(MTL_E_INVALID, "group_size %d not in {32,64,128,256}", g);
   if (K <= 0 || N <= 0) return fail(MTL_E_INVALID, "K=%d N=%d must be positive", K, N);
   if (K % g) return fail(MTL_E_INVALID, "K=%d is not a multiple of group_size %d", K, g);
+  if (fmt != MTL_FMT_REF && fmt != MTL_FMT_GPTQ && fmt != MTL_FMT_TC)
+    return fail(MTL_E_INVALID, "unknown param_fmt %d", fmt);
+  if (fmt == MTL_FMT_TC) {
+    if (N % mtl::kTcRows) return fail(MTL_E_INVALID, "N=%d is not a multiple of %d", N, mtl::kTcRows);
+    if (g == 256) return fail(MTL_E_UNSUPPORTED, "MTL_FMT_TC supports group_size 32/64/128");
+    if (K > mtl::kTcMaxK) return fail(MTL_E_UNSUPPORTED, "MTL_FMT_TC supports K <= %d", mtl::kTcMaxK);
+    return 0;
+  }
   if (N % mtl::kNT) return fail(MTL_E_INVALID, "N=%d is not a multiple of %d", N, mtl::kNT);
-  if (fmt != MTL_FMT_REF && fmt != MTL_FMT_GPTQ) return fail(MTL_E_INVALID, "unknown param_fmt %d", fmt);
   return 0;
 }
 
 size_t counters_bytes(int N) { return ((size_t)(N / mtl::kNT) * 4 + 255) / 256 * 256; }
+size_t tc_counters_bytes(int N) { return ((size_t)(N / mtl::kTcRows) * 4 + 255) / 256 * 256; }
 
 }  // namespace
 
@@ -137,6 +171,14 @@ int mtl_device_status(uint32_t* out, int clear) {
 int mtl_w4_plan(int M, int K, int N, int group_size, int param_fmt, size_t* tiles_bytes, size_t* scratch_bytes) {
   if (int r = check_w4_shape(K, N, group_size, param_fmt)) return r;
   if (M < 1) return fail(MTL_E_INVALID, "M=%d must be >= 1", M);
+  if (param_fmt == MTL_FMT_TC) {
+    mtl::TcPlan p;
+    if (get_tc_plan(K, N, group_size, &p))
+      return fail(MTL_E_UNSUPPORTED, "no tensor-core plan for K=%d N=%d g=%d", K, N, group_size);
+    if (tiles_bytes) *tiles_bytes = (size_t)p.T * p.tile_bytes;
+    if (scratch_bytes) *scratch_bytes = tc_counters_bytes(N) + p.partial_bytes;
+    return MTL_OK;
+  }
   const int mc = M < mtl::kW4MaxM ? M : mtl::kW4MaxM;
   mtl::W4Plan p;
   int r = get_plan(mc, K, N, group_size, param_fmt, &p);
@@ -155,6 +197,15 @@ int mtl_w4_pack_ref(const uint8_t* q, const uint16_t* qsz, int K, int N, int gro
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4_pack_ref");
 }
 
+int mtl_w4_pack_tc(const uint8_t* q, const uint16_t* qsz, int K, int N, int group_size, void* tiles,
+                   mtl_stream_t stream) {
+  if (int r = check_w4_shape(K, N, group_size, MTL_FMT_TC)) return r;
+  if (!q || !qsz || !tiles) return fail(MTL_E_INVALID, "mtl_w4_pack_tc: NULL pointer");
+  if (!aligned(tiles, 16)) return fail(MTL_E_ALIGN, "tiles must be 16-byte aligned");
+  cudaError_t e = mtl::w4_tc_pack(q, qsz, K, N, group_size, static_cast<uint8_t*>(tiles), stream);
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4_pack_tc");
+}
+
 int mtl_w4_pack_gptq(const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales, const int32_t* perm,
                      int K, int N, int group_size, void* tiles, mtl_stream_t stream) {
   if (int r = check_w4_shape(K, N, group_size, MTL_FMT_GPTQ)) return r;
@@ -169,6 +220,10 @@ int mtl_w4_unpack_codes(const void* tiles, int K, int N, int group_size, int par
                         mtl_stream_t stream) {
   if (int r = check_w4_shape(K, N, group_size, param_fmt)) return r;
   if (!tiles || !codes) return fail(MTL_E_INVALID, "mtl_w4_unpack_codes: NULL pointer");
+  if (param_fmt == MTL_FMT_TC) {
+    cudaError_t e = mtl::w4_tc_unpack_codes(static_cast<const uint8_t*>(tiles), K, N, group_size, codes, stream);
+    return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4_unpack_codes");
+  }
   cudaError_t e = mtl::w4_unpack_codes(static_cast<const uint8_t*>(tiles), K, N, group_size, param_fmt, codes,
                                        stream);
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4_unpack_codes");
@@ -194,6 +249,32 @@ int mtl_w4a16_linear(const uint16_t* x, int ldx, int M, int K, int N, int group_
   size_t need = 0;
   if (int r = mtl_w4_plan(M, K, N, group_size, param_fmt, nullptr, &need)) return r;
   if (scratch_bytes < need) return fail(MTL_E_SCRATCH, "scratch %zu < required %zu bytes", scratch_bytes, need);
+
+  if (param_fmt == MTL_FMT_TC) {
+    // tensor-core kernel: one launch per activation row (batch-1 decode path)
+    if (zero_offset != 0 || k_perm) return fail(MTL_E_UNSUPPORTED, "MTL_FMT_TC has no zero offset or k_perm");
+    if (!aligned(x, 16) || (ldx % 8) || (norm_w && !aligned(norm_w, 16)))
+      return fail(MTL_E_ALIGN, "MTL_FMT_TC needs 16-byte aligned x rows and norm_w");
+    mtl::TcArgs a{};
+    if (get_tc_plan(K, N, group_size, &a.p)) return fail(MTL_E_UNSUPPORTED, "no tensor-core plan");
+    a.K = K;
+    a.N = N;
+    a.g = group_size;
+    a.tiles = static_cast<const uint8_t*>(tiles);
+    a.norm_w = norm_w;
+    a.norm_eps = norm_eps;
+    a.epi = epilogue;
+    a.counters = static_cast<int*>(scratch);
+    a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + tc_counters_bytes(N));
+    for (int m = 0; m < M; ++m) {
+      a.x = x + (size_t)m * ldx;
+      a.residual = residual ? residual + (size_t)m * N : nullptr;
+      a.y = y + (size_t)m * ldy;
+      cudaError_t e = mtl::w4_tc_launch(a, stream, use_pdl() ? 1 : 0);
+      if (e != cudaSuccess) return cuda_fail(e, "mtl_w4a16_linear (tensor cores) launch");
+    }
+    return MTL_OK;
+  }
 
   for (int m0 = 0; m0 < M; m0 += mtl::kW4MaxM) {
     const int mc = (M - m0) < mtl::kW4MaxM ? (M - m0) : mtl::kW4MaxM;

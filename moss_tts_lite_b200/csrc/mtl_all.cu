@@ -1,6 +1,7 @@
 // Single translation unit for libmtl_b200.so (device globals such as the
 // error word are shared by every kernel without relocatable device code).
 #include "w4_gemv.cu"
+#include "w4_tc.cu"
 #include "step_kernels.cu"
 #include "attn_decode.cu"
 #include "sampling.cu"

@@ -23,7 +23,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from . import kernels
+from . import _lib, kernels
 from .generate import GenResult
 from .model import (AUDIO_DELAY_SLOT_TOKEN_ID, AUDIO_END_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_PAD_CODE,
                     AUDIO_START_TOKEN_ID, AUDIO_VOCAB, IM_END_TOKEN_ID, LIN_NAMES, N_VQ, PAD_TOKEN_ID,
@@ -32,16 +32,17 @@ from .quant import W4Weight
 
 _INT64_MAX = 9223372036854775807
 _LIN_NAMES = LIN_NAMES
-_FUSE_BLOCK = 32  # gate/up interleave granularity of the SwiGLU epilogue
+_FUSE_BLOCK = 32  # gate/up interleave granularity of the register-MMA tiles' SwiGLU epilogue
 
 
 # ------------------------------------------------------------------ linears
 class _W4Lin:
     """A packed W4 linear (possibly fused q|k|v or gate|up)."""
 
-    def __init__(self, w: W4Weight):
+    def __init__(self, w: W4Weight, fuse_block: int = _FUSE_BLOCK):
         self.w = w
         self.N = w.N
+        self.fuse_block = fuse_block   # gate/up interleave of a fused SwiGLU pair
 
     def __call__(self, x, out, *, norm_weight=None, residual=None, swiglu=False):
         return self.w.linear(x, out=out, norm_weight=norm_weight, norm_eps=RMS_EPS,
@@ -93,17 +94,26 @@ def bf16_linears(m) -> list:
     return lins
 
 
-def w4_from_codes(recs: dict, group_size: int) -> dict:
+def w4_from_codes(recs: dict, group_size: int, fmt: int | None = None) -> dict:
     """{name: (q uint8 [N, K], qsz bf16 [K/g, N, 2])} of one layer -> fused
-    packed W4 linears (q|k|v concatenated, gate|up interleaved)."""
+    packed W4 linears (q|k|v concatenated, gate|up interleaved).  The
+    register-MMA tiles (MTL_FMT_REF) are the decode default; ``fmt =
+    MTL_FMT_TC`` selects the tensor-core tiles where they cover every shape
+    of the layer (measured slower at batch 1 on B200: the A operand's TMEM
+    traffic, 4 bytes per weight, bounds it below the register-MMA kernel)."""
     q = torch.cat([recs["q"][0], recs["k"][0], recs["v"][0]], 0)
     qsz = torch.cat([recs["q"][1], recs["k"][1], recs["v"][1]], 1)
-    out = {"qkv": _W4Lin(W4Weight.from_ref(q, qsz, group_size))}
-    out["o"] = _W4Lin(W4Weight.from_ref(recs["o"][0], recs["o"][1], group_size))
-    gq = _interleave_rows(recs["gate"][0], recs["up"][0], _FUSE_BLOCK)
-    gs = _interleave_cols(recs["gate"][1], recs["up"][1], _FUSE_BLOCK)
-    out["gu"] = _W4Lin(W4Weight.from_ref(gq, gs, group_size))
-    out["down"] = _W4Lin(W4Weight.from_ref(recs["down"][0], recs["down"][1], group_size))
+    shapes = [tuple(q.shape), tuple(recs["o"][0].shape), (2 * recs["gate"][0].shape[0], recs["gate"][0].shape[1]),
+              tuple(recs["down"][0].shape)]
+    tc = fmt == _lib.MTL_FMT_TC and all(W4Weight.tc_supported(k, n, group_size) for n, k in shapes)
+    fmt = _lib.MTL_FMT_TC if tc else _lib.MTL_FMT_REF
+    blk = 1 if tc else _FUSE_BLOCK
+    out = {"qkv": _W4Lin(W4Weight.from_ref(q, qsz, group_size, fmt=fmt))}
+    out["o"] = _W4Lin(W4Weight.from_ref(recs["o"][0], recs["o"][1], group_size, fmt=fmt))
+    gq = _interleave_rows(recs["gate"][0], recs["up"][0], blk)
+    gs = _interleave_cols(recs["gate"][1], recs["up"][1], blk)
+    out["gu"] = _W4Lin(W4Weight.from_ref(gq, gs, group_size, fmt=fmt), fuse_block=blk)
+    out["down"] = _W4Lin(W4Weight.from_ref(recs["down"][0], recs["down"][1], group_size, fmt=fmt))
     return out
 
 
@@ -268,7 +278,8 @@ class FastMossTTS:
             out = torch.empty(x2.shape[0], lin.N, dtype=torch.bfloat16, device=x.device)
             lin(x2, out)
             if isinstance(lin, _W4Lin):
-                y = out.view(x2.shape[0], -1, 2, _FUSE_BLOCK)[:, :, 0 if name == "gate" else 1].reshape(x2.shape[0], -1)
+                fb = lin.fuse_block
+                y = out.view(x2.shape[0], -1, 2, fb)[:, :, 0 if name == "gate" else 1].reshape(x2.shape[0], -1)
             else:
                 y = out[:, 0::2] if name == "gate" else out[:, 1::2]
         else:

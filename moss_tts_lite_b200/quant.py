@@ -51,8 +51,13 @@ class W4Weight:
         return torch.empty(tb, dtype=torch.uint8, device=device)
 
     @classmethod
-    def from_ref(cls, q: torch.Tensor, qsz: torch.Tensor, group_size: int) -> "W4Weight":
-        """Codes uint8 [N, K] (0..15) + qsz bf16 [K/g, N, 2] on a CUDA device."""
+    def from_ref(cls, q: torch.Tensor, qsz: torch.Tensor, group_size: int,
+                 fmt: int | None = None) -> "W4Weight":
+        """Codes uint8 [N, K] (0..15) + qsz bf16 [K/g, N, 2] on a CUDA device.
+        ``fmt``: MTL_FMT_REF (register-MMA tiles, any batch) or MTL_FMT_TC
+        (tensor-core tiles, the batch-1 decode layout; gate/up of a SwiGLU
+        pair interleaved row by row)."""
+        fmt = _lib.MTL_FMT_REF if fmt is None else int(fmt)
         if group_size not in _GROUPS:
             raise ValueError("w4_group_size must be 32/64/128/256")
         N, K = q.shape
@@ -60,10 +65,15 @@ class W4Weight:
             raise ValueError(f"qsz shape {tuple(qsz.shape)} != {(K // group_size, N, 2)}")
         q = q.to(torch.uint8).contiguous()
         qsz = qsz.to(torch.bfloat16).contiguous()
-        tiles = cls.alloc_tiles(K, N, group_size, _lib.MTL_FMT_REF, q.device)
-        _lib.call("mtl_w4_pack_ref", q.data_ptr(), qsz.data_ptr(), K, N, group_size,
-                  tiles.data_ptr(), _stream())
-        return cls(tiles, K, N, group_size, _lib.MTL_FMT_REF)
+        tiles = cls.alloc_tiles(K, N, group_size, fmt, q.device)
+        fn = "mtl_w4_pack_tc" if fmt == _lib.MTL_FMT_TC else "mtl_w4_pack_ref"
+        _lib.call(fn, q.data_ptr(), qsz.data_ptr(), K, N, group_size, tiles.data_ptr(), _stream())
+        return cls(tiles, K, N, group_size, fmt)
+
+    @staticmethod
+    def tc_supported(K: int, N: int, group_size: int) -> bool:
+        """Whether the tensor-core tile layout (MTL_FMT_TC) covers this shape."""
+        return N % 128 == 0 and group_size in (32, 64, 128) and K % group_size == 0 and K <= 16384
 
     def unpack_codes(self) -> torch.Tensor:
         """uint8 [N, K] codes in packed row order (bit-exact inverse of packing)."""
