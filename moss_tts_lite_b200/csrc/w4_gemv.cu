@@ -41,7 +41,8 @@ __host__ __device__ __forceinline__ int cta_of_tile(long long t, int G, int T) {
 
 __host__ __device__ __forceinline__ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-constexpr int kMiscWords = 256;  // [0,64) reductions, [64,72) 1/rms, [80] bail, [96,96+nblk) last flags
+constexpr int kMiscWords = 320;  // [0,128) reductions, [128,136) 1/rms, [144] bail, [160,160+nblk) last flags
+constexpr int kW4CThreads = kW4Warps * 32;  // consumer threads
 
 struct SmemLayout {
   size_t bar, ring, xs, bsum, gsum, part, fin, misc, total;
@@ -73,7 +74,7 @@ __host__ __device__ inline SmemLayout smem_layout(const W4Plan& p, int g, int M)
   return L;
 }
 
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kW4CThreads) : "memory"); }
 
 // m16n8k16 bf16 MMA with fp32 accumulate (register-sourced operands).
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
     }
     fence_mbar_init();
   }
-  if (threadIdx.x < kMiscWords - 80) imisc[80 + threadIdx.x] = 0;
+  if (threadIdx.x < kMiscWords - 144) imisc[144 + threadIdx.x] = 0;
   __syncthreads();
   pdl_launch_dependents();
 
@@ -150,13 +151,49 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
   }
 
   // -------------------------------------------------------------- consumers
-  const int tid = threadIdx.x;  // 0..255
-  pdl_wait();
-
+  const int tid = threadIdx.x;  // consumer thread 0..kW4CThreads-1
   const int ng = min(KT, nt);   // groups touched: cyclic interval [gbeg, gbeg + ng)
   const int gbeg = t0 % KT;
   const int nb16 = g / 16;
   float* red = misc;
+  const int njobs = ng * M * nb16;  // staging jobs: 16 values of one row of one group
+  auto job_k0 = [&](int job, int& slot, int& m, int& b) {
+    slot = job / (M * nb16);
+    const int rem = job - slot * (M * nb16);
+    m = rem / nb16;
+    b = rem - m * nb16;
+    return ((gbeg + slot) % KT) * g + b * 16;
+  };
+  // The first two staging jobs of this thread keep their inputs in
+  // registers: the norm weight (a layer constant) is loaded before the
+  // wait, x right after it together with the statistics loads.
+  uint4 nwc[2][2], xc[2][2];
+  if (a.xvec) {
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      const int job = tid + kW4CThreads * jj;
+      if (job < njobs && a.norm_w) {
+        int sl, m, b;
+        const int k0 = job_k0(job, sl, m, b);
+        nwc[jj][0] = __ldg(reinterpret_cast<const uint4*>(a.norm_w + k0));
+        nwc[jj][1] = __ldg(reinterpret_cast<const uint4*>(a.norm_w + k0 + 8));
+      }
+    }
+  }
+  pdl_wait();
+  if (a.xvec) {
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      const int job = tid + kW4CThreads * jj;
+      if (job < njobs) {
+        int sl, m, b;
+        const int k0 = job_k0(job, sl, m, b);
+        const uint16_t* xr = a.x + (size_t)m * a.ldx;
+        xc[jj][0] = __ldg(reinterpret_cast<const uint4*>(xr + k0));
+        xc[jj][1] = __ldg(reinterpret_cast<const uint4*>(xr + k0 + 8));
+      }
+    }
+  }
 
   // (a) RMSNorm statistics over the full row (permutation-invariant).
   if (a.norm_w) {
@@ -164,7 +201,7 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
       float ss = 0.f;
       const uint16_t* xr = a.x + (size_t)m * a.ldx;
       if (a.xvec) {
-        for (int c = tid; c < a.K / 8; c += 256) {
+        for (int c = tid; c < a.K / 8; c += kW4CThreads) {
           const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr) + c);
           const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -175,7 +212,7 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
           }
         }
       } else {
-        for (int k = tid; k < a.K; k += 256) {
+        for (int k = tid; k < a.K; k += kW4CThreads) {
           const float h = bf16_bits_to_f32(xr[k]);
           ss = fmaf(h, h, ss);
         }
@@ -187,7 +224,7 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
     if (tid < M) {
       float ss = 0.f;
       for (int w = 0; w < kW4Warps; ++w) ss += red[w * kW4MaxM + tid];
-      misc[64 + tid] = rsqrtf(ss / (float)a.K + a.norm_eps);
+      misc[128 + tid] = rsqrtf(ss / (float)a.K + a.norm_eps);
     }
     consumer_sync();
   }
@@ -196,20 +233,28 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
   //     16-block lane t reads [2t, 2t+1, 2t+8, 2t+9] at positions 4t..4t+3,
   //     i.e. 32-bit words [w0, w4, w1, w5, w2, w6, w3, w7] of the input.
   //     The per-16-block sums feed the bias / offset terms.
-  for (int job = tid; job < ng * M * nb16; job += 256) {
-    const int slot = job / (M * nb16);
-    const int rem = job - slot * (M * nb16);
-    const int m = rem / nb16, b = rem - m * nb16;
-    const int k0 = ((gbeg + slot) % KT) * g + b * 16;
+  auto stage_job = [&](int job, bool cached, const uint4 (&xcj)[2], const uint4 (&nwj)[2]) {
+    int slot, m, b;
+    const int k0 = job_k0(job, slot, m, b);
     const uint16_t* xr = a.x + (size_t)m * a.ldx;
     uint32_t u[8], nw[8];
     if (a.xvec) {
-      const uint4 v0 = __ldg(reinterpret_cast<const uint4*>(xr + k0));
-      const uint4 v1 = __ldg(reinterpret_cast<const uint4*>(xr + k0 + 8));
+      uint4 v0, v1, n0, n1;
+      if (cached) {
+        v0 = xcj[0];
+        v1 = xcj[1];
+        n0 = nwj[0];
+        n1 = nwj[1];
+      } else {
+        v0 = __ldg(reinterpret_cast<const uint4*>(xr + k0));
+        v1 = __ldg(reinterpret_cast<const uint4*>(xr + k0 + 8));
+        if (a.norm_w) {
+          n0 = __ldg(reinterpret_cast<const uint4*>(a.norm_w + k0));
+          n1 = __ldg(reinterpret_cast<const uint4*>(a.norm_w + k0 + 8));
+        }
+      }
       u[0] = v0.x; u[1] = v0.y; u[2] = v0.z; u[3] = v0.w; u[4] = v1.x; u[5] = v1.y; u[6] = v1.z; u[7] = v1.w;
       if (a.norm_w) {
-        const uint4 n0 = __ldg(reinterpret_cast<const uint4*>(a.norm_w + k0));
-        const uint4 n1 = __ldg(reinterpret_cast<const uint4*>(a.norm_w + k0 + 8));
         nw[0] = n0.x; nw[1] = n0.y; nw[2] = n0.z; nw[3] = n0.w; nw[4] = n1.x; nw[5] = n1.y; nw[6] = n1.z; nw[7] = n1.w;
       }
     } else {
@@ -223,7 +268,7 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
     }
     float bs = 0.f;
     if (a.norm_w) {
-      const float rinv = misc[64 + m];
+      const float rinv = misc[128 + m];
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         // model.py:34-40: bf16(h * rsqrt(var + eps)), then bf16(weight * that)
@@ -239,10 +284,13 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
     *reinterpret_cast<uint4*>(dst) = make_uint4(u[0], u[4], u[1], u[5]);
     *reinterpret_cast<uint4*>(dst + 8) = make_uint4(u[2], u[6], u[3], u[7]);
     bsum[(slot * M + m) * nb16 + b] = bs;
-  }
-  for (int i = tid; i < p.nblk_max * kW4Warps * kNT * M; i += 256) part[i] = 0.f;
+  };
+  if (tid < njobs) stage_job(tid, a.xvec != 0, xc[0], nwc[0]);
+  if (tid + kW4CThreads < njobs) stage_job(tid + kW4CThreads, a.xvec != 0, xc[1], nwc[1]);
+  for (int job = tid + 2 * kW4CThreads; job < njobs; job += kW4CThreads) stage_job(job, false, xc[0], nwc[0]);
+  for (int i = tid; i < p.nblk_max * kW4Warps * kNT * M; i += kW4CThreads) part[i] = 0.f;
   consumer_sync();
-  for (int job = tid; job < ng * M; job += 256) {
+  for (int job = tid; job < ng * M; job += kW4CThreads) {
     float s = 0.f;
     for (int b = 0; b < nb16; ++b) s += bsum[job * nb16 + b];
     gsum[job] = s;
@@ -270,9 +318,15 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
       }
   };
 
+  int nb = (t0 + warp) / KT;
+  int G = (t0 + warp) - nb * KT;
+  int slot = (G - gbeg + KT) % KT;
+  // ring position of this warp's tile, advanced incrementally (tps is a power of two)
+  int ltps = 0;
+  while ((1 << ltps) < tps) ++ltps;
+  const int dst = kW4Warps >> ltps;  // stages between two tiles of this warp
+  int s = (warp >> ltps) % S, q = (warp >> ltps) / S;
   for (int i = warp; i < nt; i += kW4Warps) {
-    const int t = t0 + i;
-    const int nb = t / KT, G = t - (t / KT) * KT;
     if (nb != cur) {
       if (cur >= 0) flush(cur);
       cur = nb;
@@ -281,36 +335,44 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
 #pragma unroll
         for (int e = 0; e < 4; ++e) yacc[j][e] = 0.f;
     }
-    const int st = i / tps, s = st % S;
-    if (!mbar_wait(&full[s], (st / S) & 1)) {
+    if (!mbar_wait(&full[s], q & 1)) {
       bail = true;
       break;
     }
-    const uint8_t* tile = ring + (size_t)s * stage_bytes + (size_t)(i % tps) * p.tile_bytes;
+    const uint8_t* tile = ring + (size_t)s * stage_bytes + (size_t)(i & (tps - 1)) * p.tile_bytes;
     const uint4* wt = reinterpret_cast<const uint4*>(tile);
-    const int slot = (G - gbeg + KT) % KT;
-    const uint16_t* xg = xs + ((size_t)slot * M + mrow) * g;
-    float d[4][4];
+    const uint16_t* xg = xs + ((size_t)slot * M + mrow) * g + 4 * tq;
+    // even and odd k16-steps accumulate separately: eight independent MMA
+    // chains per warp instead of four
+    float d[4][4], d2[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) d[j][e] = 0.f;
-#pragma unroll 4
-    for (int ks = 0; ks < KS; ++ks) {
+      for (int e = 0; e < 4; ++e) d[j][e] = d2[j][e] = 0.f;
+#pragma unroll 2
+    for (int ks = 0; ks < KS; ks += 2) {
       const uint4 wv = wt[ks * 32 + lane];
-      const uint2 bx = *reinterpret_cast<const uint2*>(xg + ks * 16 + 4 * tq);
+      const uint4 wv2 = wt[(ks + 1) * 32 + lane];
+      const uint2 bx = *reinterpret_cast<const uint2*>(xg + ks * 16);
+      const uint2 bx2 = *reinterpret_cast<const uint2*>(xg + (ks + 1) * 16);
       const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
+      const uint32_t wr2[4] = {wv2.x, wv2.y, wv2.z, wv2.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint32_t w = wr[j];
-        const uint32_t a0 = lop3_and_or(w, 0x000F000Fu, 0x43004300u);
-        const uint32_t a1 = lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u);
-        const uint32_t a2 = lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u);
-        const uint32_t a3 = lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u);
-        mma_bf16_16816(d[j], a0, a1, a2, a3, bx.x, bx.y);
+        const uint32_t w = wr[j], v = wr2[j];
+        mma_bf16_16816(d[j], lop3_and_or(w, 0x000F000Fu, 0x43004300u), lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u),
+                       lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u), lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u),
+                       bx.x, bx.y);
+        mma_bf16_16816(d2[j], lop3_and_or(v, 0x000F000Fu, 0x43004300u), lop3_and_or(v >> 4, 0x000F000Fu, 0x43004300u),
+                       lop3_and_or(v >> 8, 0x000F000Fu, 0x43004300u), lop3_and_or(v >> 12, 0x000F000Fu, 0x43004300u),
+                       bx2.x, bx2.y);
       }
     }
-    // group affine: D = sum x (128 + q)  =>  y += A (D - 128 Sx) + B Sx
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) d[j][e] += d2[j][e];
+    // group affine: D = sum x (128 + q)  =>  y += A (D - 128 Sx) + B Sx = A D + C Sx
     const float sx0 = gsum[slot * M + min(2 * tq, M - 1)];
     const float sx1 = gsum[slot * M + min(2 * tq + 1, M - 1)];
     const uint8_t* prm = tile + kNT * g / 2;
@@ -319,35 +381,56 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
 #pragma unroll
       for (int hr = 0; hr < 2; ++hr) {
         const int col = 16 * j + gr + 8 * hr;
-        float A, B;
+        float A, C;
         if (FMT == kFmtRef) {
-          // gptq.py:87-97: w = (q - 8) * scale + zero = q * scale + (zero - 8 scale)
+          // gptq.py:87-97: w = (q - 8) scale + zero, so C = B - 128 A = zero - 136 scale
           const uint32_t pw = reinterpret_cast<const uint32_t*>(prm)[col];
-          A = bf16_bits_to_f32((uint16_t)(pw & 0xFFFFu));
-          B = fmaf(-8.f, A, bf16_bits_to_f32((uint16_t)(pw >> 16)));
+          A = __uint_as_float(pw * 65536u);
+          C = fmaf(-136.f, A, __uint_as_float(pw & 0xFFFF0000u));
         } else {
-          // w = (q - (z + zero_offset)) * s
+          // w = (q - (z + zero_offset)) s, so C = -(z + zero_offset + 128) s
           A = __half2float(reinterpret_cast<const __half*>(prm)[col]);
           const uint32_t zw = reinterpret_cast<const uint32_t*>(prm + 128)[col >> 3];
           const int z = (int)((zw >> (4 * (col & 7))) & 0xFu) + a.zero_offset;
-          B = -(float)z * A;
+          C = -(float)(z + 128) * A;
         }
-        yacc[j][2 * hr + 0] += fmaf(A, fmaf(-128.f, sx0, d[j][2 * hr + 0]), B * sx0);
-        yacc[j][2 * hr + 1] += fmaf(A, fmaf(-128.f, sx1, d[j][2 * hr + 1]), B * sx1);
+        yacc[j][2 * hr + 0] = fmaf(A, d[j][2 * hr + 0], fmaf(C, sx0, yacc[j][2 * hr + 0]));
+        yacc[j][2 * hr + 1] = fmaf(A, d[j][2 * hr + 1], fmaf(C, sx1, yacc[j][2 * hr + 1]));
       }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+    // next tile of this warp: kW4Warps further along
+    s += dst;
+    while (s >= S) {
+      s -= S;
+      ++q;
+    }
+    G += kW4Warps;
+    slot += kW4Warps;
+    while (G >= KT) {
+      G -= KT;
+      ++nb;
+    }
+    while (slot >= KT) slot -= KT;
   }
   if (cur >= 0 && !bail) flush(cur);
-  if (bail) imisc[80] = 1;
+  if (bail) imisc[144] = 1;
   consumer_sync();
-  if (imisc[80] == 1) return;
+  if (imisc[144] == 1) return;
 
   // ------------------------------------- CTA reduce + split-K fixup (all blocks at once)
   const int blk_last = (t1 - 1) / KT;
   const int nblk = blk_last - blk_first + 1;
   const int per = kNT * M;
-  for (int i = tid; i < nblk * per; i += 256) {
+  // the residual does not depend on the split-K partials: load it now
+  float rpf[4] = {0.f, 0.f, 0.f, 0.f};
+  if (a.epi == kEpiResidual && tid < per) {
+    const int col = tid / M, m = tid - (tid / M) * M;
+#pragma unroll
+    for (int bl = 0; bl < 4; ++bl)
+      if (bl < nblk) rpf[bl] = bf16_bits_to_f32(a.residual[(size_t)m * a.ldr + (blk_first + bl) * kNT + col]);
+  }
+  for (int i = tid; i < nblk * per; i += kW4CThreads) {
     const int bl = i / per, r = i - bl * per;
     float v = 0.f;
     for (int w = 0; w < kW4Warps; ++w) v += part[((size_t)bl * kW4Warps + w) * per + r];
@@ -360,7 +443,7 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
     any_partial |= !((blk * KT >= t0) && ((blk + 1) * KT <= t1));
   }
   if (any_partial) {
-    for (int i = tid; i < nblk * per; i += 256) {
+    for (int i = tid; i < nblk * per; i += kW4CThreads) {
       const int bl = i / per, r = i - bl * per;
       const int blk = blk_first + bl;
       if ((blk * KT >= t0) && ((blk + 1) * KT <= t1)) continue;
@@ -373,19 +456,20 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
       if (!((blk * KT >= t0) && ((blk + 1) * KT <= t1))) {
         const int c_lo = cta_of_tile((long long)blk * KT, p.G, p.T);
         const int c_hi = cta_of_tile((long long)(blk + 1) * KT - 1, p.G, p.T);
-        __threadfence();  // release this CTA's partials (cumulative over the barrier)
-        const int old = atomicAdd(&a.counters[blk], 1);
+        // release this CTA's partials (ordered before by the barrier) and,
+        // for the last contributor, acquire the others'
+        int old;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + blk) : "memory");
         if (old == c_hi - c_lo) {
-          __threadfence();  // acquire the other contributors' partials
-          imisc[96 + tid] = 1;
+          imisc[160 + tid] = 1;
           a.counters[blk] = 0;  // re-arm for the next launch
         }
       }
     }
     consumer_sync();
-    for (int i = tid; i < nblk * per; i += 256) {
+    for (int i = tid; i < nblk * per; i += kW4CThreads) {
       const int bl = i / per, r = i - bl * per;
-      if (!imisc[96 + bl]) continue;
+      if (!imisc[160 + bl]) continue;
       const int blk = blk_first + bl;
       const int c_lo = cta_of_tile((long long)blk * KT, p.G, p.T);
       const int c_hi = cta_of_tile((long long)(blk + 1) * KT - 1, p.G, p.T);
@@ -400,10 +484,10 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
   for (int bl = 0; bl < nblk; ++bl) {
     const int blk = blk_first + bl;
     const bool complete = (blk * KT >= t0) && ((blk + 1) * KT <= t1);
-    if (!complete && !imisc[96 + bl]) continue;
+    if (!complete && !imisc[160 + bl]) continue;
     const float* f = fin + (size_t)bl * per;
     if (a.epi == kEpiSwiGLU) {
-      for (int i = tid; i < (kNT / 2) * M; i += 256) {
+      for (int i = tid; i < (kNT / 2) * M; i += kW4CThreads) {
         const int col = i / M, m = i - (i / M) * M;
         // fast.py:170-171: bf16(silu(gate)) * up, each op rounded to bf16
         const float gt = round_bf16(f[col * M + m]);
@@ -412,13 +496,18 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
         a.y[(size_t)m * a.ldy + blk * (kNT / 2) + col] = f32_to_bf16_bits(sg * up);
       }
     } else {
-      for (int i = tid; i < per; i += 256) {
+      for (int i = tid; i < per; i += kW4CThreads) {
         const int col = i / M, m = i - (i / M) * M;
         const int n = blk * kNT + col;
         float v = f[i];
         if (a.epi == kEpiResidual) {
           // fast.py:168 / :170: residual + bf16(linear(...)), rounded to bf16
-          v = bf16_bits_to_f32(a.residual[(size_t)m * a.ldr + n]) + round_bf16(v);
+          float r = 0.f;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (k == bl) r = rpf[k];
+          if (bl >= 4 || i >= kW4CThreads) r = bf16_bits_to_f32(a.residual[(size_t)m * a.ldr + n]);
+          v = r + round_bf16(v);
         }
         a.y[(size_t)m * a.ldy + n] = f32_to_bf16_bits(v);
       }
@@ -481,7 +570,8 @@ int w4_plan(int M, int K, int N, int g, int fmt, int num_sms, W4Plan* out) {
   return 0;
 }
 
-cudaError_t w4_launch(const W4Args& a, int fmt, cudaStream_t stream, int use_pdl) {
+cudaError_t w4_launch(const W4Args& args, int fmt, cudaStream_t stream, int use_pdl) {
+  const W4Args& a = args;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.p.G);
   cfg.blockDim = dim3((kW4Warps + 1) * 32);
