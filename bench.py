@@ -248,67 +248,80 @@ def time_e2e(fast, prompt, steps: int, warmup: int):
     return (n - warmup) / (wall[n] - wall[warmup]), res.n_steps
 
 
-def cpu_baseline(seconds_budget: float = 20.0):
+class CpuStep:
     """The numpy oracle decode step on the host cores, bounded sample: 2 of
     the 36 layers at the cfg2 shapes (fp32 BLAS on precomputed effective
-    weights, KV length 129) plus embedding and audio-phase heads, scaled to
-    the full model.  Returns (steps/s, cores, sample description)."""
-    import numpy as np
-    from oracle import step as ost
-    from oracle.bf16 import f32_to_bf16
-    c = CFG
-    H, D = c["hidden"], c["head_dim"]
-    rng = np.random.default_rng(1)
+    weights, KV length 129) plus embedding and audio-phase heads; one
+    sample() times them once and scales the layers to the full model."""
 
-    def r(*shape):
-        return f32_to_bf16((rng.standard_normal(shape, dtype=np.float32) * np.float32(c["std"])))
+    NL = 2
 
-    nl = 2
-    w = {"language_model.embed_tokens.weight": np.zeros((c["vocab"], H), np.uint16),
-         "language_model.norm.weight": f32_to_bf16(np.ones(H, np.float32))}
-    for li in range(nl):
-        p = f"language_model.layers.{li}"
-        w[f"{p}.input_layernorm.weight"] = f32_to_bf16(np.ones(H, np.float32))
-        w[f"{p}.post_attention_layernorm.weight"] = f32_to_bf16(np.ones(H, np.float32))
-        w[f"{p}.self_attn.q_proj.weight"] = r(c["n_heads"] * D, H)
-        w[f"{p}.self_attn.k_proj.weight"] = r(c["n_kv"] * D, H)
-        w[f"{p}.self_attn.v_proj.weight"] = r(c["n_kv"] * D, H)
-        w[f"{p}.self_attn.o_proj.weight"] = r(H, c["n_heads"] * D)
-        w[f"{p}.self_attn.q_norm.weight"] = f32_to_bf16(np.ones(D, np.float32))
-        w[f"{p}.self_attn.k_norm.weight"] = f32_to_bf16(np.ones(D, np.float32))
-        w[f"{p}.mlp.gate_proj.weight"] = r(c["inter"], H)
-        w[f"{p}.mlp.up_proj.weight"] = r(c["inter"], H)
-        w[f"{p}.mlp.down_proj.weight"] = r(H, c["inter"])
-    for i in range(32):
-        w[f"emb_ext.{i}.weight"] = r(1025, H)
-    w["lm_heads.0.weight"] = np.zeros((c["vocab"], H), np.uint16)
-    for i in range(32):
-        w[f"lm_heads.{i + 1}.weight"] = r(1025, H)
-    om = ost.OracleModel(w, max_seq_len=c["prompt_len"] + 8, fp32_linears=True)
-    om.seq = c["prompt_len"]
-    row = np.concatenate([[ost.AUDIO_GEN_SLOT_TOKEN_ID], rng.integers(0, 1024, 32)]).astype(np.int64)
-    reps, t_layers, t_rest = 0, 0.0, 0.0
-    t_start = time.perf_counter()
-    while reps < 3 and (reps == 0 or time.perf_counter() - t_start < seconds_budget):
+    def __init__(self):
+        import numpy as np
+        from oracle import step as ost
+        from oracle.bf16 import f32_to_bf16
+        c = CFG
+        H, D = c["hidden"], c["head_dim"]
+        rng = np.random.default_rng(1)
+
+        def r(*shape):
+            return f32_to_bf16((rng.standard_normal(shape, dtype=np.float32) * np.float32(c["std"])))
+
+        w = {"language_model.embed_tokens.weight": np.zeros((c["vocab"], H), np.uint16),
+             "language_model.norm.weight": f32_to_bf16(np.ones(H, np.float32))}
+        for li in range(self.NL):
+            p = f"language_model.layers.{li}"
+            w[f"{p}.input_layernorm.weight"] = f32_to_bf16(np.ones(H, np.float32))
+            w[f"{p}.post_attention_layernorm.weight"] = f32_to_bf16(np.ones(H, np.float32))
+            w[f"{p}.self_attn.q_proj.weight"] = r(c["n_heads"] * D, H)
+            w[f"{p}.self_attn.k_proj.weight"] = r(c["n_kv"] * D, H)
+            w[f"{p}.self_attn.v_proj.weight"] = r(c["n_kv"] * D, H)
+            w[f"{p}.self_attn.o_proj.weight"] = r(H, c["n_heads"] * D)
+            w[f"{p}.self_attn.q_norm.weight"] = f32_to_bf16(np.ones(D, np.float32))
+            w[f"{p}.self_attn.k_norm.weight"] = f32_to_bf16(np.ones(D, np.float32))
+            w[f"{p}.mlp.gate_proj.weight"] = r(c["inter"], H)
+            w[f"{p}.mlp.up_proj.weight"] = r(c["inter"], H)
+            w[f"{p}.mlp.down_proj.weight"] = r(H, c["inter"])
+        for i in range(32):
+            w[f"emb_ext.{i}.weight"] = r(1025, H)
+        w["lm_heads.0.weight"] = np.zeros((c["vocab"], H), np.uint16)
+        for i in range(32):
+            w[f"lm_heads.{i + 1}.weight"] = r(1025, H)
+        self.ost = ost
+        self.om = ost.OracleModel(w, max_seq_len=c["prompt_len"] + 8, fp32_linears=True)
+        self.om.seq = c["prompt_len"]
+        self.row = np.concatenate([[ost.AUDIO_GEN_SLOT_TOKEN_ID], rng.integers(0, 1024, 32)]).astype(np.int64)
+        try:
+            from threadpoolctl import threadpool_info
+            self.cores = max(int(i.get("num_threads", 1)) for i in threadpool_info()) or (os.cpu_count() or 1)
+        except Exception:
+            self.cores = os.cpu_count() or 1
+        self.sample_desc = (f"numpy oracle step at cfg2 shapes: {self.NL} of {CFG['n_layers']} layers timed (fp32 "
+                            f"BLAS, effective weights precomputed, KV length {CFG['prompt_len'] + 1}) + embedding + "
+                            f"audio-phase heads per sample, layers scaled to {CFG['n_layers']}")
+
+    def sample(self) -> float:
+        """Seconds of one full decode step (estimated from this sample)."""
+        om, ost = self.om, self.ost
         t0 = time.perf_counter()
-        h = om.embed_rows(row.reshape(1, -1))
+        h = om.embed_rows(self.row.reshape(1, -1))
         t1 = time.perf_counter()
-        for li in range(nl):
+        for li in range(self.NL):
             h = om.layer(li, h, om.seq)
         t2 = time.perf_counter()
         hf = ost.rms_norm(h, om.final_norm)
         om.text_logits_2way(hf)
         om.audio_logits(hf)
         t3 = time.perf_counter()
-        t_layers += t2 - t1
-        t_rest += (t1 - t0) + (t3 - t2)
-        reps += 1
-    per_step = (t_rest + t_layers * c["n_layers"] / nl) / reps
-    cores = os.cpu_count() or 1
-    sample = (f"numpy oracle step at cfg2 shapes: {nl} of {c['n_layers']} layers timed (fp32 BLAS, effective "
-              f"weights precomputed, KV length {c['prompt_len'] + 1}) + embedding + audio-phase heads, "
-              f"{reps} reps, scaled to {c['n_layers']} layers")
-    return 1.0 / per_step, cores, sample
+        return (t1 - t0) + (t3 - t2) + (t2 - t1) * CFG["n_layers"] / self.NL
+
+
+def cpu_baseline(reps: int = 3):
+    """(steps/s, cores, sample description) of the CPU oracle step."""
+    cs = CpuStep()
+    cs.sample()  # warm
+    per_step = statistics.median(cs.sample() for _ in range(reps))
+    return 1.0 / per_step, cs.cores, cs.sample_desc + f", median of {reps} samples"
 
 
 # ------------------------------------------------------------------- main
@@ -323,7 +336,9 @@ class _Dist:
         if self.world > 1:
             import datetime
             import torch.distributed as dist
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+            import torch
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
             self.pg = dist
 
     def barrier(self):
@@ -345,15 +360,15 @@ class _Dist:
 
 def run_reference_arm(args, ctx):
     """--impl reference: the CPU restatement of the reference path (numpy
-    oracle) on the host cores; rank 0 only."""
+    oracle) on the host cores; rank 0 only.  Each step is one bounded sample
+    of the decode step (CpuStep.sample), so K steps take K x ~0.5 s."""
     if ctx.rank != 0:
         return
-    vals = []
+    cs = CpuStep()
     for _ in range(max(1, args.warmup)):
-        cpu_baseline(seconds_budget=5.0)
-    for _ in range(args.steps):
-        v, cores, sample = cpu_baseline(seconds_budget=5.0)
-        vals.append(v)
+        cs.sample()
+    vals = [1.0 / cs.sample() for _ in range(args.steps)]
+    cores, sample = cs.cores, cs.sample_desc
     v = statistics.median(vals)
     line = {"metric": METRIC, "value": v, "unit": "steps/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
