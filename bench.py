@@ -248,6 +248,38 @@ def time_e2e(fast, prompt, steps: int, warmup: int):
     return (n - warmup) / (wall[n] - wall[warmup]), res.n_steps
 
 
+def time_cfg3(fast, prompt_len: int = 4096, steps: int = 1024, seed: int = 3):
+    """Configuration 3 through the public API: a 4096-row prompt (seeded random
+    ids, last row AUDIO_START) prefilled, then `steps` sampled steps with
+    audio temperature 0.8, top-k 50, top-p 0.95 (text at the reference
+    defaults), watchdog off.  Cache lengths 4097..4096+steps."""
+    import torch
+    from moss_tts_lite_b200.fast import generate_fast
+    from moss_tts_lite_b200.model import AUDIO_START_TOKEN_ID, N_VQ
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.zeros(1, prompt_len, N_VQ + 1, dtype=torch.long)
+    ids[0, :, 0] = torch.randint(0, 151643, (prompt_len,), generator=g)
+    ids[0, :, 1:] = torch.randint(0, 1024, (prompt_len, N_VQ), generator=g)
+    ids[0, -1, 0] = AUDIO_START_TOKEN_ID
+    st = {}
+    t0 = time.perf_counter()
+    res = generate_fast(fast, {"input_ids": ids}, max_new_tokens=steps, seed=seed, audio_temperature=0.8,
+                        audio_top_k=50, audio_top_p=0.95, watchdog=False, stats=st)
+    t1 = time.perf_counter()
+    wall = st.get("step_wall_s", [])
+    n = len(wall)
+    e2e = (n - 1) / (wall[-1] - wall[0]) if n > 1 else None
+    dev = st.get("step_ms", [])
+    phase = st.get("audio_phase", [])
+    return {"workload": f"cfg3: {prompt_len}-row prompt, {n} sampled steps (audio T=0.8, top-k 50, top-p 0.95), "
+                        f"cache {prompt_len + 1}..{prompt_len + n}",
+            "e2e_steps_per_s": e2e, "device_ms_per_step_median": (statistics.median(dev) if dev else None),
+            "audio_phase_frac": (sum(phase) / len(phase) if phase else None), "steps": res.n_steps,
+            "prefill_s": (st.get("prefill_ms") or 0.0) / 1e3, "wall_s": t1 - t0,
+            # audio-phase step bytes: weights + heads (3,883,599,872 B) + 147,456 B of K/V per cached position
+            "roofline_ms_per_step_at_mean_cache": (3883599872 + 147456 * (prompt_len + n / 2)) / (_peaks()[0] * 1e6)}
+
+
 class CpuStep:
     """The numpy oracle decode step on the host cores, bounded sample: 2 of
     the 36 layers at the cfg2 shapes (fp32 BLAS on precomputed effective
@@ -543,6 +575,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="mtl", choices=["mtl", "reference", "reference-gpu"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cfg3", action="store_true", help="skip the long-context sampled configuration-3 run")
     ap.add_argument("--profile-gemv", action="store_true", help="small config-0 GEMV case for ncu")
     ap.add_argument("--profile-attn", action="store_true", help="decode attention alone (config 2 heads)")
     ap.add_argument("--profile-attn-launches", action="store_true", help="4 plain attention launches (ncu case)")
@@ -582,6 +615,9 @@ def main():
     peak, peak_kind = _peaks()
     achieved = bytes_per_launch / s_per_launch / 1e9
     traffic = _ncu_traffic()
+    cfg3 = None
+    if ctx.rank == 0 and args.gpus == 1 and not args.no_cfg3:
+        cfg3 = time_cfg3(fast)
     cpu = None
     if ctx.rank == 0 and args.gpus == 1 and not args.no_cpu_baseline:
         v, cores, sample = cpu_baseline()
@@ -615,6 +651,8 @@ def main():
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if cfg3 is not None:
+            line["cfg3"] = cfg3
         print(json.dumps(line), flush=True)
     ctx.barrier()
     del fast

@@ -523,6 +523,8 @@ def generate_fast(
             _heads_from_hidden(fast, hs.last_hidden[0, -1:], audio2=is_audio)
         else:
             fast.step(None, pos, audio2=is_audio)
+            if _stats is not None:
+                _stats.setdefault("audio_phase", []).append(bool(is_audio))
             pos += 1
         _t1(e0, "prefill" if time_step == 0 else "step")
         lt_step, la_step, two_step = fast.lt_static, fast.la_static, fast.two_static
