@@ -157,7 +157,8 @@ int mtl_attn_scratch_bytes(int streams, int n_heads, int n_kv, int splits, size_
  *   qkv        bf16 [streams, (n_heads + 2 n_kv) * 128]: q | k | v projections
  *   q_norm_w, k_norm_w  bf16 [128];  rope_cos/sin bf16 [max_seq, 128]
  *   k_cache, v_cache    bf16 [n_kv, max_seq, 128] of this layer for stream 0;
- *              stream s starts cache_stream_stride elements later
+ *              stream s starts cache_stream_stride elements later (0: the
+ *              streams share one cache, see mtl_attn_append)
  *   pos        int64 [streams] (device): position being decoded
  *   splits     KV splits per head (1..64); each covers >= 64 positions
  *   flags      0 or MTL_ATTN_KV_STABLE: pos and cache rows [0, pos) were
@@ -174,6 +175,18 @@ int mtl_attn_decode(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_
                     long long cache_stream_stride, int max_seq, const int64_t* pos, int streams, int n_heads,
                     int n_kv, int head_dim, int splits, int flags, uint16_t* out, void* scratch,
                     size_t scratch_bytes, mtl_stream_t stream);
+
+/* The K/V append of mtl_attn_decode alone, for `streams` rows at once: k
+ * head RMSNorm (eps 1e-6) + RoPE at pos[s] and v, written to cache rows
+ * pos[s] (fast.py:138-146).  With cache_stream_stride = 0 all rows share one
+ * cache: a prefill chunk appends its rows first, then one mtl_attn_decode
+ * call with the same rows as streams (cache_stream_stride 0) attends each
+ * row over [0, pos[s]] (it re-writes the same K/V values).  No reference
+ * counterpart of its own: the reference appends inside _p_pre. */
+int mtl_attn_append(const uint16_t* qkv, const uint16_t* k_norm_w, const uint16_t* rope_cos,
+                    const uint16_t* rope_sin, uint16_t* k_cache, uint16_t* v_cache, long long cache_stream_stride,
+                    int max_seq, const int64_t* pos, int streams, int n_heads, int n_kv, int head_dim,
+                    mtl_stream_t stream);
 
 /* y = epilogue(x . W^T) for bf16 weights W [N, K] (the lm heads,
  * model.py:240-295, fast.py:174-194, and bf16 backbone linears: F.linear at

@@ -139,11 +139,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint8_t* sb = ring + (size_t)(i % kAttnStages) * kAttnStageBytes;
     uint64_t* bar = &full[i % kAttnStages];
     const int y = row0 + lo + i * kAttnTile;
+    const int z = a.cache_stream_stride ? st : 0;  // streams may share one cache (prefill rows)
     mbar_arrive_expect_tx(bar, kAttnStageBytes);
-    tma_load_3d(sb + 0 * kAttnBoxBytes, &tm_k, 0, y, st, bar);
-    tma_load_3d(sb + 1 * kAttnBoxBytes, &tm_k, 64, y, st, bar);
-    tma_load_3d(sb + 2 * kAttnBoxBytes, &tm_v, 0, y, st, bar);
-    tma_load_3d(sb + 3 * kAttnBoxBytes, &tm_v, 64, y, st, bar);
+    tma_load_3d(sb + 0 * kAttnBoxBytes, &tm_k, 0, y, z, bar);
+    tma_load_3d(sb + 1 * kAttnBoxBytes, &tm_k, 64, y, z, bar);
+    tma_load_3d(sb + 2 * kAttnBoxBytes, &tm_v, 0, y, z, bar);
+    tma_load_3d(sb + 3 * kAttnBoxBytes, &tm_v, 64, y, z, bar);
   };
   // layer constants: norm weights and the RoPE row of pos (lane's dims lane + 32 j)
   float qw[4], kw[4], cv[4], sv[4];
@@ -452,6 +453,55 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 }
 
+// K/V append alone (the `_p_pre` tail, fast.py:138-146): k head RMSNorm +
+// RoPE at pos[s] and v, written to cache rows pos[s] of every KV head, for
+// `streams` rows at once.  Prefill runs it for a chunk of prompt rows before
+// their attention (which re-writes the same values), so that row r can attend
+// to rows < r of the same chunk.  Grid (n_kv, streams), 128 threads: warp 0
+// does k, warp 1 v.
+__global__ void __launch_bounds__(kAttnThreads) attn_append_kernel(const AttnArgs a) {
+  const int h = blockIdx.x, st = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t p64 = a.pos[st];
+  if (p64 < 0 || p64 >= a.max_seq) {
+    if (threadIdx.x == 0) flag_error(kDevBadIndex);
+    return;
+  }
+  const int pos = (int)p64;
+  if (warp > 1) return;
+  const uint16_t* qkv = a.qkv + (size_t)st * (a.nh + 2 * a.nkv) * kHeadDim;
+  uint16_t* dst = (warp == 0 ? a.k_cache : a.v_cache) + st * a.cache_stream_stride +
+                  ((size_t)h * a.max_seq + pos) * kHeadDim;
+  const uint16_t* src = qkv + (size_t)((warp == 0 ? a.nh : a.nh + a.nkv) + h) * kHeadDim;
+  float x[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) x[j] = bf16_bits_to_f32(src[lane + 32 * j]);
+  if (warp == 1) {  // v is used as is (fast.py:137,140)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[lane + 32 * j] = f32_to_bf16_bits(x[j]);
+    return;
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) ss = fmaf(x[j], x[j], ss);
+  ss = warp_sum(ss);
+  const float rinv = rsqrtf(ss / (float)kHeadDim + 1e-6f);
+  float xn[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    xn[j] = round_bf16(bf16_bits_to_f32(a.k_norm_w[lane + 32 * j]) * round_bf16(x[j] * rinv));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int d = lane + 32 * j;
+    const float rot = j < 2 ? -xn[j + 2] : xn[j - 2];
+    const float t1 = round_bf16(xn[j] * bf16_bits_to_f32(a.rope_cos[(size_t)pos * kHeadDim + d]));
+    const float t2 = round_bf16(rot * bf16_bits_to_f32(a.rope_sin[(size_t)pos * kHeadDim + d]));
+    dst[d] = f32_to_bf16_bits(t1 + t2);
+  }
+}
+
 // ------------------------------------------------------------------- host
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -497,12 +547,21 @@ cudaError_t launch_attn_decode(const AttnArgs& a, int streams, cudaStream_t s, i
     attr_done = true;
   }
   CUtensorMap tk, tv;
-  cudaError_t e = make_kv_map(&tk, a.k_cache, a.nkv, a.max_seq, streams, a.cache_stream_stride);
-  if (e == cudaSuccess) e = make_kv_map(&tv, a.v_cache, a.nkv, a.max_seq, streams, a.cache_stream_stride);
+  const int map_streams = a.cache_stream_stride ? streams : 1;
+  cudaError_t e = make_kv_map(&tk, a.k_cache, a.nkv, a.max_seq, map_streams, a.cache_stream_stride);
+  if (e == cudaSuccess) e = make_kv_map(&tv, a.v_cache, a.nkv, a.max_seq, map_streams, a.cache_stream_stride);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.nkv, a.splits, streams), dim3(kAttnThreads), kAttnDynSmem, s, attr, use_pdl);
   return cudaLaunchKernelEx(&cfg, attn_decode_kernel, tk, tv, a);
 }
 
+}  // namespace mtl
+
+namespace mtl {
+cudaError_t launch_attn_append(const AttnArgs& a, int streams, cudaStream_t s, int use_pdl) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.nkv, streams), dim3(kAttnThreads), 0, s, attr, use_pdl);
+  return cudaLaunchKernelEx(&cfg, attn_append_kernel, a);
+}
 }  // namespace mtl

@@ -17,6 +17,7 @@ namespace mtl {
 cudaError_t launch_embed_sum(const int64_t* ids, int M, const uint16_t* emb_text, int text_vocab,
                              const uint16_t* emb_audio, int H, uint16_t* out, cudaStream_t s, int use_pdl);
 cudaError_t launch_attn_decode(const AttnArgs& a, int streams, cudaStream_t s, int use_pdl);
+cudaError_t launch_attn_append(const AttnArgs& a, int streams, cudaStream_t s, int use_pdl);
 cudaError_t launch_bf16_gemv(const Bf16GemvArgs& a, int num_sms, cudaStream_t s, int use_pdl);
 cudaError_t launch_argmax_rows(const uint16_t* x, int rows, int cols, int ld, int64_t* out, cudaStream_t s,
                                int use_pdl);
@@ -370,6 +371,31 @@ int mtl_attn_decode(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_
   a.scale = 1.0f / sqrtf((float)head_dim);
   cudaError_t e = mtl::launch_attn_decode(a, streams, stream, use_pdl());
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_attn_decode");
+}
+
+int mtl_attn_append(const uint16_t* qkv, const uint16_t* k_norm_w, const uint16_t* rope_cos,
+                    const uint16_t* rope_sin, uint16_t* k_cache, uint16_t* v_cache, long long cache_stream_stride,
+                    int max_seq, const int64_t* pos, int streams, int n_heads, int n_kv, int head_dim,
+                    mtl_stream_t stream) {
+  if (!qkv || !k_norm_w || !rope_cos || !rope_sin || !k_cache || !v_cache || !pos)
+    return fail(MTL_E_INVALID, "mtl_attn_append: NULL pointer");
+  if (head_dim != mtl::kHeadDim) return fail(MTL_E_UNSUPPORTED, "head_dim %d (only 128)", head_dim);
+  if (n_kv < 1 || n_heads % n_kv || streams < 1 || streams > 65535 || max_seq < 1 || cache_stream_stride < 0)
+    return fail(MTL_E_INVALID, "mtl_attn_append: n_heads=%d n_kv=%d streams=%d", n_heads, n_kv, streams);
+  mtl::AttnArgs a{};
+  a.qkv = qkv;
+  a.k_norm_w = k_norm_w;
+  a.rope_cos = rope_cos;
+  a.rope_sin = rope_sin;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.cache_stream_stride = cache_stream_stride;
+  a.max_seq = max_seq;
+  a.pos = pos;
+  a.nh = n_heads;
+  a.nkv = n_kv;
+  cudaError_t e = mtl::launch_attn_append(a, streams, stream, use_pdl());
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_attn_append");
 }
 
 int mtl_bf16_linear(const uint16_t* x, int M, int K, int N, const uint16_t* W, const uint16_t* norm_w, float eps,

@@ -189,16 +189,62 @@ class _StepEngine:
         self.final_norm()
         return self.h_final.clone()
 
+    def _prefill_chunk_rows(self) -> int:
+        """Rows per prefill chunk: 8 (the register-MMA kernel's batch, the MMA
+        N dimension, so 8 rows cost one pass over the weights) when every
+        linear of the layer has an 8-row launch plan, else 4."""
+        if getattr(self, "_chunk", None) is None:
+            from . import _lib
+            self._chunk = 8
+            for lin in self.lins[0].values():
+                w = getattr(lin, "w", None)
+                if w is None:
+                    continue
+                try:
+                    _lib.w4_plan(8, w.K, w.N, w.group_size, w.fmt)
+                except Exception:
+                    self._chunk = 4
+        return self._chunk
+
     def prefill_rows(self, ids: torch.Tensor) -> torch.Tensor:
-        """Prompt rows [L, 33] decoded one position at a time (each row's
-        math is the batched prefill's row math).  Returns [L, H]."""
+        """Prompt rows [L, 33] -> final-normed hidden [L, H] (fast.py:218-270).
+        Rows go through the layers in chunks: the projections of a chunk are
+        one batched W4 launch each (the weights are read once per chunk).  The
+        chunk's attention is two launches: the K/V append of all its rows,
+        then one attention launch with the rows as streams over the shared
+        cache, row r attending over [0, pos_r] (rows of the chunk included)."""
+        m = self.m
         L = ids.shape[0]
-        out = torch.empty(L, self.m.hidden_size, dtype=torch.bfloat16, device=self.m.device)
-        for t in range(L):
-            self.ids_row.view(-1).copy_(ids[t])
-            self.pos_dev.fill_(t)
-            self.backbone()
-            kernels.rmsnorm(self.h, self.m.final_norm, out[t:t + 1], RMS_EPS)
+        H = m.hidden_size
+        C = self._prefill_chunk_rows()
+        dev = m.device
+        bf = torch.bfloat16
+        if getattr(self, "_p_h", None) is None or self._p_h.shape[0] < C:
+            self._p_h = torch.zeros(C, H, dtype=bf, device=dev)
+            self._p_qkv = torch.zeros(C, self.qkv.shape[-1], dtype=bf, device=dev)
+            self._p_attn = torch.zeros(C, self.attn.shape[-1], dtype=bf, device=dev)
+            self._p_act = torch.zeros(C, self.act.shape[-1], dtype=bf, device=dev)
+            nbytes = _lib.attn_scratch_bytes(C, m.n_heads, m.n_kv_heads, self.splits)
+            self._p_scratch = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        out = torch.empty(L, H, dtype=bf, device=dev)
+        pos_all = torch.arange(L, dtype=torch.long, device=dev)
+        for r0 in range(0, L, C):
+            R = min(C, L - r0)
+            h, qkv, attn, act = self._p_h[:R], self._p_qkv[:R], self._p_attn[:R], self._p_act[:R]
+            kernels.embed_sum(ids[r0:r0 + R].contiguous(), m.embed_tokens, self.emb_audio, h)
+            for li in range(m.n_layers):
+                lyr, Lw = m.layers[li], self.lins[li]
+                Lw["qkv"](h, qkv, norm_weight=lyr["input_layernorm"])
+                pos = pos_all[r0:r0 + R]
+                kernels.attn_append(qkv, lyr["k_norm"], m.rope_cos, m.rope_sin, m.k_cache[li], m.v_cache[li],
+                                    pos, m.n_heads, m.n_kv_heads, streams=R)
+                kernels.attn_decode(qkv, lyr["q_norm"], lyr["k_norm"], m.rope_cos, m.rope_sin, m.k_cache[li],
+                                    m.v_cache[li], pos, m.n_heads, m.n_kv_heads, self.splits, attn,
+                                    self._p_scratch, streams=R)
+                Lw["o"](attn, h, residual=h)
+                Lw["gu"](h, act, norm_weight=lyr["post_attention_layernorm"], swiglu=True)
+                Lw["down"](act, h, residual=h)
+            kernels.rmsnorm(h, m.final_norm, out[r0:r0 + R], RMS_EPS)
         return out
 
 

@@ -172,6 +172,45 @@ def test_attention_decode_vs_oracle(s1, rep, streams, stable):
     assert L.device_status() == 0
 
 
+@pytest.mark.parametrize("p0,R,rep", [(0, 8, 4), (60, 8, 4), (125, 5, 8), (1021, 8, 2), (3000, 3, 4)])
+def test_attention_prefill_chunk_matches_row_by_row(p0, R, rep):
+    """Prefill chunk: K/V append of R rows, then one attention launch with the
+    rows as streams over the shared cache, must equal R single-row decode
+    attentions run in position order (outputs and cache bit for bit)."""
+    dev = require_cuda()
+    from moss_tts_lite_b200 import _lib, kernels
+    rng = np.random.default_rng(p0 + R)
+    nkv, D, max_seq, splits = 2, 128, 4096, 16
+    nh = nkv * rep
+    kc = f32_to_bf16(rng.standard_normal((nkv, max_seq, D)).astype(np.float32))
+    vc = f32_to_bf16(rng.standard_normal((nkv, max_seq, D)).astype(np.float32))
+    kc[:, p0:] = 0x7FC0  # rows from the chunk on are not yet written
+    vc[:, p0:] = 0x7FC0
+    qkv = _t(f32_to_bf16((rng.standard_normal((R, (nh + 2 * nkv) * D)) * 2).astype(np.float32)), dev,
+             torch.bfloat16)
+    qn = _t(f32_to_bf16((1 + 0.1 * rng.standard_normal(D)).astype(np.float32)), dev, torch.bfloat16)
+    kn = _t(f32_to_bf16((1 + 0.1 * rng.standard_normal(D)).astype(np.float32)), dev, torch.bfloat16)
+    cos, sin = (_t(x, dev, torch.bfloat16) for x in ost.rope_tables(max_seq, D))
+    pos = torch.arange(p0, p0 + R, device=dev)
+    # row by row
+    k1, v1 = _t(kc, dev, torch.bfloat16), _t(vc, dev, torch.bfloat16)
+    s1 = torch.zeros(_lib.attn_scratch_bytes(1, nh, nkv, splits), dtype=torch.uint8, device=dev)
+    o1 = torch.empty(R, nh * D, dtype=torch.bfloat16, device=dev)
+    for i in range(R):
+        kernels.attn_decode(qkv[i:i + 1], qn, kn, cos, sin, k1, v1, pos[i:i + 1], nh, nkv, splits, o1[i:i + 1], s1)
+    # chunked
+    k2, v2 = _t(kc, dev, torch.bfloat16), _t(vc, dev, torch.bfloat16)
+    s2 = torch.zeros(_lib.attn_scratch_bytes(R, nh, nkv, splits), dtype=torch.uint8, device=dev)
+    o2 = torch.empty(R, nh * D, dtype=torch.bfloat16, device=dev)
+    kernels.attn_append(qkv, kn, cos, sin, k2, v2, pos, nh, nkv, streams=R)
+    kernels.attn_decode(qkv, qn, kn, cos, sin, k2, v2, pos, nh, nkv, splits, o2, s2, streams=R)
+    torch.cuda.synchronize()
+    assert torch.equal(k1.view(torch.int16), k2.view(torch.int16))
+    assert torch.equal(v1.view(torch.int16), v2.view(torch.int16))
+    assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
+    assert _lib.device_status() == 0
+
+
 def test_bf16_linear_pad_and_epilogues():
     dev = require_cuda()
     from moss_tts_lite_b200 import kernels
