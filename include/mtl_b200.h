@@ -216,9 +216,13 @@ int mtl_argmax_rows(const uint16_t* x, int rows, int cols, int ld, int64_t* out,
 /* out[0] = first-index argmax of one bf16 row of `cols` values, ignoring the
  * `n_excluded` (<= 8) column indices listed in HOST array `excluded` (the
  * greedy text decision of generate_fast, fast.py:481-514, with the -inf
- * writes of fast.py:487 and 507-511 folded in). */
+ * writes of fast.py:487 and 507-511 folded in).  NaN never wins.  scratch:
+ * optional 16 bytes, 16-byte aligned, zeroed once before first use (each
+ * call leaves it zeroed); with it, rows of >= 4096 values at a 16-byte
+ * aligned x are reduced by CTAs across the whole GPU, without it by one CTA.
+ * One scratch must not serve two calls in flight at once. */
 int mtl_argmax_masked(const uint16_t* x, int cols, const int32_t* excluded, int n_excluded, int64_t* out,
-                      mtl_stream_t stream);
+                      void* scratch, mtl_stream_t stream);
 
 /* Device-side greedy feedback for an audio-phase decode loop with no host
  * round trip: ids_row[1 + j] = argmax of audio row j (bf16 [32, 1025]),
@@ -227,6 +231,25 @@ int mtl_argmax_masked(const uint16_t* x, int cols, const int32_t* excluded, int 
  * No counterpart call in the reference (its loop decides on the host). */
 int mtl_greedy_feed(const uint16_t* audio_logits, const uint16_t* two_logits, int64_t* ids_row, int64_t* pos,
                     int gen_slot_id, int delay_slot_id, mtl_stream_t stream);
+
+/* Next input row of generate_fast from one step's decisions, on the device
+ * (the reference builds current_input_ids from device tensors and copies it
+ * into ids_row, fast.py:573-584).  dec: int64 [33], dec[0] the text decision,
+ * then the audio decisions, per channel (dec[1 + j], audio_compact 0) or
+ * compact over the channels set in audio_mask (audio_compact 1).
+ *   ids_row[0]     = text_const               (text_mode 0)
+ *                    dec[0] == 0 ? gen_slot_id : delay_slot_id   (1)
+ *                    dec[0]                    (2)
+ *   ids_row[1 + j] = channel j's decision if bit j of audio_mask, else pad_code
+ *   pos[0]         = pos_value
+ * seen_bits (optional, uint32 [2, seen_words]): the row's audio ids are ORed
+ * in, channel 0 into set 0 and channels 1..31 into set 1 (the repetition-
+ * penalty histories generation_ids[:, :, 1] and [:, :, 2:]).  Running it
+ * again with the same arguments leaves the same state. */
+int mtl_feed_row(const int64_t* dec, int text_mode, long long text_const, long long gen_slot_id,
+                 long long delay_slot_id, unsigned int audio_mask, int audio_compact, long long pad_code,
+                 int64_t* ids_row, int64_t* pos, long long pos_value, uint32_t* seen_bits, int seen_words,
+                 mtl_stream_t stream);
 
 /* Fused sample_token (sampling.py:70-98) for up to 40 logits rows of one
  * decode step (fast.py:491-545), one draw per row:

@@ -23,7 +23,9 @@ cudaError_t launch_argmax_rows(const uint16_t* x, int rows, int cols, int ld, in
                                int use_pdl);
 cudaError_t launch_rtn_quantize(const uint16_t* w, int N, int K, int g, uint8_t* q, uint16_t* qsz, cudaStream_t s);
 cudaError_t launch_argmax_masked(const uint16_t* x, int cols, const int* excl, int n_excl, int64_t* out,
-                                 cudaStream_t s, int use_pdl);
+                                 void* scratch, int num_sms, cudaStream_t s, int use_pdl);
+struct FeedArgs;
+cudaError_t launch_feed_row(const FeedArgs& f, cudaStream_t s, int use_pdl);
 cudaError_t launch_greedy_feed(const uint16_t* la, const uint16_t* two, int64_t* ids, int64_t* pos, int gen_slot,
                                int delay_slot, cudaStream_t s, int use_pdl);
 cudaError_t launch_rmsnorm_rows(const uint16_t* x, int rows, int K, int ldx, const uint16_t* w, float eps,
@@ -437,10 +439,11 @@ int mtl_argmax_rows(const uint16_t* x, int rows, int cols, int ld, int64_t* out,
 }
 
 int mtl_argmax_masked(const uint16_t* x, int cols, const int32_t* excluded, int n_excluded, int64_t* out,
-                      mtl_stream_t stream) {
+                      void* scratch, mtl_stream_t stream) {
   if (!x || !out || cols < 1 || n_excluded < 0 || n_excluded > 8 || (n_excluded && !excluded))
     return fail(MTL_E_INVALID, "mtl_argmax_masked: bad arguments");
-  cudaError_t e = mtl::launch_argmax_masked(x, cols, excluded, n_excluded, out, stream, use_pdl());
+  if (scratch && !aligned(scratch, 16)) return fail(MTL_E_ALIGN, "mtl_argmax_masked: scratch must be 16-byte aligned");
+  cudaError_t e = mtl::launch_argmax_masked(x, cols, excluded, n_excluded, out, scratch, num_sms(), stream, use_pdl());
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_argmax_masked");
 }
 
@@ -450,6 +453,31 @@ int mtl_greedy_feed(const uint16_t* audio_logits, const uint16_t* two_logits, in
   cudaError_t e = mtl::launch_greedy_feed(audio_logits, two_logits, ids_row, pos, gen_slot_id, delay_slot_id, stream,
                                           use_pdl());
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_greedy_feed");
+}
+
+int mtl_feed_row(const int64_t* dec, int text_mode, long long text_const, long long gen_slot_id,
+                 long long delay_slot_id, unsigned int audio_mask, int audio_compact, long long pad_code,
+                 int64_t* ids_row, int64_t* pos, long long pos_value, uint32_t* seen_bits, int seen_words,
+                 mtl_stream_t stream) {
+  if (!dec || !ids_row || !pos) return fail(MTL_E_INVALID, "mtl_feed_row: NULL pointer");
+  if (text_mode < 0 || text_mode > 2 || (seen_bits && seen_words < 1) || pos_value < 0)
+    return fail(MTL_E_INVALID, "mtl_feed_row: text_mode %d seen_words %d pos %lld", text_mode, seen_words, pos_value);
+  mtl::FeedArgs f{};
+  f.dec = dec;
+  f.ids = ids_row;
+  f.pos_dev = pos;
+  f.seen = seen_bits;
+  f.pos = pos_value;
+  f.text_const = text_const;
+  f.gen_slot = gen_slot_id;
+  f.delay_slot = delay_slot_id;
+  f.pad_code = pad_code;
+  f.audio_mask = audio_mask;
+  f.text_mode = text_mode;
+  f.audio_compact = audio_compact;
+  f.seen_words = seen_words;
+  cudaError_t e = mtl::launch_feed_row(f, stream, use_pdl());
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_feed_row");
 }
 
 // Threads per row (log2) of PyTorch's shared-memory cumsum of a [num_rows,

@@ -80,6 +80,8 @@ __global__ void __launch_bounds__(256) embed_sum_kernel(const int64_t* __restric
 constexpr int kGemvThreads = 256;
 constexpr int kGemvMaxK = 8192;
 constexpr int kGemvMaxM = 4;
+constexpr int kGemvBatch = 8;  // 16-byte weight loads in flight per lane
+constexpr int kGemvCtasPerSm = 3;
 
 struct Bf16GemvArgs {
   const uint16_t* x;
@@ -95,7 +97,7 @@ struct Bf16GemvArgs {
   int ldy;
 };
 
-__global__ void __launch_bounds__(kGemvThreads) bf16_gemv_kernel(const Bf16GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) bf16_gemv_kernel(const Bf16GemvArgs a) {
   extern __shared__ __align__(16) float xs[];  // [M][K] fp32
   __shared__ float red[kGemvThreads / 32][kGemvMaxM];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -135,30 +137,45 @@ __global__ void __launch_bounds__(kGemvThreads) bf16_gemv_kernel(const Bf16GemvA
   const int nout = a.N / rows_per_out;
   for (int n = blockIdx.x * (kGemvThreads / 32) + warp; n < nout; n += nwarps_total) {
     float res[2][kGemvMaxM];
-    for (int rr = 0; rr < rows_per_out; ++rr) {
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      if (rr >= rows_per_out) {
+#pragma unroll
+        for (int m = 0; m < kGemvMaxM; ++m) res[rr][m] = 0.f;
+        continue;
+      }
       const uint4* wr = reinterpret_cast<const uint4*>(a.W + (size_t)(n * rows_per_out + rr) * a.K);
       float acc[kGemvMaxM];
 #pragma unroll
       for (int m = 0; m < kGemvMaxM; ++m) acc[m] = 0.f;
-#pragma unroll 4
-      for (int c = lane; c < chunks; c += 32) {
-        const uint4 v = __ldg(wr + c);
-        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+      // all loads of a batch of kGemvBatch chunks are issued before any is
+      // used: 4 KB per warp in flight
+      for (int c0 = lane; c0 < chunks; c0 += 32 * kGemvBatch) {
+        uint4 vb[kGemvBatch];
 #pragma unroll
-        for (int m = 0; m < kGemvMaxM; ++m) {
-          if (m < a.M) {
-            const float4 x0 = reinterpret_cast<const float4*>(xs + (size_t)m * a.K)[2 * c];
-            const float4 x1 = reinterpret_cast<const float4*>(xs + (size_t)m * a.K)[2 * c + 1];
-            float s = acc[m];
-            s = fmaf(__uint_as_float(u[0] << 16), x0.x, s);
-            s = fmaf(__uint_as_float(u[0] & 0xFFFF0000u), x0.y, s);
-            s = fmaf(__uint_as_float(u[1] << 16), x0.z, s);
-            s = fmaf(__uint_as_float(u[1] & 0xFFFF0000u), x0.w, s);
-            s = fmaf(__uint_as_float(u[2] << 16), x1.x, s);
-            s = fmaf(__uint_as_float(u[2] & 0xFFFF0000u), x1.y, s);
-            s = fmaf(__uint_as_float(u[3] << 16), x1.z, s);
-            s = fmaf(__uint_as_float(u[3] & 0xFFFF0000u), x1.w, s);
-            acc[m] = s;
+        for (int i = 0; i < kGemvBatch; ++i)
+          vb[i] = (c0 + 32 * i < chunks) ? __ldg(wr + c0 + 32 * i) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int i = 0; i < kGemvBatch; ++i) {
+          const int c = c0 + 32 * i;
+          if (c >= chunks) break;
+          const uint32_t u[4] = {vb[i].x, vb[i].y, vb[i].z, vb[i].w};
+#pragma unroll
+          for (int m = 0; m < kGemvMaxM; ++m) {
+            if (m < a.M) {
+              const float4 x0 = reinterpret_cast<const float4*>(xs + (size_t)m * a.K)[2 * c];
+              const float4 x1 = reinterpret_cast<const float4*>(xs + (size_t)m * a.K)[2 * c + 1];
+              float s = acc[m];
+              s = fmaf(__uint_as_float(u[0] << 16), x0.x, s);
+              s = fmaf(__uint_as_float(u[0] & 0xFFFF0000u), x0.y, s);
+              s = fmaf(__uint_as_float(u[1] << 16), x0.z, s);
+              s = fmaf(__uint_as_float(u[1] & 0xFFFF0000u), x0.w, s);
+              s = fmaf(__uint_as_float(u[2] << 16), x1.x, s);
+              s = fmaf(__uint_as_float(u[2] & 0xFFFF0000u), x1.y, s);
+              s = fmaf(__uint_as_float(u[3] << 16), x1.z, s);
+              s = fmaf(__uint_as_float(u[3] & 0xFFFF0000u), x1.w, s);
+              acc[m] = s;
+            }
           }
         }
       }
@@ -306,6 +323,70 @@ __global__ void __launch_bounds__(256) argmax_masked_kernel(const uint16_t* __re
   }
 }
 
+// The same decision spread over the whole GPU for long rows (the 155,648-way
+// text head): each CTA reduces its chunks to one 64-bit key (order-preserving
+// value bits << 32 | ~index, so the largest key is the largest value at the
+// smallest index), merges it with atomicMax into key_slot[0], and the last
+// CTA to arrive (counter key_slot[1]) writes the index and re-arms both
+// words for the next call.  NaN never wins and -0 ranks as +0, as in the
+// one-CTA kernel.  x must be 16-byte aligned.
+__device__ __forceinline__ unsigned long long argmax_key(uint32_t bits, int idx) {
+  if ((bits & 0x7FFFFFFFu) > 0x7F800000u) return 0ull;  // NaN
+  if ((bits & 0x7FFFFFFFu) == 0u) bits = 0u;            // -0 == +0
+  const uint32_t ord = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+  return ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
+}
+
+__global__ void __launch_bounds__(256) argmax_masked_grid_kernel(const uint16_t* __restrict__ x, int cols,
+                                                                 ExcludeList ex, int64_t* __restrict__ out,
+                                                                 unsigned long long* key_slot) {
+  __shared__ unsigned long long sk[8];
+  __shared__ int last;
+  pdl_launch_dependents();
+  pdl_wait();
+  unsigned long long best = 0ull;
+  const int nchunks = cols >> 3;
+  const int stride = gridDim.x * blockDim.x;
+  auto take = [&](uint32_t bits, int idx) {
+    bool skip = false;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) skip |= (e < ex.n) && (ex.idx[e] == idx);
+    const unsigned long long k = skip ? 0ull : argmax_key(bits, idx);
+    best = k > best ? k : best;
+  };
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < nchunks; c += stride) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(x) + c);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      take(u[q] << 16, 8 * c + 2 * q);
+      take(u[q] & 0xFFFF0000u, 8 * c + 2 * q + 1);
+    }
+  }
+  for (int i = 8 * nchunks + blockIdx.x * blockDim.x + threadIdx.x; i < cols; i += stride)
+    take((uint32_t)x[i] << 16, i);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long ob = __shfl_xor_sync(0xffffffffu, best, o);
+    best = ob > best ? ob : best;
+  }
+  if ((threadIdx.x & 31) == 0) sk[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = sk[w] > best ? sk[w] : best;
+    atomicMax(&key_slot[0], best);
+    __threadfence();
+    last = atomicAdd(&key_slot[1], 1ull) == (unsigned long long)(gridDim.x - 1);
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence();
+    const unsigned long long k = atomicExch(&key_slot[0], 0ull);
+    atomicExch(&key_slot[1], 0ull);
+    out[0] = k ? (int64_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull)) : 0;
+  }
+}
+
 // ---------------------------------------------------------- greedy feed
 // Device-side greedy feedback for an autoregressive audio-phase decode loop
 // without host round trips: next row = [GEN_SLOT or DELAY_SLOT by the 2-way
@@ -343,6 +424,43 @@ __global__ void __launch_bounds__(1024) greedy_feed_kernel(const uint16_t* __res
     const float a = bf16_bits_to_f32(two[0]), b = bf16_bits_to_f32(two[1]);
     ids[0] = (b > a) ? delay_slot : gen_slot;
     pos[0] += 1;
+  }
+}
+
+// Next input row of generate_fast built on the device from the step's
+// decisions (the reference builds current_input_ids with device tensors,
+// fast.py:573-584): dec = [text decision, audio decisions], the audio ones
+// either per channel (dec[1 + j]) or compact over the sampled channels
+// (dec[1 + rank of j in audio_mask]).  Also sets pos and ORs the new audio
+// ids into the repetition-penalty sets (channel 0 -> set 0, 1..31 -> set 1).
+// Re-running it with the same inputs writes the same row (the OR is
+// idempotent), which the pipelined host loop relies on.
+struct FeedArgs {
+  const int64_t* dec;
+  int64_t* ids;
+  int64_t* pos_dev;
+  uint32_t* seen;
+  long long pos, text_const, gen_slot, delay_slot, pad_code;
+  unsigned int audio_mask;
+  int text_mode, audio_compact, seen_words;
+};
+
+__global__ void __launch_bounds__(32) feed_row_kernel(const FeedArgs f) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int j = threadIdx.x;
+  const unsigned bit = 1u << j;
+  int64_t tok = f.pad_code;
+  if (f.audio_mask & bit) tok = f.dec[1 + (f.audio_compact ? __popc(f.audio_mask & (bit - 1u)) : j)];
+  f.ids[1 + j] = tok;
+  if (f.seen && tok >= 0 && tok < (int64_t)f.seen_words * 32)
+    atomicOr(f.seen + (j ? f.seen_words : 0) + (int)(tok >> 5), 1u << (tok & 31));
+  if (j == 0) {
+    int64_t t = f.text_const;
+    if (f.text_mode == 1) t = f.dec[0] == 0 ? f.gen_slot : f.delay_slot;
+    if (f.text_mode == 2) t = f.dec[0];
+    f.ids[0] = t;
+    f.pos_dev[0] = f.pos;
   }
 }
 
@@ -417,7 +535,7 @@ cudaError_t launch_bf16_gemv(const Bf16GemvArgs& a, int num_sms, cudaStream_t s,
   }
   const int rows_per_cta = kGemvThreads / 32;
   const int nout = (a.epi == 2) ? a.N / 2 : a.N;
-  const int grid = std::max(1, std::min((nout + rows_per_cta - 1) / rows_per_cta, num_sms * 4));
+  const int grid = std::max(1, std::min((nout + rows_per_cta - 1) / rows_per_cta, num_sms * kGemvCtasPerSm));
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_cfg(dim3(grid), dim3(kGemvThreads), (size_t)a.M * a.K * 4, s, attr, use_pdl);
   return cudaLaunchKernelEx(&cfg, bf16_gemv_kernel, a);
@@ -438,12 +556,18 @@ cudaError_t launch_rmsnorm_rows(const uint16_t* x, int rows, int K, int ldx, con
 }
 
 cudaError_t launch_argmax_masked(const uint16_t* x, int cols, const int* excl, int n_excl, int64_t* out,
-                                 cudaStream_t s, int use_pdl) {
+                                 void* scratch, int num_sms, cudaStream_t s, int use_pdl) {
   ExcludeList ex{};
   ex.n = n_excl;
   for (int i = 0; i < n_excl && i < 8; ++i) ex.idx[i] = excl[i];
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_cfg(dim3(1), dim3(256), 0, s, attr, use_pdl);
+  if (scratch && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && cols >= 4096) {
+    const int grid = std::max(1, std::min(num_sms, (cols / 8 + 255) / 256));
+    cudaLaunchConfig_t gcfg = pdl_cfg(dim3(grid), dim3(256), 0, s, attr, use_pdl);
+    return cudaLaunchKernelEx(&gcfg, argmax_masked_grid_kernel, x, cols, ex, out,
+                              reinterpret_cast<unsigned long long*>(scratch));
+  }
   return cudaLaunchKernelEx(&cfg, argmax_masked_kernel, x, cols, ex, out);
 }
 
@@ -452,6 +576,12 @@ cudaError_t launch_greedy_feed(const uint16_t* la, const uint16_t* two, int64_t*
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_cfg(dim3(1), dim3(kNVQ * 32), 0, s, attr, use_pdl);
   return cudaLaunchKernelEx(&cfg, greedy_feed_kernel, la, two, ids, pos, gen_slot, delay_slot);
+}
+
+cudaError_t launch_feed_row(const FeedArgs& f, cudaStream_t s, int use_pdl) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_cfg(dim3(1), dim3(kNVQ), 0, s, attr, use_pdl);
+  return cudaLaunchKernelEx(&cfg, feed_row_kernel, f);
 }
 
 cudaError_t launch_rtn_quantize(const uint16_t* w, int N, int K, int g, uint8_t* q, uint16_t* qsz, cudaStream_t s) {

@@ -17,13 +17,12 @@ buffers, plus ``generate_fast``.  What changes is the step itself:
 """
 from __future__ import annotations
 
-import math
 import time
 from dataclasses import dataclass, field
 
 import torch
 
-from . import _lib, kernels
+from . import _lib, fsm, kernels
 from .generate import GenResult
 from .model import (AUDIO_DELAY_SLOT_TOKEN_ID, AUDIO_END_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_PAD_CODE,
                     AUDIO_START_TOKEN_ID, AUDIO_VOCAB, IM_END_TOKEN_ID, LIN_NAMES, N_VQ, PAD_TOKEN_ID,
@@ -414,11 +413,9 @@ class FastMossTTS:
 
 
 # ------------------------------------------------------------ generate_fast
-_WD_LOW_ENERGY_CH0 = frozenset(
-    (9, 60, 109, 123, 163, 209, 216, 365, 399, 402, 421, 580, 715, 734,
-     774, 795, 827, 888, 890, 936, 971, 996, 1001))
-_WD_SEGMENT_FLOOR = 640
-_WD_SEGMENT_BACKSTOP_RUN = 32
+_WD_LOW_ENERGY_CH0 = fsm.WD_LOW_ENERGY_CH0
+_WD_SEGMENT_FLOOR = fsm.WD_SEGMENT_FLOOR
+_WD_SEGMENT_BACKSTOP_RUN = fsm.WD_SEGMENT_BACKSTOP_RUN
 
 
 @dataclass
@@ -430,29 +427,81 @@ class GenResultWatchdog(GenResult):
     watchdog_stats: dict = field(default_factory=dict)
 
 
-class _Decider:
-    """Device-side token decisions of one generate_fast step: greedy argmax
-    over the 32 audio rows and the masked text decision, fetched with one
-    device->host copy."""
+def _seen_bits(audio_cols: torch.Tensor, device) -> torch.Tensor:
+    """Repetition-penalty histories of the prompt as int32 bit sets [2, 33]:
+    set 0 = channel 0 ids (generation_ids[:, :, 1]), set 1 = channels 1..31
+    (generation_ids[:, :, 2:]), ids outside [0, 1025) ignored."""
+    words = (AUDIO_VOCAB + 31) // 32
+    bits = torch.zeros(2, words * 32, dtype=torch.bool)
+    for si, ids in enumerate((audio_cols[:, 0], audio_cols[:, 1:])):
+        ids = torch.unique(ids.reshape(-1).cpu())
+        bits[si, ids[(ids >= 0) & (ids < AUDIO_VOCAB)]] = True
+    w = (bits.view(2, words, 32).to(torch.int64) << torch.arange(32)).sum(-1)
+    return w.to(torch.int32).to(device)
 
-    def __init__(self, fast: FastMossTTS):
+
+class _DeviceOps:
+    """The device side of one generate_fast call for fsm.drive: step launches
+    (input-row feed, head graph, decisions into a two-slot ring) and the
+    read-back of a step's decision slot (one pinned 264-byte copy)."""
+
+    def __init__(self, fast: FastMossTTS, input_ids: torch.Tensor, sampling: dict, seen: torch.Tensor | None,
+                 stats: dict | None):
         dev = fast.m.device
         self.fast = fast
-        self.dev_out = torch.zeros(N_VQ + 1, dtype=torch.long, device=dev)
-        self.host = torch.zeros(N_VQ + 1, dtype=torch.long, pin_memory=True)
+        self.input_ids = input_ids
+        self.sp = sampling
+        self.seen = seen
+        self.stats = stats
+        self.dec = torch.zeros(2, N_VQ + 1, dtype=torch.long, device=dev)
+        self.host = torch.zeros(2, N_VQ + 1, dtype=torch.long, pin_memory=True)
+        self.ev = [torch.cuda.Event(), torch.cuda.Event()]
+        self.amax = kernels.argmax_scratch(dev)
+        self.times: dict = {}
+        self.launches = 0
 
-    def run(self, la, text_src, text_excluded, need_text: bool, need_audio: bool):
-        if need_audio:
-            kernels.argmax_rows(la, self.dev_out[1:])
-        if need_text:
-            kernels.argmax_masked(text_src, self.dev_out[0:1], text_excluded)
-        return self.fetch()
+    def _event(self):
+        if self.stats is None:
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
 
-    def fetch(self):
-        """One device->host copy of the step's decisions."""
-        self.host.copy_(self.dev_out, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        return self.host.tolist()
+    def launch(self, t: int, plan: fsm.StepPlan, prev: fsm.StepPlan | None, pos: int) -> None:
+        from .sampling import sample_rows
+        fast, sp = self.fast, self.sp
+        self.launches += 1
+        e0 = self._event()
+        if t == 0:
+            hs = fast.prefill(self.input_ids)
+            fast.capture()
+            _heads_from_hidden(fast, hs.last_hidden[0, -1:], audio2=plan.audio2)
+        else:
+            kernels.feed_row(self.dec[(t - 1) & 1], fast.ids_row, fast.pos_dev, pos, text_mode=prev.text_mode,
+                             text_const=prev.text_const, gen_slot=AUDIO_GEN_SLOT_TOKEN_ID,
+                             delay_slot=AUDIO_DELAY_SLOT_TOKEN_ID, audio_mask=prev.smask,
+                             audio_compact=prev.sample_audio, pad_code=AUDIO_PAD_CODE, seen_bits=self.seen)
+            fast.graphs[1 if plan.audio2 else 0].replay()
+        if self.stats is not None:
+            self.times[t] = (e0, self._event())
+        out = self.dec[t & 1]
+        if plan.greedy_audio:
+            kernels.argmax_rows(fast.la_static, out[1:])
+        if plan.greedy_text:
+            kernels.argmax_masked(fast.two_static if plan.text_two else fast.lt_static, out[0:1], plan.excluded,
+                                  scratch=self.amax)
+        if plan.sample_text:
+            sample_rows.text(fast, plan.is_audio, t, sp["text_temperature"], sp["text_top_k"], sp["text_top_p"],
+                             sp["seed"], 2 * plan.offset, out[0:1])
+        if plan.sample_audio:
+            sample_rows.audio(fast, plan.smask_list, sp["audio_temperature"], sp["audio_top_k"], sp["audio_top_p"],
+                              sp["audio_repetition_penalty"], self.seen, sp["seed"], 2 * plan.offset + 1, out[1:])
+        self.host[t & 1].copy_(out, non_blocking=True)
+        self.ev[t & 1].record()
+
+    def fetch(self, t: int) -> list:
+        self.ev[t & 1].synchronize()
+        return self.host[t & 1].tolist()
 
 
 @torch.inference_mode()
@@ -474,13 +523,19 @@ def generate_fast(
     watchdog_silence_frames: int | None = None,
     watchdog_max_segment_frames: int | None = None,
     max_requested_pause_s: float | None = None,
+    pipelined: bool = True,
 ) -> GenResult:
     """Delay-pattern generation on FastMossTTS with the control flow of the
     reference's generate_fast (fast.py:342-610): same text decision, per-
-    channel audio mask, watchdog and stopping rules.  Greedy decisions are
-    first-index argmaxes computed on the device; sampled decisions use the
-    fused sampling kernel (see moss_tts_lite_b200.sampling)."""
-    from .sampling import sample_rows
+    channel audio mask, watchdog and stopping rules (moss_tts_lite_b200.fsm).
+    Greedy decisions are first-index argmaxes computed on the device; sampled
+    decisions use the fused sampling kernel (moss_tts_lite_b200.sampling).
+    The next input row is built on the device from the decisions, and with
+    ``pipelined`` (the default) step t+1 is enqueued before the host reads
+    step t back, so the GPU does not wait for the host between steps.  With
+    a stop or the step budget reached, that one speculated step may still run
+    after the call returns (it only writes the static buffers and the cache
+    row past the generated sequence)."""
     model = fast.m
     device = model.device
     input_ids = prompt["input_ids"].to(device=device, dtype=torch.long)
@@ -499,25 +554,6 @@ def generate_fast(
         raise ValueError(f"prompt {int(input_ids.shape[1])} + max_new_tokens {max_new_tokens} "
                          f"exceeds KV cache {model.max_seq_len}")
     seq_len = int(input_ids.shape[1])
-    _stats = stats if stats is not None else None
-
-    def _t0():
-        if _stats is None:
-            return None
-        e = torch.cuda.Event(enable_timing=True)
-        e.record()
-        return e
-
-    def _t1(e0, slot):
-        if _stats is None:
-            return
-        e = torch.cuda.Event(enable_timing=True)
-        e.record()
-        if slot == "prefill":
-            _stats["prefill"] = (e0, e)
-        else:
-            _stats.setdefault("step_ms", []).append((e0, e))
-
     if greedy:
         text_temperature = 0
         audio_temperature = 0
@@ -527,180 +563,43 @@ def generate_fast(
     audio_do_sample = audio_temperature > 0
     if not audio_do_sample:
         audio_temperature = 1
-    step_offset = 0      # Philox stream offset of the sampled decisions
+    cfg = fsm.GenConfig.make(text_do_sample, audio_do_sample, watchdog, watchdog_silence_frames,
+                             watchdog_max_segment_frames, max_requested_pause_s)
+    st = fsm.FsmState.from_prompt(input_ids[0, :, 0].tolist())
+    seen = None
+    if audio_do_sample and audio_repetition_penalty != 1.0:
+        seen = _seen_bits(input_ids[0, :, 1:], device)
+    sampling = dict(seed=seed, text_temperature=text_temperature, text_top_k=text_top_k, text_top_p=text_top_p,
+                    audio_temperature=audio_temperature, audio_top_k=audio_top_k, audio_top_p=audio_top_p,
+                    audio_repetition_penalty=audio_repetition_penalty)
+    ops = _DeviceOps(fast, input_ids, sampling, seen, stats)
 
-    col0 = input_ids[0, :, 0].tolist()
-    last0 = col0[-1]
-    is_continuation = last0 in (AUDIO_START_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID)
-    hits = [i for i, c in enumerate(col0) if c == AUDIO_START_TOKEN_ID]
-    start_idx = hits[-1] if hits else -1
-    al = seq_len - start_idx if (is_continuation and start_idx != -1) else 0
-    is_audio = is_continuation and start_idx != -1
-    dl = _INT64_MAX
-    is_stopping = False
-    pre_exclude0 = (PAD_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_DELAY_SLOT_TOKEN_ID, AUDIO_END_TOKEN_ID)
+    def on_step(t, plan):
+        if stats is None:
+            return
+        if t > 0:
+            stats.setdefault("audio_phase", []).append(bool(plan.audio2))
+        stats.setdefault("step_wall_s", []).append(time.perf_counter())
 
-    prompt_audio = input_ids[0, :, 1:].tolist()
-    seen_ch0 = {r[0] for r in prompt_audio}                      # generation_ids[:, :, 1]
-    seen_rest = {t for r in prompt_audio for t in r[1:]}         # generation_ids[:, :, 2:]
-    text_steps: list = []
-    audio_steps: list = []
-    n_steps = 0
-    pos = seq_len
-    captured = False
-    decider = _Decider(fast)
-    wd_stop = False
-    wd_reason = ""
-    wd_silent_run = 0
-    wd_peak_segment = 0
-    wd_stats: dict = {}
-    wd_floor = watchdog_max_segment_frames if watchdog_max_segment_frames is not None else _WD_SEGMENT_FLOOR
-    wd_sil = watchdog_silence_frames if watchdog_silence_frames is not None else 64
-    if max_requested_pause_s is not None and max_requested_pause_s > 0:
-        wd_sil = max(wd_sil, math.ceil((max_requested_pause_s + 2.0) * 12.5))
-
-    for time_step in range(max_new_tokens):
-        e0 = _t0()
-        if time_step == 0:
-            hs = fast.prefill(input_ids)
-            if not captured:
-                fast.capture()
-                captured = True
-            _heads_from_hidden(fast, hs.last_hidden[0, -1:], audio2=is_audio)
-        else:
-            fast.step(None, pos, audio2=is_audio)
-            if _stats is not None:
-                _stats.setdefault("audio_phase", []).append(bool(is_audio))
-            pos += 1
-        _t1(e0, "prefill" if time_step == 0 else "step")
-        lt_step, la_step, two_step = fast.lt_static, fast.la_static, fast.two_static
-
-        next_text = PAD_TOKEN_ID
-        if wd_stop:
-            if dl == _INT64_MAX or dl < N_VQ:
-                next_text = AUDIO_DELAY_SLOT_TOKEN_ID
-            else:
-                next_text = AUDIO_END_TOKEN_ID
-                is_audio = False
-        elif not is_stopping and dl < N_VQ:
-            next_text = AUDIO_DELAY_SLOT_TOKEN_ID
-        elif not is_stopping and dl == N_VQ:
-            next_text = AUDIO_END_TOKEN_ID
-            is_audio = False
-        sampling_text = (not is_stopping) and (not wd_stop) and dl > N_VQ
-        smask = [(al > j) and (dl == _INT64_MAX or j > dl - 1) for j in range(N_VQ)]
-        need_audio = any(smask)
-
-        if (sampling_text and not text_do_sample) or (need_audio and not audio_do_sample):
-            text_src, excluded = two_step, ()
-            if sampling_text and is_audio:
-                excluded = (1,) if time_step == 0 else ()
-            elif sampling_text:
-                text_src = lt_step
-                ex = list(pre_exclude0)
-                if time_step == 0:
-                    ex.append(AUDIO_DELAY_SLOT_TOKEN_ID)
-                if time_step <= N_VQ:
-                    ex.append(IM_END_TOKEN_ID)
-                excluded = tuple(sorted(set(ex)))
-            dec = decider.run(la_step, text_src, excluded,
-                              need_text=sampling_text and not text_do_sample,
-                              need_audio=need_audio and not audio_do_sample)
-        else:
-            dec = None
-
-        sampled = None
-        if (sampling_text and text_do_sample) or (need_audio and audio_do_sample):
-            step_offset += 1
-            if sampling_text and text_do_sample:
-                sample_rows.text(fast, is_audio, time_step, text_temperature, text_top_k, text_top_p,
-                                 seed, 2 * step_offset, decider.dev_out[0:1])
-            rows = []
-            if need_audio and audio_do_sample:
-                rows = sample_rows.audio(fast, smask, audio_temperature, audio_top_k, audio_top_p,
-                                         audio_repetition_penalty, seen_ch0, seen_rest, seed,
-                                         2 * step_offset + 1, decider.dev_out[1:])
-            host = decider.fetch()
-            sampled = (host[0], {j: host[1 + i] for i, j in enumerate(rows)})
-
-        if sampling_text:
-            if not text_do_sample:
-                if is_audio:
-                    next_text = AUDIO_GEN_SLOT_TOKEN_ID if dec[0] == 0 else AUDIO_DELAY_SLOT_TOKEN_ID
-                else:
-                    next_text = int(dec[0])
-            elif is_audio:
-                next_text = AUDIO_GEN_SLOT_TOKEN_ID if sampled[0] == 0 else AUDIO_DELAY_SLOT_TOKEN_ID
-            else:
-                next_text = int(sampled[0])
-        if next_text == AUDIO_START_TOKEN_ID:
-            is_audio = True
-        if next_text == IM_END_TOKEN_ID:
-            is_stopping = True
-
-        next_audio = [AUDIO_PAD_CODE] * N_VQ
-        if need_audio:
-            for j in range(N_VQ):
-                if smask[j]:
-                    next_audio[j] = int(dec[1 + j]) if not audio_do_sample else int(sampled[1][j])
-
-        ch0_val = next_audio[0]
-        if watchdog and not wd_stop and is_audio and dl == _INT64_MAX:
-            if ch0_val in _WD_LOW_ENERGY_CH0:
-                wd_silent_run += 1
-            else:
-                wd_silent_run = 0
-            seg_bound = max(wd_floor, 2 * wd_peak_segment)
-            if wd_silent_run >= wd_sil:
-                wd_stop, wd_reason = True, "silence"
-            elif al > seg_bound and wd_silent_run >= _WD_SEGMENT_BACKSTOP_RUN:
-                wd_stop, wd_reason = True, "max_segment"
-            if wd_stop:
-                wd_stats = {"reason": wd_reason, "step": n_steps + 1, "segment_frames": al,
-                            "silent_run": wd_silent_run, "peak_completed_segment": wd_peak_segment,
-                            "silence_threshold_frames": wd_sil, "segment_bound_frames": seg_bound,
-                            "max_requested_pause_s": max_requested_pause_s}
-
-        if next_text in (AUDIO_START_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_DELAY_SLOT_TOKEN_ID):
-            al += 1
-        if next_text == AUDIO_END_TOKEN_ID:
-            wd_peak_segment = max(wd_peak_segment, al)
-            wd_silent_run = 0
-            al = 0
-        if dl == _INT64_MAX and next_text == AUDIO_DELAY_SLOT_TOKEN_ID:
-            dl = 0
-        if dl != _INT64_MAX:
-            dl += 1
-        if dl > N_VQ:
-            dl = _INT64_MAX
-
-        # pageable source: the copy is staged before copy_ returns
-        fast.ids_row.view(-1).copy_(torch.tensor([next_text] + next_audio, dtype=torch.long))
-        seen_ch0.add(next_audio[0])
-        seen_rest.update(next_audio[1:])
-        if _stats is not None:
-            _stats.setdefault("step_wall_s", []).append(time.perf_counter())
-        text_steps.append(next_text)
-        audio_steps.append(next_audio)
-        n_steps += 1
-        if is_stopping:
-            break
-        if wd_stop and next_text == AUDIO_END_TOKEN_ID:
-            break
-
-    text_ids = torch.tensor(text_steps, dtype=torch.long) if text_steps else torch.empty(0, dtype=torch.long)
-    audio_frames = (torch.tensor(audio_steps, dtype=torch.long) if audio_steps
+    r = fsm.drive(ops, st, cfg, max_new_tokens, seq_len, pipelined=pipelined, on_step=on_step)
+    st = r.state
+    text_ids = (torch.tensor(r.text_steps, dtype=torch.long) if r.text_steps
+                else torch.empty(0, dtype=torch.long))
+    audio_frames = (torch.tensor(r.audio_steps, dtype=torch.long) if r.audio_steps
                     else torch.empty(0, N_VQ, dtype=torch.long))
-    if _stats is not None:
+    if stats is not None:
         torch.cuda.synchronize()
-        p = _stats.get("prefill")
-        _stats["prefill_ms"] = float(p[0].elapsed_time(p[1])) if p else None
-        _stats["step_ms"] = [float(a.elapsed_time(b)) for a, b in _stats.get("step_ms", [])]
-        _stats["steps"] = len(_stats["step_ms"])
+        p = ops.times.get(0)
+        stats["prefill_ms"] = float(p[0].elapsed_time(p[1])) if p else None
+        stats["step_ms"] = [float(a.elapsed_time(b)) for t, (a, b) in sorted(ops.times.items())
+                            if 0 < t < r.n_steps]
+        stats["steps"] = len(stats["step_ms"])
+        stats["launches"] = ops.launches
+        stats["relaunches"] = r.relaunches
     return GenResultWatchdog(text_ids=text_ids, audio_frames=audio_frames,
-                             finished=bool(is_stopping) or bool(wd_stats), n_steps=n_steps,
-                             watchdog_triggered=bool(wd_stats), watchdog_reason=wd_reason,
-                             watchdog_stats=wd_stats)
+                             finished=bool(st.is_stopping) or bool(st.wd_stats), n_steps=r.n_steps,
+                             watchdog_triggered=bool(st.wd_stats), watchdog_reason=st.wd_reason,
+                             watchdog_stats=st.wd_stats)
 
 
 def _heads_from_hidden(fast: FastMossTTS, hv: torch.Tensor, audio2: bool) -> None:

@@ -91,12 +91,27 @@ def argmax_rows(x: torch.Tensor, out: torch.Tensor, cols: int | None = None) -> 
     return out
 
 
-def argmax_masked(x: torch.Tensor, out: torch.Tensor, excluded=()) -> torch.Tensor:
-    """out[0] = first-index argmax of the bf16 row ``x`` ignoring ``excluded`` (<= 8 indices)."""
+def argmax_scratch(device) -> torch.Tensor:
+    """16 zeroed bytes for the GPU-wide argmax (one per concurrent caller)."""
+    return torch.zeros(16, dtype=torch.uint8, device=device)
+
+
+def argmax_masked(x: torch.Tensor, out: torch.Tensor, excluded=(), scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """out[0] = first-index argmax of the bf16 row ``x`` ignoring ``excluded``
+    (<= 8 indices); with ``scratch`` (argmax_scratch) long rows use the whole GPU."""
     ex = list(excluded)
     arr = (ctypes.c_int32 * max(1, len(ex)))(*ex)
-    _lib.call("mtl_argmax_masked", x.data_ptr(), x.numel(), arr, len(ex), out.data_ptr(), _s())
+    _lib.call("mtl_argmax_masked", x.data_ptr(), x.numel(), arr, len(ex), out.data_ptr(), _p(scratch), _s())
     return out
+
+
+def feed_row(dec: torch.Tensor, ids_row: torch.Tensor, pos_dev: torch.Tensor, pos: int, *, text_mode: int,
+             text_const: int, gen_slot: int, delay_slot: int, audio_mask: int, audio_compact: bool, pad_code: int,
+             seen_bits: torch.Tensor | None = None) -> None:
+    """Next generate_fast input row from the step's decisions ``dec`` (int64 [33]), on the device."""
+    words = seen_bits.shape[-1] if seen_bits is not None else 0
+    _lib.call("mtl_feed_row", dec.data_ptr(), text_mode, text_const, gen_slot, delay_slot, audio_mask,
+              int(audio_compact), pad_code, ids_row.data_ptr(), pos_dev.data_ptr(), pos, _p(seen_bits), words, _s())
 
 
 def greedy_feed(la: torch.Tensor, two: torch.Tensor, ids_row: torch.Tensor, pos_dev: torch.Tensor,

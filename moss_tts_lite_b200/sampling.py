@@ -16,8 +16,8 @@ import itertools
 import torch
 
 from . import kernels
-from .model import (AUDIO_DELAY_SLOT_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_PAD_CODE, AUDIO_VOCAB,
-                    IM_END_TOKEN_ID, N_VQ)
+from .model import (AUDIO_DELAY_SLOT_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_PAD_CODE, IM_END_TOKEN_ID,
+                    N_VQ)
 
 _offsets = itertools.count(1)
 
@@ -77,27 +77,23 @@ class sample_rows:  # noqa: N801 - namespace of the two sampled decisions of gen
                                 offset=offset, out=out)
 
     @staticmethod
-    def audio(fast, smask, temperature: float, top_k, top_p, penalty: float, seen_ch0: set, seen_rest: set,
-              seed: int, offset: int, out: torch.Tensor) -> list:
+    def audio(fast, smask, temperature: float, top_k, top_p, penalty: float, seen_bits, seed: int, offset: int,
+              out: torch.Tensor) -> list:
         """fast.py:516-545: channel 0 with its own history for the penalty,
         the other sampled channels with the union of channels 1..31 (the
         reference passes generation_ids[:, :, 2:] to a 2-D sample_token).
-        Writes one token per sampled channel to out[0:n]; returns the rows."""
+        ``seen_bits``: device int32 [2, 33] bit sets of those two histories
+        (needed when penalty != 1).  Writes one token per sampled channel to
+        out[0:n]; returns the rows."""
         rows = [j for j in range(N_VQ) if smask[j]]
-        seen = None
         sets = [0 if j == 0 else 1 for j in rows]
         # the reference scans channel 0 as [1, V] and the rest as [R, V]
         n_rest = sum(1 for j in rows if j > 0)
         scan = [1 if j == 0 else n_rest for j in rows]
-        if penalty != 1.0:
-            words = (AUDIO_VOCAB + 31) // 32
-            bits = torch.zeros(2, words, dtype=torch.int64)
-            for si, ids in enumerate((seen_ch0, seen_rest)):
-                for t in ids:
-                    if 0 <= t < AUDIO_VOCAB:
-                        bits[si, t >> 5] |= (1 << (t & 31))
-            seen = bits.to(torch.int32).to(fast.la_static.device)
+        if penalty != 1.0 and seen_bits is None:
+            raise ValueError("repetition penalty needs the history bit sets")
         kernels.sample_rows(fast.la_static, rows, temperature=temperature, top_k=top_k or 0,
-                            top_p=1.0 if top_p is None else top_p, penalty=penalty, seen_bits=seen, seen_set=sets,
+                            top_p=1.0 if top_p is None else top_p, penalty=penalty,
+                            seen_bits=seen_bits if penalty != 1.0 else None, seen_set=sets,
                             excluded=(AUDIO_PAD_CODE,), seed=seed, offset=offset, out=out, scan_rows=scan)
         return rows

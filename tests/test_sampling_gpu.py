@@ -130,3 +130,64 @@ def test_generate_fast_sampled_reproducible():
     assert int(a.audio_frames.max()) <= 1024 and int(a.audio_frames.min()) >= 0
     from moss_tts_lite_b200 import _lib
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("mode,compact", [(0, False), (1, False), (1, True), (2, True), (2, False)])
+def test_feed_row_kernel(mode, compact):
+    """mtl_feed_row against its definition: text by mode, audio by mask
+    (per-channel or compact decisions), pos, and the history bit sets."""
+    dev = require_cuda()
+    from moss_tts_lite_b200 import kernels
+    rng = np.random.default_rng(mode * 2 + compact)
+    for trial in range(4):
+        dec = rng.integers(0, 1025, 33)
+        dec[0] = trial % 2 if mode == 1 else rng.integers(0, 151000)
+        mask = int(rng.integers(0, 1 << 32)) if trial else 0xFFFFFFFF
+        seen0 = rng.integers(0, 1 << 31, (2, 33)).astype(np.int32)
+        ids = torch.zeros(33, dtype=torch.long, device=dev)
+        pos = torch.zeros(1, dtype=torch.long, device=dev)
+        seen = torch.from_numpy(seen0.copy()).to(dev)
+        d = torch.from_numpy(dec).to(dev)
+        for _ in range(2):  # a second identical feed changes nothing
+            kernels.feed_row(d, ids, pos, 77 + trial, text_mode=mode, text_const=151662, gen_slot=151656,
+                             delay_slot=151662, audio_mask=mask, audio_compact=compact, pad_code=1024,
+                             seen_bits=seen)
+        torch.cuda.synchronize()
+        want = [151662 if mode == 0 else ((151656 if dec[0] == 0 else 151662) if mode == 1 else int(dec[0]))]
+        k = 0
+        for j in range(32):
+            if mask >> j & 1:
+                want.append(int(dec[1 + (k if compact else j)]))
+                k += 1
+            else:
+                want.append(1024)
+        assert ids.cpu().tolist() == want
+        assert int(pos[0]) == 77 + trial
+        exp = seen0.view(np.uint32).copy()
+        for j in range(32):
+            t = want[1 + j]
+            exp[0 if j == 0 else 1, t >> 5] |= np.uint32(1 << (t & 31))
+        assert np.array_equal(seen.cpu().numpy().view(np.uint32), exp)
+
+
+def test_generate_fast_pipelined_matches_serial():
+    """Speculative next-step launches (the default) give exactly the tokens of
+    the loop that waits for every step, greedy and sampled, with a repetition
+    penalty (device history bit sets) and a watchdog that fires."""
+    dev = require_cuda()
+    from test_step_gpu import _prompt, _t, _w4_setup
+    from moss_tts_lite_b200.fast import generate_fast
+    fast, m, om = _w4_setup(dev, seed=23, max_seq=160)
+    ids = _t(_prompt(12, seed=8), dev).view(1, 12, 33)
+    for kw in (dict(greedy=True, watchdog=False), dict(seed=5, watchdog=False),
+               dict(seed=6, audio_repetition_penalty=1.3, watchdog_silence_frames=2),
+               dict(seed=7, greedy=True, watchdog_silence_frames=1)):
+        st = {}
+        a = generate_fast(fast, {"input_ids": ids}, max_new_tokens=60, pipelined=True, stats=st, **kw)
+        b = generate_fast(fast, {"input_ids": ids}, max_new_tokens=60, pipelined=False, **kw)
+        assert a.n_steps == b.n_steps, kw
+        assert torch.equal(a.text_ids, b.text_ids) and torch.equal(a.audio_frames, b.audio_frames), kw
+        assert a.watchdog_stats == b.watchdog_stats
+        assert st["launches"] >= a.n_steps and len(st["step_ms"]) == a.n_steps - 1
+    from moss_tts_lite_b200 import _lib
+    assert _lib.device_status() == 0

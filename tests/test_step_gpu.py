@@ -118,7 +118,44 @@ def test_rmsnorm_and_argmax():
     assert int(o1[0]) == 900
 
 
-@pytest.mark.parametrize("s1,rep,streams,stable", [(1, 4, 1, False), (7, 4, 1, True), (64, 4, 1, False),
+@pytest.mark.parametrize("cols", [4096, 155648, 151937])
+def test_argmax_masked_grid_matches_one_cta(cols):
+    """The GPU-wide text argmax (scratch given) equals the one-CTA kernel and
+    numpy's first-index argmax over the non-excluded, non-NaN values, with
+    planted ties, excluded maxima, -0/+0 and NaN, and re-arms its scratch."""
+    dev = require_cuda()
+    from moss_tts_lite_b200 import kernels
+    rng = np.random.default_rng(cols)
+    sc = kernels.argmax_scratch(dev)
+    for trial in range(6):
+        x = f32_to_bf16(rng.standard_normal(cols).astype(np.float32))
+        top = int(rng.integers(0, cols))
+        excl = tuple(int(v) for v in rng.choice(cols, size=trial + 1, replace=False))
+        x[top] = f32_to_bf16(np.array([9.0], np.float32))[0]
+        if trial == 1:
+            x[list(excl)] = 0x7F80                        # excluded +inf never wins
+        if trial == 2:
+            x[cols - 1] = x[top]                           # tie: first index wins
+        if trial == 3:
+            x[:] = 0x8000                                  # all -0 except one +0
+            x[cols // 2] = 0x0000
+        if trial == 4:
+            x[top] = 0x7FC0                                # NaN is skipped
+        ref = bf16_to_f32(x).astype(np.float64)
+        ref[np.isnan(ref)] = -np.inf
+        ref[list(excl)] = -np.inf
+        want = int(np.argmax(ref))
+        xt = _t(x, dev, torch.bfloat16)
+        o1 = torch.empty(1, dtype=torch.long, device=dev)
+        o2 = torch.empty(1, dtype=torch.long, device=dev)
+        kernels.argmax_masked(xt, o1, excl)
+        kernels.argmax_masked(xt, o2, excl, scratch=sc)
+        assert int(o1[0]) == want and int(o2[0]) == want, (trial, int(o1[0]), int(o2[0]), want)
+    torch.cuda.synchronize()
+    assert int(sc.count_nonzero()) == 0
+
+
+@pytest.mark.parametrize("s1,rep,streams,stable",[(1, 4, 1, False), (7, 4, 1, True), (64, 4, 1, False),
                                                      (65, 8, 1, True), (130, 4, 1, False), (641, 4, 2, True),
                                                      (2000, 4, 1, True), (4096, 2, 1, False), (3000, 8, 2, False)])
 def test_attention_decode_vs_oracle(s1, rep, streams, stable):
