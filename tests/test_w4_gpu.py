@@ -77,10 +77,14 @@ def test_gptq_gemv_vs_oracle(K, N, g):
     assert _lib.device_status() == 0
 
 
-@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 13])
-def test_batch_rows(M):
+@pytest.mark.parametrize("M,K,N", [(1, 1024, 512), (2, 1024, 512), (3, 1024, 512), (5, 1024, 512), (8, 1024, 512),
+                                   (9, 1024, 512), (13, 1024, 512), (16, 1024, 512), (21, 1024, 512),
+                                   (16, 4096, 4096), (16, 4096, 6144), (16, 4096, 24576), (12, 12288, 4096)])
+def test_batch_rows(M, K, N):
+    """Batches of 1..21 rows: one launch per 8 rows (the n8 MMA tile), at
+    small shapes and at the decode step's qkv / o / gate|up / down shapes."""
     dev = require_cuda()
-    d, x, W = _gptq_case(1024, 512, 128, seed=3, M=M)
+    d, x, W = _gptq_case(K, N, 128, seed=3, M=M)
     ql = _quantlinear(d, 128, dev)
     y = ql(_t(x, dev, torch.bfloat16))
     _check(_bits(y), ow.linear_f64(x, W))
