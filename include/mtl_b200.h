@@ -225,12 +225,14 @@ int mtl_argmax_masked(const uint16_t* x, int cols, const int32_t* excluded, int 
                       void* scratch, mtl_stream_t stream);
 
 /* Device-side greedy feedback for an audio-phase decode loop with no host
- * round trip: ids_row[1 + j] = argmax of audio row j (bf16 [32, 1025]),
- * ids_row[0] = delay_slot_id if two_logits[1] > two_logits[0] else
- * gen_slot_id (the greedy 2-way decision of fast.py:481-490), pos[0] += 1.
- * No counterpart call in the reference (its loop decides on the host). */
+ * round trip, for `streams` independent streams s (stream s's buffers at
+ * s times the one-stream size): ids_row[s][1 + j] = argmax of its audio row
+ * j (bf16 [32, 1025]), ids_row[s][0] = delay_slot_id if two_logits[s][1] >
+ * two_logits[s][0] else gen_slot_id (the greedy 2-way decision of
+ * fast.py:481-490), pos[s] += 1.  No counterpart call in the reference (its
+ * loop decides on the host). */
 int mtl_greedy_feed(const uint16_t* audio_logits, const uint16_t* two_logits, int64_t* ids_row, int64_t* pos,
-                    int gen_slot_id, int delay_slot_id, mtl_stream_t stream);
+                    int streams, int gen_slot_id, int delay_slot_id, mtl_stream_t stream);
 
 /* Next input row of generate_fast from one step's decisions, on the device
  * (the reference builds current_input_ids from device tensors and copies it

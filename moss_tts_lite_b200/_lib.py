@@ -62,7 +62,7 @@ SIGNATURES = {
     "mtl_feed_row": (_c_int, [_c_void_p, _c_int, ctypes.c_longlong, ctypes.c_longlong, ctypes.c_longlong,
                               ctypes.c_uint, _c_int, ctypes.c_longlong, _c_void_p, _c_void_p, ctypes.c_longlong,
                               _c_void_p, _c_int, _c_void_p]),
-    "mtl_greedy_feed": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p]),
+    "mtl_greedy_feed": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_void_p]),
     "mtl_sample_rows": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int32), _c_float,
                                  _c_int, _c_float, _c_float, _c_void_p, _c_int, ctypes.POINTER(ctypes.c_int32),
                                  ctypes.POINTER(ctypes.c_int32), _c_int, ctypes.POINTER(ctypes.c_int32),

@@ -1,0 +1,147 @@
+"""Batched multi-stream decode: B independent utterances advanced together.
+
+The reference decodes one utterance at a time (batch 1, moss_tts_lite/
+fast.py:272-325); its throughput configuration runs streams one after the
+other.  Here one decode step advances all B streams:
+
+* every W4 projection reads its weights once for the B rows (register-MMA
+  launches of up to 8 rows, the MMA N dimension);
+* attention runs the B streams in one launch, each over its own KV cache
+  (``mtl_attn_decode`` with ``streams = B`` and a per-stream cache stride);
+* the final norm, the two-way text head and the 32 audio heads run on the
+  B rows, and the greedy audio-phase decision (first-index argmax, GEN/DELAY
+  from the two-way logits) writes each stream's next row and position on the
+  device, so a captured step graph replays with no host round trip.
+
+Each stream's prompt is prefilled into its own cache slice with the chunked
+prefill of the batch-1 engine.  Stream s's results equal a batch-1 decode of
+the same stream up to the W4 linears' fp32 summation order (same kernels,
+same split-K plan when the batch fits one launch).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import kernels
+from .model import AUDIO_DELAY_SLOT_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_PAD_CODE, AUDIO_VOCAB, N_VQ, RMS_EPS
+
+_HEAD_ROWS = 4  # rows per bf16 head launch (mtl_bf16_linear)
+
+
+class BatchedFastMossTTS:
+    """``streams`` decode streams over the weights of a FastMossTTS (shared)."""
+
+    def __init__(self, fast, streams: int, max_seq: int | None = None):
+        m = fast.m
+        if streams < 1:
+            raise ValueError("streams must be >= 1")
+        self.fast = fast
+        self.m = m
+        self.B = streams
+        self.max_seq = int(max_seq or m.max_seq_len)
+        if self.max_seq > m.max_seq_len:
+            raise ValueError(f"max_seq {self.max_seq} exceeds the model's RoPE table {m.max_seq_len}")
+        dev, bf = m.device, torch.bfloat16
+        H, D = m.hidden_size, m.head_dim
+        eng = fast.engine
+        self.lins = eng.lins
+        self.emb_audio = eng.emb_audio
+        self.head_audio2d = eng.head_audio2d
+        B = streams
+        # caches: [layer][stream] slices of one allocation per layer
+        self.k_cache = torch.zeros(m.n_layers, B, m.n_kv_heads, self.max_seq, D, dtype=bf, device=dev)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.ids = torch.zeros(B, N_VQ + 1, dtype=torch.long, device=dev)
+        self.pos = torch.zeros(B, dtype=torch.long, device=dev)
+        nq = m.n_heads * D
+        self.h = torch.zeros(B, H, dtype=bf, device=dev)
+        self.qkv = torch.zeros(B, nq + 2 * m.n_kv_heads * D, dtype=bf, device=dev)
+        self.attn = torch.zeros(B, nq, dtype=bf, device=dev)
+        self.act = torch.zeros(B, self.lins[0]["gu"].N // 2, dtype=bf, device=dev)
+        self.h_final = torch.zeros(B, H, dtype=bf, device=dev)
+        self.two = torch.zeros(B, 2, dtype=bf, device=dev)
+        self.la = torch.zeros(B, N_VQ, AUDIO_VOCAB, dtype=bf, device=dev)
+        self.splits = eng.splits
+        from . import _lib
+        self.attn_scratch = torch.zeros(_lib.attn_scratch_bytes(B, m.n_heads, m.n_kv_heads, self.splits),
+                                        dtype=torch.uint8, device=dev)
+        self.kv_stable = False
+        self.graph = None
+        self.seq = [0] * B
+
+    # ---------------------------------------------------------------- prefill
+    def prefill(self, s: int, ids: torch.Tensor) -> torch.Tensor:
+        """Prompt rows [L, 33] of stream ``s`` into its cache; returns the
+        final-normed hidden [L, H] (the batch-1 chunked prefill)."""
+        if not 0 <= s < self.B:
+            raise IndexError(f"stream {s} of {self.B}")
+        ids = ids.reshape(-1, N_VQ + 1).to(device=self.m.device, dtype=torch.long)
+        L = int(ids.shape[0])
+        if L >= self.max_seq:
+            raise ValueError(f"prompt of {L} rows leaves no room in a cache of {self.max_seq}")
+        k = [self.k_cache[li, s] for li in range(self.m.n_layers)]
+        v = [self.v_cache[li, s] for li in range(self.m.n_layers)]
+        out = self.fast.engine.prefill_rows(ids, caches=(k, v))
+        self.seq[s] = L
+        return out
+
+    def start(self, s: int, row: torch.Tensor, pos: int) -> None:
+        """Set stream ``s``'s next input row [33] and its cache position."""
+        self.ids[s].copy_(row.reshape(-1))
+        self.pos[s].fill_(pos)
+
+    # ------------------------------------------------------------------- step
+    def _step(self) -> None:
+        m, B = self.m, self.B
+        kernels.embed_sum(self.ids, m.embed_tokens, self.emb_audio, self.h)
+        stride = m.n_kv_heads * self.max_seq * m.head_dim
+        for li in range(m.n_layers):
+            lyr, L = m.layers[li], self.lins[li]
+            L["qkv"](self.h, self.qkv, norm_weight=lyr["input_layernorm"])
+            kernels.attn_decode(self.qkv, lyr["q_norm"], lyr["k_norm"], m.rope_cos, m.rope_sin,
+                                self.k_cache[li], self.v_cache[li], self.pos, m.n_heads, m.n_kv_heads,
+                                self.splits, self.attn, self.attn_scratch, streams=B, cache_stream_stride=stride,
+                                kv_stable=self.kv_stable)
+            L["o"](self.attn, self.h, residual=self.h)
+            L["gu"](self.h, self.act, norm_weight=lyr["post_attention_layernorm"], swiglu=True)
+            L["down"](self.act, self.h, residual=self.h)
+        la2 = self.la.view(B, N_VQ * AUDIO_VOCAB)
+        for r0 in range(0, B, _HEAD_ROWS):
+            r1 = min(B, r0 + _HEAD_ROWS)
+            kernels.bf16_linear(self.h[r0:r1], m.head_2way, self.two[r0:r1], norm_weight=m.final_norm, eps=RMS_EPS,
+                                x_normed=self.h_final[r0:r1])
+            kernels.bf16_linear(self.h[r0:r1], self.head_audio2d, la2[r0:r1], norm_weight=m.final_norm, eps=RMS_EPS,
+                                pad_period=AUDIO_VOCAB, pad_col=AUDIO_PAD_CODE)
+        kernels.greedy_feed(self.la, self.two, self.ids, self.pos, AUDIO_GEN_SLOT_TOKEN_ID,
+                            AUDIO_DELAY_SLOT_TOKEN_ID, streams=B)
+
+    def step(self) -> None:
+        """One greedy audio-phase step of every stream (graph replay once captured)."""
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._step()
+
+    def capture(self) -> None:
+        """Capture one batched step as a CUDA graph (warm-up launches first)."""
+        if self.graph is not None:
+            return
+        saved = (self.ids.clone(), self.pos.clone())
+        s = torch.cuda.Stream(device=self.m.device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self._step()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        self.kv_stable = True
+        try:
+            with torch.cuda.graph(g, stream=self.fast.capture_stream):
+                self._step()
+        finally:
+            self.kv_stable = False
+        torch.cuda.synchronize()
+        # the warm-up and the capture advanced the streams: restore them
+        self.ids.copy_(saved[0])
+        self.pos.copy_(saved[1])
+        self.graph = g

@@ -26,8 +26,8 @@ cudaError_t launch_argmax_masked(const uint16_t* x, int cols, const int* excl, i
                                  void* scratch, int num_sms, cudaStream_t s, int use_pdl);
 struct FeedArgs;
 cudaError_t launch_feed_row(const FeedArgs& f, cudaStream_t s, int use_pdl);
-cudaError_t launch_greedy_feed(const uint16_t* la, const uint16_t* two, int64_t* ids, int64_t* pos, int gen_slot,
-                               int delay_slot, cudaStream_t s, int use_pdl);
+cudaError_t launch_greedy_feed(const uint16_t* la, const uint16_t* two, int64_t* ids, int64_t* pos, int streams,
+                               int gen_slot, int delay_slot, cudaStream_t s, int use_pdl);
 cudaError_t launch_rmsnorm_rows(const uint16_t* x, int rows, int K, int ldx, const uint16_t* w, float eps,
                                 uint16_t* y, int ldy, cudaStream_t s, int use_pdl);
 cudaError_t launch_sample_rows(const SampleArgs& a, cudaStream_t s);
@@ -448,10 +448,11 @@ int mtl_argmax_masked(const uint16_t* x, int cols, const int32_t* excluded, int 
 }
 
 int mtl_greedy_feed(const uint16_t* audio_logits, const uint16_t* two_logits, int64_t* ids_row, int64_t* pos,
-                    int gen_slot_id, int delay_slot_id, mtl_stream_t stream) {
+                    int streams, int gen_slot_id, int delay_slot_id, mtl_stream_t stream) {
   if (!audio_logits || !two_logits || !ids_row || !pos) return fail(MTL_E_INVALID, "mtl_greedy_feed: NULL pointer");
-  cudaError_t e = mtl::launch_greedy_feed(audio_logits, two_logits, ids_row, pos, gen_slot_id, delay_slot_id, stream,
-                                          use_pdl());
+  if (streams < 1 || streams > 65535) return fail(MTL_E_INVALID, "mtl_greedy_feed: streams=%d", streams);
+  cudaError_t e = mtl::launch_greedy_feed(audio_logits, two_logits, ids_row, pos, streams, gen_slot_id,
+                                          delay_slot_id, stream, use_pdl());
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_greedy_feed");
 }
 

@@ -395,6 +395,11 @@ __global__ void __launch_bounds__(256) argmax_masked_grid_kernel(const uint16_t*
 __global__ void __launch_bounds__(1024) greedy_feed_kernel(const uint16_t* __restrict__ la,
                                                            const uint16_t* __restrict__ two, int64_t* ids,
                                                            int64_t* pos, int gen_slot, int delay_slot) {
+  // one CTA per stream: stream blockIdx.x's logits, row and position
+  la += (size_t)blockIdx.x * kNVQ * kAudioVocab;
+  two += 2 * (size_t)blockIdx.x;
+  ids += (size_t)blockIdx.x * (kNVQ + 1);
+  pos += blockIdx.x;
   pdl_launch_dependents();
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -571,10 +576,10 @@ cudaError_t launch_argmax_masked(const uint16_t* x, int cols, const int* excl, i
   return cudaLaunchKernelEx(&cfg, argmax_masked_kernel, x, cols, ex, out);
 }
 
-cudaError_t launch_greedy_feed(const uint16_t* la, const uint16_t* two, int64_t* ids, int64_t* pos, int gen_slot,
-                               int delay_slot, cudaStream_t s, int use_pdl) {
+cudaError_t launch_greedy_feed(const uint16_t* la, const uint16_t* two, int64_t* ids, int64_t* pos, int streams,
+                               int gen_slot, int delay_slot, cudaStream_t s, int use_pdl) {
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = pdl_cfg(dim3(1), dim3(kNVQ * 32), 0, s, attr, use_pdl);
+  cudaLaunchConfig_t cfg = pdl_cfg(dim3(streams), dim3(kNVQ * 32), 0, s, attr, use_pdl);
   return cudaLaunchKernelEx(&cfg, greedy_feed_kernel, la, two, ids, pos, gen_slot, delay_slot);
 }
 

@@ -205,14 +205,17 @@ class _StepEngine:
                     self._chunk = 4
         return self._chunk
 
-    def prefill_rows(self, ids: torch.Tensor) -> torch.Tensor:
+    def prefill_rows(self, ids: torch.Tensor, caches=None) -> torch.Tensor:
         """Prompt rows [L, 33] -> final-normed hidden [L, H] (fast.py:218-270).
         Rows go through the layers in chunks: the projections of a chunk are
         one batched W4 launch each (the weights are read once per chunk).  The
         chunk's attention is two launches: the K/V append of all its rows,
         then one attention launch with the rows as streams over the shared
-        cache, row r attending over [0, pos_r] (rows of the chunk included)."""
+        cache, row r attending over [0, pos_r] (rows of the chunk included).
+        ``caches`` = (k layers, v layers) selects another stream's KV cache
+        (bf16 [n_kv, max_seq, 128] per layer; default the model's own)."""
         m = self.m
+        kcs, vcs = caches if caches is not None else (m.k_cache, m.v_cache)
         L = ids.shape[0]
         H = m.hidden_size
         C = self._prefill_chunk_rows()
@@ -235,10 +238,10 @@ class _StepEngine:
                 lyr, Lw = m.layers[li], self.lins[li]
                 Lw["qkv"](h, qkv, norm_weight=lyr["input_layernorm"])
                 pos = pos_all[r0:r0 + R]
-                kernels.attn_append(qkv, lyr["k_norm"], m.rope_cos, m.rope_sin, m.k_cache[li], m.v_cache[li],
+                kernels.attn_append(qkv, lyr["k_norm"], m.rope_cos, m.rope_sin, kcs[li], vcs[li],
                                     pos, m.n_heads, m.n_kv_heads, streams=R)
-                kernels.attn_decode(qkv, lyr["q_norm"], lyr["k_norm"], m.rope_cos, m.rope_sin, m.k_cache[li],
-                                    m.v_cache[li], pos, m.n_heads, m.n_kv_heads, self.splits, attn,
+                kernels.attn_decode(qkv, lyr["q_norm"], lyr["k_norm"], m.rope_cos, m.rope_sin, kcs[li],
+                                    vcs[li], pos, m.n_heads, m.n_kv_heads, self.splits, attn,
                                     self._p_scratch, streams=R)
                 Lw["o"](attn, h, residual=h)
                 Lw["gu"](h, act, norm_weight=lyr["post_attention_layernorm"], swiglu=True)

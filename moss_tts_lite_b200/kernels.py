@@ -115,10 +115,10 @@ def feed_row(dec: torch.Tensor, ids_row: torch.Tensor, pos_dev: torch.Tensor, po
 
 
 def greedy_feed(la: torch.Tensor, two: torch.Tensor, ids_row: torch.Tensor, pos_dev: torch.Tensor,
-                gen_slot: int, delay_slot: int) -> None:
-    """Next row and position of a device-side greedy audio-phase loop."""
+                gen_slot: int, delay_slot: int, streams: int = 1) -> None:
+    """Next row and position of a device-side greedy audio-phase loop, per stream."""
     _lib.call("mtl_greedy_feed", la.data_ptr(), two.data_ptr(), ids_row.data_ptr(), pos_dev.data_ptr(),
-              gen_slot, delay_slot, _s())
+              streams, gen_slot, delay_slot, _s())
 
 
 def sample_rows(logits: torch.Tensor, rows, *, temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0,

@@ -1,0 +1,70 @@
+"""Batched multi-stream decode (moss_tts_lite_b200.batched) on the B200.
+
+Every stream of a batched step must give exactly what a batch-1 decode of
+that stream gives with the same kernels: the W4 rows, attention streams and
+head rows are computed independently, so logits, final hidden states and the
+greedily fed next rows are compared bit for bit, over several steps, eager
+and as a replayed CUDA graph."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import require_cuda
+from test_step_gpu import _prompt, _t, _w4_setup
+
+pytestmark = pytest.mark.gpu
+
+GEN, DELAY = 151656, 151662
+
+
+def _batch1_trajectory(fast, prompt, first_row, steps):
+    """Greedy audio-phase steps of one stream through the batch-1 engine."""
+    from moss_tts_lite_b200.model import AUDIO_PAD_CODE
+    L = prompt.shape[0]
+    fast.prefill(prompt.view(1, L, 33))
+    row = first_row.clone()
+    out = []
+    for t in range(steps):
+        fast.ids_row.view(-1).copy_(row)
+        fast.pos_dev.fill_(L + t)
+        fast._run_eager(True)
+        la, two = fast.la_static.clone(), fast.two_static.clone()
+        h = fast.h_final.clone()
+        lf = la.float()
+        assert torch.isinf(lf[:, AUDIO_PAD_CODE]).all()
+        nxt = torch.empty(33, dtype=torch.long, device=la.device)
+        nxt[1:] = torch.argmax(lf, -1)                 # first index on ties, as the kernel
+        nxt[0] = DELAY if float(two[1]) > float(two[0]) else GEN
+        out.append((la, two, h, nxt.clone()))
+        row = nxt
+    return out
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_batched_streams_equal_batch1(graph):
+    dev = require_cuda()
+    from moss_tts_lite_b200.batched import BatchedFastMossTTS
+    fast, m, om = _w4_setup(dev, seed=31, max_seq=128)
+    B, steps = 5, 4
+    prompts = [_t(_prompt(6 + 3 * s, seed=40 + s), dev) for s in range(B)]
+    rng = np.random.default_rng(9)
+    firsts = [_t(np.concatenate([[GEN], rng.integers(0, 1024, 32)]).astype(np.int64), dev) for _ in range(B)]
+    ref = [_batch1_trajectory(fast, prompts[s], firsts[s], steps) for s in range(B)]
+    bt = BatchedFastMossTTS(fast, B, max_seq=128)
+    for s in range(B):
+        bt.prefill(s, prompts[s])
+        bt.start(s, firsts[s], prompts[s].shape[0])
+    if graph:
+        bt.capture()
+    for t in range(steps):
+        bt.step()
+        torch.cuda.synchronize()
+        for s in range(B):
+            la, two, h, nxt = ref[s][t]
+            assert torch.equal(bt.la[s].view(torch.int16), la.view(torch.int16)), (s, t)
+            assert torch.equal(bt.two[s].view(torch.int16), two.view(torch.int16)), (s, t)
+            assert torch.equal(bt.h_final[s].view(torch.int16), h.view(-1).view(torch.int16)), (s, t)
+            assert torch.equal(bt.ids[s], nxt), (s, t)
+            assert int(bt.pos[s]) == prompts[s].shape[0] + t + 1
+    from moss_tts_lite_b200 import _lib
+    assert _lib.device_status() == 0
