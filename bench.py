@@ -280,6 +280,51 @@ def time_cfg3(fast, prompt_len: int = 4096, steps: int = 1024, seed: int = 3):
             "roofline_ms_per_step_at_mean_cache": (3883599872 + 147456 * (prompt_len + n / 2)) / (_peaks()[0] * 1e6)}
 
 
+def time_cfg4(fast, streams: int = 16, prompt_len: int = 256, steps: int = 2048, seed: int = 4):
+    """Configuration 4: ``streams`` independent utterances per GPU, each a
+    seeded random ``prompt_len``-row prompt (last row AUDIO_START) prefilled
+    into its own KV cache, then ``steps`` batched greedy audio-phase decode
+    steps replayed as one CUDA graph per step (every stream advances each
+    step).  Device time by CUDA events; frames/s = streams x steps/s."""
+    import torch
+    from moss_tts_lite_b200.batched import BatchedFastMossTTS
+    from moss_tts_lite_b200.model import AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_START_TOKEN_ID, N_VQ
+    g = torch.Generator().manual_seed(seed)
+    dev = fast.m.device
+    bt = BatchedFastMossTTS(fast, streams, max_seq=prompt_len + steps + 8)
+    t0 = time.perf_counter()
+    for s in range(streams):
+        ids = torch.zeros(prompt_len, N_VQ + 1, dtype=torch.long)
+        ids[:, 0] = torch.randint(0, 151643, (prompt_len,), generator=g)
+        ids[:, 1:] = torch.randint(0, 1024, (prompt_len, N_VQ), generator=g)
+        ids[-1, 0] = AUDIO_START_TOKEN_ID
+        bt.prefill(s, ids.to(dev))
+        first = torch.cat([torch.tensor([AUDIO_GEN_SLOT_TOKEN_ID]), torch.randint(0, 1024, (N_VQ,), generator=g)])
+        bt.start(s, first.to(dev), prompt_len)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    bt.capture()
+    for _ in range(3):      # warm-up steps advance the streams like timed ones
+        bt.step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = steps - 3
+    e0.record()
+    for _ in range(n):
+        bt.step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    out = {"workload": f"cfg4: {streams} streams x {prompt_len}-row prompts (chunked W4 prefill per stream), "
+                       f"{steps} batched greedy audio-phase steps, one graph per step",
+           "streams": streams, "steps": steps, "device_ms_per_step": ms, "steps_per_s": 1e3 / ms,
+           "frames_per_s": streams * 1e3 / ms, "prefill_s": prefill_s,
+           "cache": f"{prompt_len + 1}..{prompt_len + steps} per stream"}
+    del bt
+    torch.cuda.empty_cache()
+    return out
+
+
 class CpuStep:
     """The numpy oracle decode step on the host cores, bounded sample: 2 of
     the 36 layers at the cfg2 shapes (fp32 BLAS on precomputed effective
@@ -576,6 +621,7 @@ def main():
     ap.add_argument("--impl", default="mtl", choices=["mtl", "reference", "reference-gpu"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cfg3", action="store_true", help="skip the long-context sampled configuration-3 run")
+    ap.add_argument("--no-cfg4", action="store_true", help="skip the 16-stream batched configuration-4 run")
     ap.add_argument("--profile-gemv", action="store_true", help="small config-0 GEMV case for ncu")
     ap.add_argument("--profile-attn", action="store_true", help="decode attention alone (config 2 heads)")
     ap.add_argument("--profile-attn-launches", action="store_true", help="4 plain attention launches (ncu case)")
@@ -618,6 +664,9 @@ def main():
     cfg3 = None
     if ctx.rank == 0 and args.gpus == 1 and not args.no_cfg3:
         cfg3 = time_cfg3(fast)
+    cfg4 = None
+    if ctx.rank == 0 and args.gpus == 1 and not args.no_cfg4:
+        cfg4 = time_cfg4(fast)
     cpu = None
     if ctx.rank == 0 and args.gpus == 1 and not args.no_cpu_baseline:
         v, cores, sample = cpu_baseline()
@@ -658,6 +707,8 @@ def main():
             line["cpu_baseline"] = cpu
         if cfg3 is not None:
             line["cfg3"] = cfg3
+        if cfg4 is not None:
+            line["cfg4"] = cfg4
         print(json.dumps(line), flush=True)
     ctx.barrier()
     del fast
