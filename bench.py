@@ -488,6 +488,61 @@ def profile_gemv(launches: int = 6):
         raise SystemExit(1)
 
 
+def profile_heads(launches: int = 3):
+    """Small case for ncu: the text-phase head of configuration 2 alone, the
+    final RMSNorm fused into the bf16 GEMV over the [151936, 4096] text head
+    (1.245 GB, > L2; seeded synthetic weights), `launches` launches."""
+    import torch
+    from moss_tts_lite_b200 import _lib, kernels
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    H, V = CFG["hidden"], CFG["vocab"]
+    W = (torch.randn(V, H, generator=g, device=dev) * CFG["std"]).to(torch.bfloat16)
+    nw = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    h = torch.randn(1, H, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty(1, V, dtype=torch.bfloat16, device=dev)
+    hn = torch.empty(1, H, dtype=torch.bfloat16, device=dev)
+    for _ in range(launches):
+        kernels.bf16_linear(h, W, out, norm_weight=nw, eps=1e-6, x_normed=hn)
+    torch.cuda.synchronize()
+    st = _lib.device_status()
+    print(json.dumps({"profile": "bf16_gemv text head", "launches": launches, "bytes_per_launch": V * H * 2 + 4 * H
+                      + 2 * V, "device_status": st}))
+    if st != 0:
+        raise SystemExit(1)
+
+
+def profile_cfg4(steps: int = 2):
+    """Configuration 4's batched step (16 streams, 256-row prompts) with
+    `steps` graph replays inside the NVTX range `mtl_timed` (the ncu launch-
+    list case)."""
+    import torch
+    from moss_tts_lite_b200.batched import BatchedFastMossTTS
+    from moss_tts_lite_b200.model import AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_START_TOKEN_ID, N_VQ
+    dev = torch.device("cuda", 0)
+    fast = build_fast(dev, seed=CFG["seed"])
+    g = torch.Generator().manual_seed(4)
+    bt = BatchedFastMossTTS(fast, 16, max_seq=512)
+    for s in range(16):
+        ids = torch.zeros(256, N_VQ + 1, dtype=torch.long)
+        ids[:, 0] = torch.randint(0, 151643, (256,), generator=g)
+        ids[:, 1:] = torch.randint(0, 1024, (256, N_VQ), generator=g)
+        ids[-1, 0] = AUDIO_START_TOKEN_ID
+        bt.prefill(s, ids.to(dev))
+        first = torch.cat([torch.tensor([AUDIO_GEN_SLOT_TOKEN_ID]), torch.randint(0, 1024, (N_VQ,), generator=g)])
+        bt.start(s, first.to(dev), 256)
+    bt.capture()
+    for _ in range(3):
+        bt.step()
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("mtl_timed")
+    for _ in range(steps):
+        bt.step()
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    print(json.dumps({"profile": "cfg4 batched step", "steps": steps}))
+
+
 def profile_attn(timed: bool = True, launches: int = 4, lengths=(136, 1024, 4096, 8191)):
     """Decode attention of configuration 2 alone (32 query / 8 KV heads x 128,
     KV cache [8, 8192, 128] for one layer, seeded synthetic values): per cache
@@ -625,7 +680,15 @@ def main():
     ap.add_argument("--profile-gemv", action="store_true", help="small config-0 GEMV case for ncu")
     ap.add_argument("--profile-attn", action="store_true", help="decode attention alone (config 2 heads)")
     ap.add_argument("--profile-attn-launches", action="store_true", help="4 plain attention launches (ncu case)")
+    ap.add_argument("--profile-heads", action="store_true", help="text-head bf16 GEMV alone (ncu case)")
+    ap.add_argument("--profile-cfg4", action="store_true", help="2 batched configuration-4 steps in an NVTX range")
     args = ap.parse_args()
+    if args.profile_heads:
+        profile_heads()
+        return
+    if args.profile_cfg4:
+        profile_cfg4()
+        return
     if args.profile_gemv:
         profile_gemv()
         return
