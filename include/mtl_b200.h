@@ -91,6 +91,14 @@ int mtl_w4_pack_tc(const uint8_t* q, const uint16_t* qsz, int K, int N, int grou
 int mtl_w4_pack_gptq(const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
                      const int32_t* perm, int K, int N, int group_size, void* tiles, mtl_stream_t stream);
 
+/* Effective weights of packed tiles as bf16 w [N, K] row-major: REF
+ * (q - 8) * scale + zero (gptq.py:87-97 effective_weight), GPTQ
+ * (q - (z + zero_offset)) * scale, computed in fp32, rounded to bf16 — the
+ * operand of the prompt-prefill GEMMs (many rows per pass over a layer),
+ * where the reference runs tinygemm with M = prompt length (fast.py:218-270). */
+int mtl_w4_dequant(const void* tiles, int K, int N, int group_size, int param_fmt, int zero_offset, uint16_t* w,
+                   mtl_stream_t stream);
+
 /* Inverse of the packers for the codes: codes uint8 [N, K] (row n = output
  * column; packed row order, i.e. after any perm). */
 int mtl_w4_unpack_codes(const void* tiles, int K, int N, int group_size, int param_fmt, uint8_t* codes,

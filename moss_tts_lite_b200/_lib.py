@@ -40,6 +40,7 @@ SIGNATURES = {
     "mtl_w4_pack_tc": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
     "mtl_w4_pack_gptq": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_int,
                                   _c_void_p, _c_void_p]),
+    "mtl_w4_dequant": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
     "mtl_w4_unpack_codes": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
     "mtl_w4a16_linear": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p,
                                   _c_int, _c_void_p, _c_void_p, _c_float, _c_int, _c_void_p, _c_void_p,

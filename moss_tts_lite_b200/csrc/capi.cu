@@ -232,6 +232,18 @@ int mtl_w4_unpack_codes(const void* tiles, int K, int N, int group_size, int par
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4_unpack_codes");
 }
 
+int mtl_w4_dequant(const void* tiles, int K, int N, int group_size, int param_fmt, int zero_offset, uint16_t* w,
+                   mtl_stream_t stream) {
+  if (int r = check_w4_shape(K, N, group_size, param_fmt)) return r;
+  if (param_fmt == MTL_FMT_TC) return fail(MTL_E_UNSUPPORTED, "mtl_w4_dequant: MTL_FMT_TC tiles");
+  if (!tiles || !w) return fail(MTL_E_INVALID, "mtl_w4_dequant: NULL pointer");
+  if (!aligned(tiles, 16) || !aligned(w, 4)) return fail(MTL_E_ALIGN, "mtl_w4_dequant: misaligned tiles / w");
+  if (zero_offset < 0 || zero_offset > 1) return fail(MTL_E_INVALID, "zero_offset must be 0 or 1");
+  cudaError_t e = mtl::w4_dequant(static_cast<const uint8_t*>(tiles), K, N, group_size, param_fmt, zero_offset, w,
+                                  stream);
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4_dequant");
+}
+
 int mtl_w4a16_linear(const uint16_t* x, int ldx, int M, int K, int N, int group_size, int param_fmt,
                      const void* tiles, int zero_offset, const int32_t* k_perm, const uint16_t* norm_w,
                      float norm_eps, int epilogue, const uint16_t* residual, uint16_t* y, int ldy, void* scratch,

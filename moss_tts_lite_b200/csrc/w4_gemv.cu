@@ -690,6 +690,46 @@ __global__ void unpack_codes_kernel(const uint8_t* tiles, int K, int N, int g, i
   }
 }
 
+// Effective bf16 weights W[n][k] from the tiles (the prefill GEMM operand):
+// REF  w = (q - 8) * scale + zero            (gptq.py:87-97)
+// GPTQ w = (q - (z + zero_offset)) * scale    (AutoGPTQ)
+// computed in fp32 and rounded to bf16; two consecutive k per thread.
+template <int FMT>
+__global__ void dequant_kernel(const uint8_t* tiles, int K, int N, int g, int tile_bytes, int zero_offset,
+                               uint16_t* w) {
+  const int KT = K / g;
+  const long long total = (long long)N * K / 2;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(idx / (K / 2)), k = (int)(idx % (K / 2)) * 2;
+    const int nb = n / kNT, c = n % kNT, G = k / g, kin = k % g;
+    const int j = c / 16, rr = c % 16, gr = rr & 7, hi_row = rr >> 3;
+    const int ks = kin / 16, k16 = kin % 16;
+    const int hi_k = k16 >= 8 ? 1 : 0;
+    const int tq = (k16 & 7) >> 1;
+    const int lane = gr * 4 + tq;
+    const int slot = (hi_row ? 1 : 0) + (hi_k ? 2 : 0);  // even k; k + 1 is slot + 4
+    const uint8_t* tile = tiles + ((long long)nb * KT + G) * tile_bytes;
+    const uint32_t wd = reinterpret_cast<const uint32_t*>(tile)[(ks * 32 + lane) * 4 + j];
+    const float q0 = (float)((wd >> (4 * slot)) & 0xFu), q1 = (float)((wd >> (4 * (slot + 4))) & 0xFu);
+    const uint8_t* prm = tile + kNT * g / 2;
+    float v0, v1;
+    if (FMT == kFmtRef) {
+      const uint32_t pw = reinterpret_cast<const uint32_t*>(prm)[c];
+      const float sc = __uint_as_float(pw << 16), ze = __uint_as_float(pw & 0xFFFF0000u);
+      v0 = fmaf(q0 - 8.f, sc, ze);
+      v1 = fmaf(q1 - 8.f, sc, ze);
+    } else {
+      const float sc = __half2float(reinterpret_cast<const __half*>(prm)[c]);
+      const uint32_t zw = reinterpret_cast<const uint32_t*>(prm + 128)[c >> 3];
+      const float z = (float)((int)((zw >> (4 * (c & 7))) & 0xFu) + zero_offset);
+      v0 = (q0 - z) * sc;
+      v1 = (q1 - z) * sc;
+    }
+    reinterpret_cast<uint32_t*>(w)[idx] = (uint32_t)f32_to_bf16_bits(v0) | ((uint32_t)f32_to_bf16_bits(v1) << 16);
+  }
+}
+
 inline int grid_for(long long work) {
   long long b = (work + 255) / 256;
   return (int)std::max<long long>(1, std::min<long long>(b, 148LL * 32));
@@ -714,6 +754,16 @@ cudaError_t w4_pack_ref(const uint8_t* q, const uint16_t* qsz, int K, int N, int
   long long words = (long long)(N / kNT) * (K / g) * (g / 16) * 128;
   pack_words_kernel<<<grid_for(words), 256, 0, s>>>(src, K, N, g, tb, tiles);
   pack_params_ref_kernel<<<grid_for((long long)N * (K / g)), 256, 0, s>>>(qsz, K, N, g, tb, tiles);
+  return cudaGetLastError();
+}
+
+cudaError_t w4_dequant(const uint8_t* tiles, int K, int N, int g, int fmt, int zero_offset, uint16_t* w,
+                       cudaStream_t s) {
+  const long long pairs = (long long)N * K / 2;
+  if (fmt == kFmtRef)
+    dequant_kernel<kFmtRef><<<grid_for(pairs), 256, 0, s>>>(tiles, K, N, g, tile_bytes(g, fmt), zero_offset, w);
+  else
+    dequant_kernel<kFmtGptq><<<grid_for(pairs), 256, 0, s>>>(tiles, K, N, g, tile_bytes(g, fmt), zero_offset, w);
   return cudaGetLastError();
 }
 

@@ -74,6 +74,10 @@ struct W4Args {
 // Host planning (grid, ring depth, shared memory, scratch) for one shape.
 int w4_plan(int M, int K, int N, int g, int fmt, int num_sms, W4Plan* out);
 
+// Effective bf16 weights [N, K] row-major from the tiles (REF or GPTQ).
+cudaError_t w4_dequant(const uint8_t* tiles, int K, int N, int g, int fmt, int zero_offset, uint16_t* w,
+                       cudaStream_t s);
+
 // Launch on `stream` (programmatic dependent launch when use_pdl != 0).
 cudaError_t w4_launch(const W4Args& a, int fmt, cudaStream_t stream, int use_pdl);
 

@@ -21,6 +21,7 @@ import time
 from dataclasses import dataclass, field
 
 import torch
+import torch.nn.functional as F
 
 from . import _lib, fsm, kernels
 from .generate import GenResult
@@ -32,6 +33,7 @@ from .quant import W4Weight
 _INT64_MAX = 9223372036854775807
 _LIN_NAMES = LIN_NAMES
 _FUSE_BLOCK = 32  # gate/up interleave granularity of the register-MMA tiles' SwiGLU epilogue
+_GEMM_PREFILL_ROWS = 32  # prompts from this many rows prefill through dequantised bf16 GEMMs
 
 
 # ------------------------------------------------------------------ linears
@@ -217,6 +219,10 @@ class _StepEngine:
         m = self.m
         kcs, vcs = caches if caches is not None else (m.k_cache, m.v_cache)
         L = ids.shape[0]
+        if L >= _GEMM_PREFILL_ROWS and all(isinstance(self.lins[0][n], _W4Lin) and self.lins[0][n].w.fmt !=
+                                          _lib.MTL_FMT_TC and self.lins[0][n].w.k_perm is None
+                                          for n in ("qkv", "o", "gu", "down")):
+            return self._prefill_gemm(ids, kcs, vcs)
         H = m.hidden_size
         C = self._prefill_chunk_rows()
         dev = m.device
@@ -247,6 +253,57 @@ class _StepEngine:
                 Lw["gu"](h, act, norm_weight=lyr["post_attention_layernorm"], swiglu=True)
                 Lw["down"](act, h, residual=h)
             kernels.rmsnorm(h, m.final_norm, out[r0:r0 + R], RMS_EPS)
+        return out
+
+    def _prefill_gemm(self, ids: torch.Tensor, kcs, vcs) -> torch.Tensor:
+        """A long prompt, layer by layer over all its rows (fast.py:218-270,
+        where the reference runs each projection as one tinygemm call with
+        M = L): each projection is one bf16 GEMM (cuBLAS through
+        torch.matmul) on the layer's effective weights, dequantised from the
+        W4 tiles just before (``mtl_w4_dequant``); the K/V append of all rows
+        is one launch and the attention runs the rows as streams over the
+        shared cache (row r over [0, r]) in launches of 512 rows.  The
+        residual adds and SwiGLU are the reference's bf16 tensor ops."""
+        m = self.m
+        L = ids.shape[0]
+        H, D = m.hidden_size, m.head_dim
+        dev, bf = m.device, torch.bfloat16
+        nq = m.n_heads * D
+        A = 512
+        if getattr(self, "_g_scratch", None) is None:
+            self._g_scratch = torch.zeros(_lib.attn_scratch_bytes(A, m.n_heads, m.n_kv_heads, self.splits),
+                                          dtype=torch.uint8, device=dev)
+            big = max(Lw[n].w.N * Lw[n].w.K for Lw in self.lins[:1] for n in ("qkv", "o", "gu", "down"))
+            self._g_wbuf = torch.empty(big, dtype=bf, device=dev)
+
+        def weight(lin):
+            w = lin.w
+            return w.dequant(self._g_wbuf[:w.N * w.K].view(w.N, w.K))
+        h = torch.empty(L, H, dtype=bf, device=dev)
+        xn = torch.empty(L, H, dtype=bf, device=dev)
+        attn = torch.empty(L, nq, dtype=bf, device=dev)
+        pos = torch.arange(L, dtype=torch.long, device=dev)
+        kernels.embed_sum(ids.contiguous(), m.embed_tokens, self.emb_audio, h)
+        for li in range(m.n_layers):
+            lyr, Lw = m.layers[li], self.lins[li]
+            kernels.rmsnorm(h, lyr["input_layernorm"], xn, RMS_EPS)
+            qkv = torch.matmul(xn, weight(Lw["qkv"]).t())
+            kernels.attn_append(qkv, lyr["k_norm"], m.rope_cos, m.rope_sin, kcs[li], vcs[li], pos, m.n_heads,
+                                m.n_kv_heads, streams=L)
+            for r0 in range(0, L, A):
+                r1 = min(L, r0 + A)
+                kernels.attn_decode(qkv[r0:r1], lyr["q_norm"], lyr["k_norm"], m.rope_cos, m.rope_sin, kcs[li],
+                                    vcs[li], pos[r0:r1], m.n_heads, m.n_kv_heads, self.splits, attn[r0:r1],
+                                    self._g_scratch, streams=r1 - r0)
+            h = h + torch.matmul(attn, weight(Lw["o"]).t())                 # fast.py:168
+            kernels.rmsnorm(h, lyr["post_attention_layernorm"], xn, RMS_EPS)
+            gu = torch.matmul(xn, weight(Lw["gu"]).t())
+            fb = Lw["gu"].fuse_block                                         # gate|up interleaved per block
+            gu = gu.view(L, -1, 2, fb)
+            act = (F.silu(gu[:, :, 0]) * gu[:, :, 1]).reshape(L, -1)         # fast.py:170-171
+            h = h + torch.matmul(act, weight(Lw["down"]).t())                # fast.py:170
+        out = torch.empty(L, H, dtype=bf, device=dev)
+        kernels.rmsnorm(h, m.final_norm, out, RMS_EPS)
         return out
 
 

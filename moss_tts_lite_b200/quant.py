@@ -82,6 +82,15 @@ class W4Weight:
                   self.fmt, out.data_ptr(), _stream())
         return out
 
+    def dequant(self, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Effective weights bf16 [N, K] in packed column order (k_perm order
+        for act-order AutoGPTQ weights), as the operand of a many-row GEMM."""
+        if out is None:
+            out = torch.empty(self.N, self.K, dtype=torch.bfloat16, device=self.tiles.device)
+        _lib.call("mtl_w4_dequant", self.tiles.data_ptr(), self.K, self.N, self.group_size, self.fmt,
+                  self.zero_offset, out.data_ptr(), _stream())
+        return out
+
     def linear(self, x: torch.Tensor, *, out: torch.Tensor | None = None,
                residual: torch.Tensor | None = None, norm_weight: torch.Tensor | None = None,
                norm_eps: float = 1e-6, swiglu: bool = False) -> torch.Tensor:

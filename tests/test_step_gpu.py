@@ -358,6 +358,50 @@ def test_w4_fast_step_graph_vs_eager_and_oracle():
     assert _lib.device_status() == 0
 
 
+def test_w4_prefill_gemm_vs_chunked_and_oracle():
+    """A 40-row prompt prefills through dequantised bf16 GEMMs (all rows per
+    projection); the final hidden rows and the K/V cache agree with the
+    chunked W4 prefill and with the oracle to within bf16 noise, and the
+    decode steps that follow match the oracle (teacher-forced cover)."""
+    dev = require_cuda()
+    import moss_tts_lite_b200.fast as fm
+    fast, m, om = _w4_setup(dev, seed=29, max_seq=128)
+    ids = _prompt(40, seed=31)
+    h_gemm = fast.prefill(_t(ids, dev).view(1, 40, 33)).last_hidden[0].clone()
+    kc_gemm = m.k_cache[:, :, :40].clone()
+    saved = fm._GEMM_PREFILL_ROWS
+    fm._GEMM_PREFILL_ROWS = 10 ** 9
+    try:
+        h_chunk = fast.prefill(_t(ids, dev).view(1, 40, 33)).last_hidden[0].clone()
+        kc_chunk = m.k_cache[:, :, :40].clone()
+    finally:
+        fm._GEMM_PREFILL_ROWS = saved
+    ho = om.prefill(ids)
+    a, b, o = bf16_to_f32(_bits(h_gemm)), bf16_to_f32(_bits(h_chunk)), bf16_to_f32(ho.reshape(40, -1))
+    scale = np.abs(o).max()
+    assert np.abs(a - b).max() < 0.05 * scale, np.abs(a - b).max()
+    assert np.abs(a - o).max() < 0.05 * scale, np.abs(a - o).max()
+    kg, kk = bf16_to_f32(_bits(kc_gemm)), bf16_to_f32(_bits(kc_chunk))
+    kd = np.abs(kg - kk)
+    # bf16 noise: normed + rotated keys differ by about one ulp in part of the elements
+    assert kd.max() < 0.1 * np.abs(kk).max() and kd.mean() < 0.02 * np.abs(kk).mean()
+    # decode after the GEMM prefill
+    fast.prefill(_t(ids, dev).view(1, 40, 33))
+    fast.capture()
+    rng = np.random.default_rng(6)
+    cover = []
+    for t in range(3):
+        row = np.concatenate([[ost.AUDIO_GEN_SLOT_TOKEN_ID], rng.integers(0, 1024, 32)]).astype(np.int64)
+        lt, la, hh, two = fast.step(_t(row, dev).view(1, 33), 40 + t, audio2=True)
+        hs = om.step(row)
+        lo = bf16_to_f32(om.audio_logits(hs))
+        am = np.argmax(bf16_to_f32(_bits(la)), -1)
+        cover.append((lo[np.arange(32), am] >= lo.max(-1) - 0.05).mean())
+    assert np.mean(cover) > 0.95, cover
+    from moss_tts_lite_b200 import _lib
+    assert _lib.device_status() == 0
+
+
 def test_w4_format_matches_reference_codes():
     """G1-style: the W4 codes this package packs are the reference's RTN codes."""
     dev = require_cuda()

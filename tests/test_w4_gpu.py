@@ -242,3 +242,18 @@ def test_back_to_back_same_scratch(K, N, M):
     zb = (N // 64 * 4 + 255) // 256 * 256   # split-K counters
     assert int(lin.w.scratch[:zb].count_nonzero()) == 0
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("K,N,g", [(4096, 1024, 128), (1024, 192, 64), (512, 128, 32)])
+def test_dequant_effective_weights(K, N, g):
+    """mtl_w4_dequant: the reference's effective_weight (q - 8) * scale + zero
+    (gptq.py:87-97) rounded to bf16, for every element (one fp32 FMA: equal to
+    the oracle's multiply-then-add except rare 1-ulp bf16 roundings)."""
+    dev = require_cuda()
+    from moss_tts_lite_b200.quant import RefW4Linear
+    q, qsz, Wnk = _ref_case(K, N, g, seed=K + N + g)
+    lin = RefW4Linear(_t(q, dev), _t(qsz, dev, torch.bfloat16), g)
+    got = _bits(lin.w.dequant())
+    want = f32_to_bf16(Wnk.astype(np.float32))
+    diff = np.abs(got.astype(np.int32) - want.astype(np.int32))
+    assert diff.max() <= 1 and (diff == 0).mean() > 0.999
