@@ -257,3 +257,24 @@ def test_dequant_effective_weights(K, N, g):
     want = f32_to_bf16(Wnk.astype(np.float32))
     diff = np.abs(got.astype(np.int32) - want.astype(np.int32))
     assert diff.max() <= 1 and (diff == 0).mean() > 0.999
+
+
+@pytest.mark.parametrize("M", [1, 3])
+def test_activation_range_beyond_fp16(M):
+    """Activation groups with |x| up to 1e6 (past fp16's 65504) and down to
+    1e-8 (below fp16's normal range) meet the same tolerance against the fp64
+    product as ordinary ones (bf16 staging covers the range; an fp16-staged
+    variant with per-group power-of-two scaling failed this case)."""
+    dev = require_cuda()
+    from moss_tts_lite_b200.quant import RefW4Linear
+    K, N, g = 4096, 1024, 128
+    q, qsz, Wnk = _ref_case(K, N, g, seed=77)
+    lin = RefW4Linear(_t(q, dev), _t(qsz, dev, torch.bfloat16), g)
+    rng = np.random.default_rng(78)
+    mags = np.array([1e6, 3e4, 1.0, 1e-3, 1e-8, 7e4, 0.01, 200.0])
+    xf = rng.standard_normal((M, K)) * np.repeat(np.resize(mags, K // g), g)[None, :]
+    x = f32_to_bf16(xf.astype(np.float32))
+    y = lin(_t(x, dev, torch.bfloat16))
+    torch.cuda.synchronize()
+    assert np.isfinite(bf16_to_f32(_bits(y))).all()
+    _check(_bits(y), ow.linear_f64(x, Wnk.T))
