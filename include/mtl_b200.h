@@ -189,11 +189,14 @@ int mtl_attn_decode(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_
  * pos[s] (fast.py:138-146).  With cache_stream_stride = 0 all rows share one
  * cache: a prefill chunk appends its rows first, then one mtl_attn_decode
  * call with the same rows as streams (cache_stream_stride 0) attends each
- * row over [0, pos[s]] (it re-writes the same K/V values).  No reference
- * counterpart of its own: the reference appends inside _p_pre. */
-int mtl_attn_append(const uint16_t* qkv, const uint16_t* k_norm_w, const uint16_t* rope_cos,
+ * row over [0, pos[s]] (it re-writes the same K/V values).  q_out (nullable,
+ * bf16 [streams, n_heads, 128]) also receives the rows' q heads after their
+ * RMSNorm (q_norm_w) and RoPE, the q operand of a prefill attention over
+ * many rows (fast.py:229-235).  No reference counterpart of its own: the
+ * reference does this inside _p_pre and _layer_q. */
+int mtl_attn_append(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_t* k_norm_w, const uint16_t* rope_cos,
                     const uint16_t* rope_sin, uint16_t* k_cache, uint16_t* v_cache, long long cache_stream_stride,
-                    int max_seq, const int64_t* pos, int streams, int n_heads, int n_kv, int head_dim,
+                    int max_seq, const int64_t* pos, int streams, int n_heads, int n_kv, int head_dim, uint16_t* q_out,
                     mtl_stream_t stream);
 
 /* y = epilogue(x . W^T) for bf16 weights W [N, K] (the lm heads,

@@ -53,8 +53,9 @@ SIGNATURES = {
     "mtl_attn_decode": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                  ctypes.c_longlong, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int,
                                  _c_int, _c_void_p, _c_void_p, _c_size_t, _c_void_p]),
-    "mtl_attn_append": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
-                                 ctypes.c_longlong, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_void_p]),
+    "mtl_attn_append": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                 ctypes.c_longlong, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_void_p,
+                                 _c_void_p]),
     "mtl_bf16_linear": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_float, _c_void_p,
                                  _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_int, _c_void_p]),
     "mtl_argmax_rows": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),

@@ -469,10 +469,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
 // K/V append alone (the `_p_pre` tail, fast.py:138-146): k head RMSNorm +
 // RoPE at pos[s] and v, written to cache rows pos[s] of every KV head, for
-// `streams` rows at once.  Prefill runs it for a chunk of prompt rows before
-// their attention (which re-writes the same values), so that row r can attend
-// to rows < r of the same chunk.  Grid (n_kv, streams), 128 threads: warp 0
-// does k, warp 1 v.
+// `streams` rows at once; with a.out set, also the rows' q heads normed and
+// rotated into a.out ([streams, nh, 128], the operand of a prefill attention
+// over many rows, fast.py:229-235).  Prefill runs it for prompt rows before
+// their attention (the decode attention re-writes the same K/V values).
+// Grid (n_kv, streams), 128 threads: warp 0 k, warp 1 v, warps 2-3 the
+// group's q heads.
+__device__ __forceinline__ void norm_rope_row(const uint16_t* src, const uint16_t* w, const uint16_t* cosr,
+                                              const uint16_t* sinr, uint16_t* dst, int lane) {
+  float x[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) x[j] = bf16_bits_to_f32(src[lane + 32 * j]);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) ss = fmaf(x[j], x[j], ss);
+  ss = warp_sum(ss);
+  const float rinv = rsqrtf(ss / (float)kHeadDim + 1e-6f);
+  float xn[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) xn[j] = round_bf16(bf16_bits_to_f32(w[lane + 32 * j]) * round_bf16(x[j] * rinv));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int d = lane + 32 * j;
+    const float rot = j < 2 ? -xn[j + 2] : xn[j - 2];
+    const float t1 = round_bf16(xn[j] * bf16_bits_to_f32(cosr[d]));
+    const float t2 = round_bf16(rot * bf16_bits_to_f32(sinr[d]));
+    dst[d] = f32_to_bf16_bits(t1 + t2);
+  }
+}
+
 __global__ void __launch_bounds__(kAttnThreads) attn_append_kernel(const AttnArgs a) {
   const int h = blockIdx.x, st = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -484,36 +509,28 @@ __global__ void __launch_bounds__(kAttnThreads) attn_append_kernel(const AttnArg
     return;
   }
   const int pos = (int)p64;
-  if (warp > 1) return;
   const uint16_t* qkv = a.qkv + (size_t)st * (a.nh + 2 * a.nkv) * kHeadDim;
+  const uint16_t* cosr = a.rope_cos + (size_t)pos * kHeadDim;
+  const uint16_t* sinr = a.rope_sin + (size_t)pos * kHeadDim;
+  if (warp >= 2) {
+    if (!a.out) return;
+    const int rep = a.nh / a.nkv;
+    for (int r = warp - 2; r < rep; r += 2) {
+      const int qh = h * rep + r;
+      norm_rope_row(qkv + (size_t)qh * kHeadDim, a.q_norm_w, cosr, sinr,
+                    a.out + ((size_t)st * a.nh + qh) * kHeadDim, lane);
+    }
+    return;
+  }
   uint16_t* dst = (warp == 0 ? a.k_cache : a.v_cache) + st * a.cache_stream_stride +
                   ((size_t)h * a.max_seq + pos) * kHeadDim;
   const uint16_t* src = qkv + (size_t)((warp == 0 ? a.nh : a.nh + a.nkv) + h) * kHeadDim;
-  float x[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) x[j] = bf16_bits_to_f32(src[lane + 32 * j]);
   if (warp == 1) {  // v is used as is (fast.py:137,140)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) dst[lane + 32 * j] = f32_to_bf16_bits(x[j]);
+    for (int j = 0; j < 4; ++j) dst[lane + 32 * j] = src[lane + 32 * j];
     return;
   }
-  float ss = 0.f;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) ss = fmaf(x[j], x[j], ss);
-  ss = warp_sum(ss);
-  const float rinv = rsqrtf(ss / (float)kHeadDim + 1e-6f);
-  float xn[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-    xn[j] = round_bf16(bf16_bits_to_f32(a.k_norm_w[lane + 32 * j]) * round_bf16(x[j] * rinv));
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int d = lane + 32 * j;
-    const float rot = j < 2 ? -xn[j + 2] : xn[j - 2];
-    const float t1 = round_bf16(xn[j] * bf16_bits_to_f32(a.rope_cos[(size_t)pos * kHeadDim + d]));
-    const float t2 = round_bf16(rot * bf16_bits_to_f32(a.rope_sin[(size_t)pos * kHeadDim + d]));
-    dst[d] = f32_to_bf16_bits(t1 + t2);
-  }
+  norm_rope_row(src, a.k_norm_w, cosr, sinr, dst, lane);
 }
 
 // ------------------------------------------------------------------- host

@@ -387,11 +387,11 @@ int mtl_attn_decode(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_attn_decode");
 }
 
-int mtl_attn_append(const uint16_t* qkv, const uint16_t* k_norm_w, const uint16_t* rope_cos,
+int mtl_attn_append(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_t* k_norm_w, const uint16_t* rope_cos,
                     const uint16_t* rope_sin, uint16_t* k_cache, uint16_t* v_cache, long long cache_stream_stride,
-                    int max_seq, const int64_t* pos, int streams, int n_heads, int n_kv, int head_dim,
+                    int max_seq, const int64_t* pos, int streams, int n_heads, int n_kv, int head_dim, uint16_t* q_out,
                     mtl_stream_t stream) {
-  if (!qkv || !k_norm_w || !rope_cos || !rope_sin || !k_cache || !v_cache || !pos)
+  if (!qkv || !k_norm_w || !rope_cos || !rope_sin || !k_cache || !v_cache || !pos || (q_out && !q_norm_w))
     return fail(MTL_E_INVALID, "mtl_attn_append: NULL pointer");
   if (head_dim != mtl::kHeadDim) return fail(MTL_E_UNSUPPORTED, "head_dim %d (only 128)", head_dim);
   if (n_kv < 1 || n_heads % n_kv || streams < 1 || streams > 65535 || max_seq < 1 || cache_stream_stride < 0)
@@ -408,6 +408,8 @@ int mtl_attn_append(const uint16_t* qkv, const uint16_t* k_norm_w, const uint16_
   a.pos = pos;
   a.nh = n_heads;
   a.nkv = n_kv;
+  a.q_norm_w = q_norm_w;
+  a.out = q_out;
   cudaError_t e = mtl::launch_attn_append(a, streams, stream, use_pdl());
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_attn_append");
 }

@@ -260,19 +260,18 @@ class _StepEngine:
         where the reference runs each projection as one tinygemm call with
         M = L): each projection is one bf16 GEMM (cuBLAS through
         torch.matmul) on the layer's effective weights, dequantised from the
-        W4 tiles just before (``mtl_w4_dequant``); the K/V append of all rows
-        is one launch and the attention runs the rows as streams over the
-        shared cache (row r over [0, r]) in launches of 512 rows.  The
-        residual adds and SwiGLU are the reference's bf16 tensor ops."""
+        W4 tiles just before (``mtl_w4_dequant``); one launch appends every
+        row's normed + rotated K and V to the cache and writes the normed +
+        rotated q heads, and the attention is the reference's own causal
+        ``F.scaled_dot_product_attention`` over the cache (fast.py:237-241).
+        The residual adds and SwiGLU are the reference's bf16 tensor ops."""
         m = self.m
         L = ids.shape[0]
         H, D = m.hidden_size, m.head_dim
         dev, bf = m.device, torch.bfloat16
         nq = m.n_heads * D
-        A = 512
-        if getattr(self, "_g_scratch", None) is None:
-            self._g_scratch = torch.zeros(_lib.attn_scratch_bytes(A, m.n_heads, m.n_kv_heads, self.splits),
-                                          dtype=torch.uint8, device=dev)
+        rep = m.n_heads // m.n_kv_heads
+        if getattr(self, "_g_wbuf", None) is None:
             big = max(Lw[n].w.N * Lw[n].w.K for Lw in self.lins[:1] for n in ("qkv", "o", "gu", "down"))
             self._g_wbuf = torch.empty(big, dtype=bf, device=dev)
 
@@ -281,7 +280,7 @@ class _StepEngine:
             return w.dequant(self._g_wbuf[:w.N * w.K].view(w.N, w.K))
         h = torch.empty(L, H, dtype=bf, device=dev)
         xn = torch.empty(L, H, dtype=bf, device=dev)
-        attn = torch.empty(L, nq, dtype=bf, device=dev)
+        qn = torch.empty(L, m.n_heads, D, dtype=bf, device=dev)
         pos = torch.arange(L, dtype=torch.long, device=dev)
         kernels.embed_sum(ids.contiguous(), m.embed_tokens, self.emb_audio, h)
         for li in range(m.n_layers):
@@ -289,12 +288,11 @@ class _StepEngine:
             kernels.rmsnorm(h, lyr["input_layernorm"], xn, RMS_EPS)
             qkv = torch.matmul(xn, weight(Lw["qkv"]).t())
             kernels.attn_append(qkv, lyr["k_norm"], m.rope_cos, m.rope_sin, kcs[li], vcs[li], pos, m.n_heads,
-                                m.n_kv_heads, streams=L)
-            for r0 in range(0, L, A):
-                r1 = min(L, r0 + A)
-                kernels.attn_decode(qkv[r0:r1], lyr["q_norm"], lyr["k_norm"], m.rope_cos, m.rope_sin, kcs[li],
-                                    vcs[li], pos[r0:r1], m.n_heads, m.n_kv_heads, self.splits, attn[r0:r1],
-                                    self._g_scratch, streams=r1 - r0)
+                                m.n_kv_heads, streams=L, q_norm_w=lyr["q_norm"], q_out=qn)
+            keys = kcs[li][:, :L].repeat_interleave(rep, dim=0).unsqueeze(0)
+            vals = vcs[li][:, :L].repeat_interleave(rep, dim=0).unsqueeze(0)
+            attn = F.scaled_dot_product_attention(qn.view(1, L, m.n_heads, D).transpose(1, 2), keys, vals,
+                                                  is_causal=True).transpose(1, 2).reshape(L, nq)
             h = h + torch.matmul(attn, weight(Lw["o"]).t())                 # fast.py:168
             kernels.rmsnorm(h, lyr["post_attention_layernorm"], xn, RMS_EPS)
             gu = torch.matmul(xn, weight(Lw["gu"]).t())

@@ -60,12 +60,14 @@ def attn_decode(qkv, q_norm_w, k_norm_w, rope_cos, rope_sin, k_cache_layer, v_ca
 
 
 def attn_append(qkv, k_norm_w, rope_cos, rope_sin, k_cache_layer, v_cache_layer, pos_dev, n_heads: int,
-                n_kv: int, streams: int = 1, cache_stream_stride: int = 0) -> None:
-    """K/V append of `streams` rows (k norm + RoPE, v) into cache rows pos_dev[s]."""
+                n_kv: int, streams: int = 1, cache_stream_stride: int = 0, q_norm_w=None, q_out=None) -> None:
+    """K/V append of `streams` rows (k norm + RoPE, v) into cache rows
+    pos_dev[s]; with ``q_out`` also the rows' normed + rotated q heads."""
     max_seq = k_cache_layer.shape[-2]
-    _lib.call("mtl_attn_append", qkv.data_ptr(), k_norm_w.data_ptr(), rope_cos.data_ptr(), rope_sin.data_ptr(),
-              k_cache_layer.data_ptr(), v_cache_layer.data_ptr(), ctypes.c_longlong(cache_stream_stride), max_seq,
-              pos_dev.data_ptr(), streams, n_heads, n_kv, k_cache_layer.shape[-1], _s())
+    _lib.call("mtl_attn_append", qkv.data_ptr(), _p(q_norm_w), k_norm_w.data_ptr(), rope_cos.data_ptr(),
+              rope_sin.data_ptr(), k_cache_layer.data_ptr(), v_cache_layer.data_ptr(),
+              ctypes.c_longlong(cache_stream_stride), max_seq, pos_dev.data_ptr(), streams, n_heads, n_kv,
+              k_cache_layer.shape[-1], _p(q_out), _s())
 
 
 def bf16_linear(x: torch.Tensor, W: torch.Tensor, out: torch.Tensor, *, norm_weight=None, eps: float = 1e-6,
