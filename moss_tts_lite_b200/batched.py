@@ -4,8 +4,11 @@ The reference decodes one utterance at a time (batch 1, moss_tts_lite/
 fast.py:272-325); its throughput configuration runs streams one after the
 other.  Here one decode step advances all B streams:
 
-* every W4 projection reads its weights once for the B rows (register-MMA
-  launches of up to 8 rows, the MMA N dimension);
+* every W4 projection reads its weights once for the B rows: with
+  ``tc=True`` (the default from 2 streams) in tensor-core tiles, the B rows
+  being the N dimension of the tcgen05 MMAs (up to 16 rows per launch);
+  with ``tc=False`` in the register-MMA tiles of the batch-1 engine
+  (launches of up to 8 rows, the mma.sync N dimension);
 * attention runs the B streams in one launch, each over its own KV cache
   (``mtl_attn_decode`` with ``streams = B`` and a per-stream cache stride);
 * the final norm, the two-way text head and the 32 audio heads run on the
@@ -13,16 +16,17 @@ other.  Here one decode step advances all B streams:
   from the two-way logits) writes each stream's next row and position on the
   device, so a captured step graph replays with no host round trip.
 
-Each stream's prompt is prefilled into its own cache slice with the chunked
-prefill of the batch-1 engine.  Stream s's results equal a batch-1 decode of
-the same stream up to the W4 linears' fp32 summation order (same kernels,
-same split-K plan when the batch fits one launch).
+Each stream's prompt is prefilled into its own cache slice with the
+prefill of the batch-1 engine.  With ``tc=False`` stream s's results equal a
+batch-1 decode of the same stream bit for bit (same kernels, same split-K
+plan); with the tensor-core tiles they agree to within the two W4 kernels'
+fp32 summation orders.
 """
 from __future__ import annotations
 
 import torch
 
-from . import kernels
+from . import _lib, kernels
 from .model import AUDIO_DELAY_SLOT_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_PAD_CODE, AUDIO_VOCAB, N_VQ, RMS_EPS
 
 _HEAD_ROWS = 4  # rows per bf16 head launch (mtl_bf16_linear)
@@ -31,7 +35,7 @@ _HEAD_ROWS = 4  # rows per bf16 head launch (mtl_bf16_linear)
 class BatchedFastMossTTS:
     """``streams`` decode streams over the weights of a FastMossTTS (shared)."""
 
-    def __init__(self, fast, streams: int, max_seq: int | None = None):
+    def __init__(self, fast, streams: int, max_seq: int | None = None, tc: bool | None = None):
         m = fast.m
         if streams < 1:
             raise ValueError("streams must be >= 1")
@@ -45,6 +49,11 @@ class BatchedFastMossTTS:
         H, D = m.hidden_size, m.head_dim
         eng = fast.engine
         self.lins = eng.lins
+        if tc is None:
+            tc = streams >= 2
+        self.tc = bool(tc) and self._tc_capable(eng.lins)
+        if self.tc:
+            self.lins = self._tc_lins(eng.lins)
         self.emb_audio = eng.emb_audio
         self.head_audio2d = eng.head_audio2d
         B = streams
@@ -68,6 +77,26 @@ class BatchedFastMossTTS:
         self.kv_stable = False
         self.graph = None
         self.seq = [0] * B
+
+    @staticmethod
+    def _tc_capable(lins) -> bool:
+        from .fast import _W4Lin
+        from .quant import W4Weight
+        return all(isinstance(L[n], _W4Lin) and L[n].w.fmt == _lib.MTL_FMT_REF and L[n].w.k_perm is None
+                   and W4Weight.tc_supported(L[n].w.K, L[n].w.N, L[n].w.group_size)
+                   for L in lins for n in ("qkv", "o", "gu", "down"))
+
+    @staticmethod
+    def _tc_lins(lins) -> list:
+        """The layers' W4 weights re-packed into tensor-core tiles (same codes
+        and (scale, zero); gate|up interleaved row by row)."""
+        from .fast import _W4Lin
+        out = []
+        for L in lins:
+            out.append({"qkv": _W4Lin(L["qkv"].w.to_tc()), "o": _W4Lin(L["o"].w.to_tc()),
+                        "gu": _W4Lin(L["gu"].w.to_tc(swiglu_block=L["gu"].fuse_block), fuse_block=1),
+                        "down": _W4Lin(L["down"].w.to_tc())})
+        return out
 
     # ---------------------------------------------------------------- prefill
     def prefill(self, s: int, ids: torch.Tensor) -> torch.Tensor:

@@ -38,6 +38,8 @@ cudaError_t w4_pack_ref(const uint8_t* q, const uint16_t* qsz, int K, int N, int
 cudaError_t w4_unpack_codes(const uint8_t* tiles, int K, int N, int g, int fmt, uint8_t* codes, cudaStream_t s);
 int w4_tc_plan(int K, int N, int g, int num_sms, TcPlan* out);
 cudaError_t w4_tc_launch(const TcArgs& a, cudaStream_t stream, int use_pdl);
+int w4_tcb_plan(int K, int N, int g, int num_sms, TcPlan* out);
+cudaError_t w4_tcb_launch(const TcbArgs& a, cudaStream_t stream, int use_pdl);
 cudaError_t w4_tc_pack(const uint8_t* q, const uint16_t* qsz, int K, int N, int g, uint8_t* tiles, cudaStream_t s);
 cudaError_t w4_tc_unpack_codes(const uint8_t* tiles, int K, int N, int g, uint8_t* codes, cudaStream_t s);
 }  // namespace mtl
@@ -178,8 +180,12 @@ int mtl_w4_plan(int M, int K, int N, int group_size, int param_fmt, size_t* tile
     mtl::TcPlan p;
     if (get_tc_plan(K, N, group_size, &p))
       return fail(MTL_E_UNSUPPORTED, "no tensor-core plan for K=%d N=%d g=%d", K, N, group_size);
+    size_t part = p.partial_bytes;
+    mtl::TcPlan pb;
+    if (M > 1 && mtl::w4_tcb_plan(K, N, group_size, num_sms(), &pb) == 0 && pb.partial_bytes > part)
+      part = pb.partial_bytes;
     if (tiles_bytes) *tiles_bytes = (size_t)p.T * p.tile_bytes;
-    if (scratch_bytes) *scratch_bytes = tc_counters_bytes(N) + p.partial_bytes;
+    if (scratch_bytes) *scratch_bytes = tc_counters_bytes(N) + part;
     return MTL_OK;
   }
   const int mc = M < mtl::kW4MaxM ? M : mtl::kW4MaxM;
@@ -281,6 +287,32 @@ int mtl_w4a16_linear(const uint16_t* x, int ldx, int M, int K, int N, int group_
     a.epi = epilogue;
     a.counters = static_cast<int*>(scratch);
     a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + tc_counters_bytes(N));
+    if (M > 1) {
+      // several rows: the batch is the N = 16 dimension of the MMAs
+      mtl::TcbArgs b{};
+      if (mtl::w4_tcb_plan(K, N, group_size, num_sms(), &b.p))
+        return fail(MTL_E_UNSUPPORTED, "no batched tensor-core plan");
+      b.ldx = ldx;
+      b.K = K;
+      b.N = N;
+      b.g = group_size;
+      b.tiles = a.tiles;
+      b.norm_w = norm_w;
+      b.norm_eps = norm_eps;
+      b.epi = epilogue;
+      b.ldy = ldy;
+      b.counters = a.counters;
+      b.partials = a.partials;
+      for (int m0 = 0; m0 < M; m0 += mtl::kTcbMaxM) {
+        b.M = (M - m0) < mtl::kTcbMaxM ? (M - m0) : mtl::kTcbMaxM;
+        b.x = x + (size_t)m0 * ldx;
+        b.residual = residual ? residual + (size_t)m0 * N : nullptr;
+        b.y = y + (size_t)m0 * ldy;
+        cudaError_t e = mtl::w4_tcb_launch(b, stream, use_pdl() ? 1 : 0);
+        if (e != cudaSuccess) return cuda_fail(e, "mtl_w4a16_linear (tensor cores, batched) launch");
+      }
+      return MTL_OK;
+    }
     for (int m = 0; m < M; ++m) {
       a.x = x + (size_t)m * ldx;
       a.residual = residual ? residual + (size_t)m * N : nullptr;

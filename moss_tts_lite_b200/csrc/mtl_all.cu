@@ -2,6 +2,7 @@
 // error word are shared by every kernel without relocatable device code).
 #include "w4_gemv.cu"
 #include "w4_tc.cu"
+#include "w4_tcb.cu"
 #include "step_kernels.cu"
 #include "attn_decode.cu"
 #include "sampling.cu"

@@ -82,6 +82,29 @@ class W4Weight:
                   self.fmt, out.data_ptr(), _stream())
         return out
 
+    def ref_params(self) -> torch.Tensor:
+        """qsz bf16 [K/g, N, 2] (scale, zero) read back from reference-format tiles."""
+        if self.fmt != _lib.MTL_FMT_REF:
+            raise ValueError("ref_params needs MTL_FMT_REF tiles")
+        KT, nb, g = self.K // self.group_size, self.N // 64, self.group_size
+        t = self.tiles.view(nb, KT, -1)[:, :, 64 * g // 2:64 * g // 2 + 256]       # [nb, KT, 64 x (scale, zero)]
+        prm = t.contiguous().view(torch.bfloat16).view(nb, KT, 64, 2)
+        return prm.permute(1, 0, 2, 3).reshape(KT, self.N, 2).contiguous()
+
+    def to_tc(self, swiglu_block: int = 0) -> "W4Weight":
+        """The same reference-format codes and (scale, zero) in tensor-core
+        tiles (MTL_FMT_TC).  ``swiglu_block``: the weight is a gate|up pair
+        interleaved in blocks of that many rows; the TC tiles interleave the
+        pair row by row."""
+        q, qsz = self.unpack_codes(), self.ref_params()
+        if swiglu_block:
+            b = swiglu_block
+            q = q.view(-1, 2, b, self.K).permute(1, 0, 2, 3).reshape(2, -1, self.K)      # [gate | up][I][K]
+            q = q.permute(1, 0, 2).reshape(self.N, self.K)
+            z = qsz.view(qsz.shape[0], -1, 2, b, 2).permute(0, 2, 1, 3, 4).reshape(qsz.shape[0], 2, -1, 2)
+            qsz = z.permute(0, 2, 1, 3).reshape(qsz.shape[0], self.N, 2)
+        return W4Weight.from_ref(q.contiguous(), qsz.contiguous(), self.group_size, fmt=_lib.MTL_FMT_TC)
+
     def dequant(self, out: torch.Tensor | None = None) -> torch.Tensor:
         """Effective weights bf16 [N, K] in packed column order (k_perm order
         for act-order AutoGPTQ weights), as the operand of a many-row GEMM."""

@@ -50,7 +50,7 @@ def test_batched_streams_equal_batch1(graph):
     rng = np.random.default_rng(9)
     firsts = [_t(np.concatenate([[GEN], rng.integers(0, 1024, 32)]).astype(np.int64), dev) for _ in range(B)]
     ref = [_batch1_trajectory(fast, prompts[s], firsts[s], steps) for s in range(B)]
-    bt = BatchedFastMossTTS(fast, B, max_seq=128)
+    bt = BatchedFastMossTTS(fast, B, max_seq=128, tc=False)
     for s in range(B):
         bt.prefill(s, prompts[s])
         bt.start(s, firsts[s], prompts[s].shape[0])
@@ -66,5 +66,38 @@ def test_batched_streams_equal_batch1(graph):
             assert torch.equal(bt.h_final[s].view(torch.int16), h.view(-1).view(torch.int16)), (s, t)
             assert torch.equal(bt.ids[s], nxt), (s, t)
             assert int(bt.pos[s]) == prompts[s].shape[0] + t + 1
+    from moss_tts_lite_b200 import _lib
+    assert _lib.device_status() == 0
+
+
+def test_batched_tensor_core_tiles_agree():
+    """The tensor-core tiles (tcgen05, the batch as the MMA N dimension)
+    against the register-MMA batched step: every stream's logits agree to
+    within bf16 noise and >= 95% of the greedy audio codes coincide."""
+    dev = require_cuda()
+    from moss_tts_lite_b200.batched import BatchedFastMossTTS
+    fast, m, om = _w4_setup(dev, seed=33, max_seq=128)
+    B = 6
+    prompts = [_t(_prompt(5 + 2 * s, seed=60 + s), dev) for s in range(B)]
+    rng = np.random.default_rng(19)
+    firsts = [_t(np.concatenate([[GEN], rng.integers(0, 1024, 32)]).astype(np.int64), dev) for _ in range(B)]
+    outs = {}
+    for tc in (False, True):
+        bt = BatchedFastMossTTS(fast, B, max_seq=128, tc=tc)
+        assert bt.tc == tc
+        for s in range(B):
+            bt.prefill(s, prompts[s])
+            bt.start(s, firsts[s], prompts[s].shape[0])
+        bt.step()
+        torch.cuda.synchronize()
+        outs[tc] = (bt.la.float().cpu().numpy(), bt.h_final.float().cpu().numpy())
+    la0, h0 = outs[False]
+    la1, h1 = outs[True]
+    assert np.abs(h0 - h1).max() < 0.05 * np.abs(h0).max()
+    fin = np.isfinite(la0)
+    assert np.array_equal(fin, np.isfinite(la1))
+    assert np.abs(la0[fin] - la1[fin]).max() < 0.05 * np.abs(la0[fin]).max()
+    agree = (np.argmax(la0, -1) == np.argmax(la1, -1)).mean()
+    assert agree >= 0.95, agree
     from moss_tts_lite_b200 import _lib
     assert _lib.device_status() == 0

@@ -125,3 +125,60 @@ def test_tc_deterministic_and_graph_capture():
     gr.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, y1)
+
+
+@pytest.mark.parametrize("M,K,N,g", [(2, 4096, 6144, 128), (5, 12288, 4096, 128), (16, 4096, 24576, 128),
+                                     (21, 1024, 384, 64), (16, 2048, 640, 32), (9, 4096, 4096, 128)])
+def test_tc_batched_rows(M, K, N, g):
+    """2..16 rows per launch (the batch is the N dimension of the tcgen05
+    MMAs, activations staged per tile): every row equals its own one-row
+    call bit for bit and the oracle within tolerance; 21 rows run as 16 + 5."""
+    dev = require_cuda()
+    q, qsz, Wnk = _ref_case(K, N, g, seed=M + K + N)
+    w = _tc(q, qsz, g, dev)
+    rng = np.random.default_rng(M)
+    x = f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    xt = _t(x, dev, torch.bfloat16)
+    y = w.linear(xt)
+    torch.cuda.synchronize()
+    _check(_bits(y), ow.linear_f64(x, Wnk.T))
+    for r in range(M):
+        assert torch.equal(y[r:r + 1], w.linear(xt[r:r + 1])), r
+    from moss_tts_lite_b200 import _lib
+    assert _lib.device_status() == 0
+
+
+def test_tc_batched_epilogues_norm_residual_swiglu():
+    """The fused RMSNorm prologue, the in-place residual and the SwiGLU
+    epilogue with 5 rows per launch, against the oracle."""
+    dev = require_cuda()
+    from moss_tts_lite_b200 import _lib
+    from moss_tts_lite_b200.quant import W4Weight
+    K, I, g, M = 4096, 1024, 128, 5
+    rng = np.random.default_rng(31)
+    q, qsz, Wnk = _ref_case(K, K, g, seed=11)
+    w = _tc(q, qsz, g, dev)
+    h = f32_to_bf16((rng.standard_normal((M, K)) * 3).astype(np.float32))
+    nw = f32_to_bf16((1 + 0.1 * rng.standard_normal(K)).astype(np.float32))
+    ht = _t(h, dev, torch.bfloat16)
+    y = w.linear(ht, norm_weight=_t(nw, dev, torch.bfloat16), residual=ht.clone())
+    xn = ost.rms_norm(h, nw)
+    ref = f32_to_bf16(bf16_to_f32(h) + bf16_to_f32(ow.linear_bf16(xn, Wnk.T)))
+    d = np.abs(bf16_to_f32(_bits(y)) - bf16_to_f32(ref))
+    assert d.max() <= 2e-2 + 1e-2 * np.abs(bf16_to_f32(ref)).max()
+    assert (d == 0).mean() > 0.95
+    h2 = ht.clone()
+    w.linear(h2, norm_weight=_t(nw, dev, torch.bfloat16), residual=h2, out=h2)
+    assert torch.equal(h2, y)
+    qg, qszg, Wg = _ref_case(K, I, g, seed=12)
+    qu, qszu, Wu = _ref_case(K, I, g, seed=13)
+    qf = np.stack([qg, qu], 1).reshape(2 * I, K)
+    qszf = np.stack([qszg, qszu], 2).reshape(K // g, 2 * I, 2)
+    wf = W4Weight.from_ref(_t(qf, dev), _t(qszf, dev, torch.bfloat16), g, fmt=_lib.MTL_FMT_TC)
+    x = f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    y = wf.linear(_t(x, dev, torch.bfloat16), swiglu=True)
+    ref = ost.silu_mul(ow.linear_bf16(x, Wg.T), ow.linear_bf16(x, Wu.T))
+    d = np.abs(bf16_to_f32(_bits(y)) - bf16_to_f32(ref))
+    assert d.max() <= 2e-2 + 1e-2 * np.abs(bf16_to_f32(ref)).max()
+    assert (d == 0).mean() > 0.95
+    assert _lib.device_status() == 0
