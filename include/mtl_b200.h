@@ -95,7 +95,8 @@ int mtl_w4_pack_gptq(const int32_t* qweight, const int32_t* qzeros, const uint16
  * (q - 8) * scale + zero (gptq.py:87-97 effective_weight), GPTQ
  * (q - (z + zero_offset)) * scale, computed in fp32, rounded to bf16 — the
  * operand of the prompt-prefill GEMMs (many rows per pass over a layer),
- * where the reference runs tinygemm with M = prompt length (fast.py:218-270). */
+ * where the reference runs tinygemm with M = prompt length (fast.py:218-270).
+ * tiles and w 16-byte aligned (MTL_E_ALIGN otherwise). */
 int mtl_w4_dequant(const void* tiles, int K, int N, int group_size, int param_fmt, int zero_offset, uint16_t* w,
                    mtl_stream_t stream);
 

@@ -243,7 +243,7 @@ int mtl_w4_dequant(const void* tiles, int K, int N, int group_size, int param_fm
   if (int r = check_w4_shape(K, N, group_size, param_fmt)) return r;
   if (param_fmt == MTL_FMT_TC) return fail(MTL_E_UNSUPPORTED, "mtl_w4_dequant: MTL_FMT_TC tiles");
   if (!tiles || !w) return fail(MTL_E_INVALID, "mtl_w4_dequant: NULL pointer");
-  if (!aligned(tiles, 16) || !aligned(w, 4)) return fail(MTL_E_ALIGN, "mtl_w4_dequant: misaligned tiles / w");
+  if (!aligned(tiles, 16) || !aligned(w, 16)) return fail(MTL_E_ALIGN, "mtl_w4_dequant: tiles / w must be 16-byte aligned");
   if (zero_offset < 0 || zero_offset > 1) return fail(MTL_E_INVALID, "zero_offset must be 0 or 1");
   cudaError_t e = mtl::w4_dequant(static_cast<const uint8_t*>(tiles), K, N, group_size, param_fmt, zero_offset, w,
                                   stream);

@@ -694,39 +694,72 @@ __global__ void unpack_codes_kernel(const uint8_t* tiles, int K, int N, int g, i
 // REF  w = (q - 8) * scale + zero            (gptq.py:87-97)
 // GPTQ w = (q - (z + zero_offset)) * scale    (AutoGPTQ)
 // computed in fp32 and rounded to bf16; two consecutive k per thread.
+// One 64-column x group tile per CTA iteration: warp w unpacks k16-steps
+// w, w + 8, ... in the MMA lane layout the tiles are packed in (one uint4 of
+// codes per lane: rows 16 j + gr (+8), columns 16 ks + 2 tq (+1, +8, +9)),
+// writes bf16 pairs into a padded shared-memory tile (row stride g + 8
+// elements: the 32 lanes of a store hit 32 distinct banks), and the CTA then
+// writes the tile's 64 rows as 16-byte chunks.  (q - 8) comes from the float
+// 2^23 + q minus (2^23 + 8), exact, so v = fmaf(q - 8, scale, zero) is the
+// same single-rounding FMA as the GEMV's group affine.
 template <int FMT>
-__global__ void dequant_kernel(const uint8_t* tiles, int K, int N, int g, int tile_bytes, int zero_offset,
-                               uint16_t* w) {
-  const int KT = K / g;
-  const long long total = (long long)N * K / 2;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const int n = (int)(idx / (K / 2)), k = (int)(idx % (K / 2)) * 2;
-    const int nb = n / kNT, c = n % kNT, G = k / g, kin = k % g;
-    const int j = c / 16, rr = c % 16, gr = rr & 7, hi_row = rr >> 3;
-    const int ks = kin / 16, k16 = kin % 16;
-    const int hi_k = k16 >= 8 ? 1 : 0;
-    const int tq = (k16 & 7) >> 1;
-    const int lane = gr * 4 + tq;
-    const int slot = (hi_row ? 1 : 0) + (hi_k ? 2 : 0);  // even k; k + 1 is slot + 4
-    const uint8_t* tile = tiles + ((long long)nb * KT + G) * tile_bytes;
-    const uint32_t wd = reinterpret_cast<const uint32_t*>(tile)[(ks * 32 + lane) * 4 + j];
-    const float q0 = (float)((wd >> (4 * slot)) & 0xFu), q1 = (float)((wd >> (4 * (slot + 4))) & 0xFu);
+__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* tiles, int K, int N, int g, int tile_bytes,
+                                                      int zero_offset, uint16_t* w) {
+  extern __shared__ __align__(16) uint16_t sout[];  // [kNT][g + 8]
+  const int KT = K / g, KS = g / 16, ld = g + 8, cpr = g / 8;
+  const int ntiles = (N / kNT) * KT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gr = lane >> 2, tq = lane & 3;
+  for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const int nb = t / KT, G = t - nb * KT;
+    const uint8_t* tile = tiles + (size_t)t * tile_bytes;
     const uint8_t* prm = tile + kNT * g / 2;
-    float v0, v1;
-    if (FMT == kFmtRef) {
-      const uint32_t pw = reinterpret_cast<const uint32_t*>(prm)[c];
-      const float sc = __uint_as_float(pw << 16), ze = __uint_as_float(pw & 0xFFFF0000u);
-      v0 = fmaf(q0 - 8.f, sc, ze);
-      v1 = fmaf(q1 - 8.f, sc, ze);
-    } else {
-      const float sc = __half2float(reinterpret_cast<const __half*>(prm)[c]);
-      const uint32_t zw = reinterpret_cast<const uint32_t*>(prm + 128)[c >> 3];
-      const float z = (float)((int)((zw >> (4 * (c & 7))) & 0xFu) + zero_offset);
-      v0 = (q0 - z) * sc;
-      v1 = (q1 - z) * sc;
+    float sc[4][2], zo[4][2];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int c = 16 * j + gr + 8 * hr;
+        if (FMT == kFmtRef) {
+          const uint32_t pw = reinterpret_cast<const uint32_t*>(prm)[c];
+          sc[j][hr] = __uint_as_float(pw << 16);
+          zo[j][hr] = __uint_as_float(pw & 0xFFFF0000u);
+        } else {
+          sc[j][hr] = __half2float(reinterpret_cast<const __half*>(prm)[c]);
+          const uint32_t zw = reinterpret_cast<const uint32_t*>(prm + 128)[c >> 3];
+          zo[j][hr] = (float)((int)((zw >> (4 * (c & 7))) & 0xFu) + zero_offset);
+        }
+      }
+    for (int ks = warp; ks < KS; ks += 8) {
+      const uint4 wv = reinterpret_cast<const uint4*>(tile)[ks * 32 + lane];
+      const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr)
+#pragma unroll
+          for (int hk = 0; hk < 2; ++hk) {
+            const int slot = hr + 2 * hk;
+            const uint32_t n0 = (wr[j] >> (4 * slot)) & 0xFu, n1 = (wr[j] >> (4 * (slot + 4))) & 0xFu;
+            float v0, v1;
+            if (FMT == kFmtRef) {
+              v0 = fmaf(__uint_as_float(0x4B000000u | n0) - 8388616.f, sc[j][hr], zo[j][hr]);
+              v1 = fmaf(__uint_as_float(0x4B000000u | n1) - 8388616.f, sc[j][hr], zo[j][hr]);
+            } else {
+              v0 = ((__uint_as_float(0x4B000000u | n0) - 8388608.f) - zo[j][hr]) * sc[j][hr];
+              v1 = ((__uint_as_float(0x4B000000u | n1) - 8388608.f) - zo[j][hr]) * sc[j][hr];
+            }
+            const int c = 16 * j + gr + 8 * hr, k = 16 * ks + 8 * hk + 2 * tq;
+            *reinterpret_cast<uint32_t*>(sout + c * ld + k) =
+                (uint32_t)f32_to_bf16_bits(v0) | ((uint32_t)f32_to_bf16_bits(v1) << 16);
+          }
     }
-    reinterpret_cast<uint32_t*>(w)[idx] = (uint32_t)f32_to_bf16_bits(v0) | ((uint32_t)f32_to_bf16_bits(v1) << 16);
+    __syncthreads();
+    for (int i = threadIdx.x; i < kNT * cpr; i += blockDim.x) {
+      const int r = i / cpr, ch = i - r * cpr;
+      *reinterpret_cast<uint4*>(w + (size_t)(nb * kNT + r) * K + (size_t)G * g + ch * 8) =
+          *reinterpret_cast<const uint4*>(sout + r * ld + ch * 8);
+    }
+    __syncthreads();
   }
 }
 
@@ -759,11 +792,14 @@ cudaError_t w4_pack_ref(const uint8_t* q, const uint16_t* qsz, int K, int N, int
 
 cudaError_t w4_dequant(const uint8_t* tiles, int K, int N, int g, int fmt, int zero_offset, uint16_t* w,
                        cudaStream_t s) {
-  const long long pairs = (long long)N * K / 2;
+  const int ntiles = (N / kNT) * (K / g);
+  const int grid = std::max(1, std::min(ntiles, 148 * 8));
+  const size_t smem = (size_t)kNT * (g + 8) * 2;
+  if (smem > 48 * 1024) return cudaErrorInvalidValue;  // g <= 376
   if (fmt == kFmtRef)
-    dequant_kernel<kFmtRef><<<grid_for(pairs), 256, 0, s>>>(tiles, K, N, g, tile_bytes(g, fmt), zero_offset, w);
+    dequant_kernel<kFmtRef><<<grid, 256, smem, s>>>(tiles, K, N, g, tile_bytes(g, fmt), zero_offset, w);
   else
-    dequant_kernel<kFmtGptq><<<grid_for(pairs), 256, 0, s>>>(tiles, K, N, g, tile_bytes(g, fmt), zero_offset, w);
+    dequant_kernel<kFmtGptq><<<grid, 256, smem, s>>>(tiles, K, N, g, tile_bytes(g, fmt), zero_offset, w);
   return cudaGetLastError();
 }
 
