@@ -34,7 +34,9 @@ typedef struct CUstream_st* mtl_stream_t; /* == cudaStream_t */
 #define MTL_FMT_GPTQ 1 /* AutoGPTQ: fp16 scale + 4-bit zero, w = (q-(z+off))*s   */
 #define MTL_FMT_TC 2   /* reference qsz in the tensor-core tile layout (128-row
                           tiles, per-row (scale, zero)); mtl_w4a16_linear runs
-                          the tcgen05 kernel once per activation row.  N % 128
+                          the tcgen05 kernels: one row per launch for M == 1,
+                          up to 16 rows per launch (the MMA N dimension)
+                          otherwise.  N % 128
                           == 0, group_size 32/64/128, K <= 16384; the SwiGLU
                           epilogue expects gate and up rows interleaved one by
                           one (row 2j = gate j, row 2j + 1 = up j) */
@@ -279,13 +281,22 @@ int mtl_feed_row(const int64_t* dec, int text_mode, long long text_const, long l
  *   bf16 groups its roundings differently for one-row and multi-row
  *   tensors, and the top-p cut-off follows the same grouping.
  *   out[r] (device int64) = sampled column + out_add.
+ *   scratch (device, 16-byte aligned, nullable): rows of >= 16384 columns
+ *   with a top-k (the text head) are cut into slices selected by one CTA
+ *   each when scratch holds mtl_sample_scratch_bytes(cols, n_rows, top_k)
+ *   bytes (MTL_E_SCRATCH if it is smaller); with NULL each row is one CTA.
+ *   The draw is the same either way.
  * Candidate sets and probabilities follow the reference's arithmetic; the
  * random stream is this library's own (not torch.multinomial's). */
 int mtl_sample_rows(const uint16_t* logits, int ld, int cols, int n_rows, const int32_t* row_index,
                     float temperature, int top_k, float top_p, float repetition_penalty, const uint32_t* seen_bits,
                     int words_per_set, const int32_t* seen_set_of_row, const int32_t* excluded, int n_excluded,
                     const int32_t* scan_rows, uint64_t seed, uint64_t offset, int64_t out_add, int64_t* out,
-                    mtl_stream_t stream);
+                    void* scratch, size_t scratch_bytes, mtl_stream_t stream);
+
+/* Scratch bytes of mtl_sample_rows' sliced path for these arguments (0: the
+ * rows are sampled one CTA each and need none). */
+size_t mtl_sample_scratch_bytes(int cols, int n_rows, int top_k);
 
 /* Round-to-nearest W4 quantisation of a bf16 weight [N, K] exactly as
  * FastMossTTS._quantize (fast.py:85-96) / gptq.rtn_quantize (gptq.py:54-64):

@@ -13,6 +13,11 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmtl_b200.so")
 
 MTL_OK = 0
+MTL_E_INVALID = -1
+MTL_E_ALIGN = -2
+MTL_E_SCRATCH = -3
+MTL_E_CUDA = -4
+MTL_E_UNSUPPORTED = -5
 MTL_FMT_REF = 0
 MTL_FMT_GPTQ = 1
 MTL_FMT_TC = 2
@@ -21,7 +26,7 @@ MTL_EPI_RESIDUAL = 1
 MTL_EPI_SWIGLU = 2
 MTL_ATTN_KV_STABLE = 1
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _c_void_p = ctypes.c_void_p
 _c_int = ctypes.c_int
@@ -68,7 +73,9 @@ SIGNATURES = {
     "mtl_sample_rows": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_int32), _c_float,
                                  _c_int, _c_float, _c_float, _c_void_p, _c_int, ctypes.POINTER(ctypes.c_int32),
                                  ctypes.POINTER(ctypes.c_int32), _c_int, ctypes.POINTER(ctypes.c_int32),
-                                 ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64, _c_void_p, _c_void_p]),
+                                 ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64, _c_void_p, _c_void_p,
+                                 _c_size_t, _c_void_p]),
+    "mtl_sample_scratch_bytes": (_c_size_t, [_c_int, _c_int, _c_int]),
     "mtl_rmsnorm": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_float, _c_void_p, _c_int,
                              _c_void_p]),
     "mtl_w4_rtn_quantize": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p]),

@@ -155,7 +155,7 @@ extern "C" {
 
 const char* mtl_last_error(void) { return g_err; }
 
-int mtl_abi_version(void) { return 1; }
+int mtl_abi_version(void) { return 2; }
 
 int mtl_device_status(uint32_t* out, int clear) {
   if (!out) return fail(MTL_E_INVALID, "mtl_device_status: out is NULL");
@@ -539,11 +539,17 @@ static int inner_scan_log_threads_x(int num_rows, int row_size) {
   return l < 4 ? 4 : (l > 9 ? 9 : l);
 }
 
+size_t mtl_sample_scratch_bytes(int cols, int n_rows, int top_k) {
+  int slice_len = 0;
+  const int slices = mtl::sample_slice_count(cols, top_k, &slice_len);
+  return slices > 0 && n_rows > 0 ? (size_t)n_rows * slices * top_k * 8 : 0;
+}
+
 int mtl_sample_rows(const uint16_t* logits, int ld, int cols, int n_rows, const int32_t* row_index,
                     float temperature, int top_k, float top_p, float repetition_penalty, const uint32_t* seen_bits,
                     int words_per_set, const int32_t* seen_set_of_row, const int32_t* excluded, int n_excluded,
                     const int32_t* scan_rows, uint64_t seed, uint64_t offset, int64_t out_add, int64_t* out,
-                    mtl_stream_t stream) {
+                    void* scratch, size_t scratch_bytes, mtl_stream_t stream) {
   if (!logits || !out || !row_index) return fail(MTL_E_INVALID, "mtl_sample_rows: NULL pointer");
   if (n_rows < 1 || n_rows > mtl::kSampleMaxRows || cols < 1 || ld < cols)
     return fail(MTL_E_INVALID, "mtl_sample_rows: n_rows=%d (1..%d) cols=%d ld=%d", n_rows, mtl::kSampleMaxRows, cols, ld);
@@ -586,6 +592,17 @@ int mtl_sample_rows(const uint16_t* logits, int ld, int cols, int n_rows, const 
   a.off_hi = (uint32_t)(offset >> 32);
   a.out = out;
   a.out_add = out_add;
+  int slice_len = 0;
+  const int slices = scratch ? mtl::sample_slice_count(cols, top_k, &slice_len) : 0;
+  if (slices > 0) {
+    const size_t per = (size_t)n_rows * slices * top_k;
+    if (scratch_bytes < per * 8) return fail(MTL_E_SCRATCH, "mtl_sample_rows: scratch %zu < %zu bytes", scratch_bytes, per * 8);
+    if (!aligned(scratch, 16)) return fail(MTL_E_ALIGN, "mtl_sample_rows: scratch must be 16-byte aligned");
+    a.slices = slices;
+    a.slice_len = slice_len;
+    a.cand_val = static_cast<float*>(scratch);
+    a.cand_id = reinterpret_cast<int32_t*>(static_cast<float*>(scratch) + per);
+  }
   cudaError_t e = mtl::launch_sample_rows(a, stream);
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_sample_rows");
 }

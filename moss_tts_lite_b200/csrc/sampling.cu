@@ -18,10 +18,21 @@
 //      categorical draw in id order from a Philox4x32-10 uniform (Salmon et
 //      al., SC'11) keyed by (seed, offset, row).
 //
+// Rows of at least kSliceMinCols columns with a top-k (the text head's
+// 151,936 logits) take two launches: sample_slices_kernel splits the row
+// into slices of equal length (each at least top_k long), one CTA per slice,
+// and writes each slice's top-k (value after steps 1-2, id) in id order;
+// sample_rows_kernel<true> then runs steps 3-5 on the concatenated slice
+// candidates.  The row's top-k is a subset of the union of the slices'
+// top-k, and both selections keep the lowest ids among ties at the
+// threshold, so the candidate set is the same as one pass over the row.
+//
 // The candidate set and its probabilities follow the reference's arithmetic;
 // the random stream is this library's own (torch.multinomial's stream cannot
 // be reproduced), so sampled tokens agree with the reference in
 // distribution, and bit-exactly with oracle/sampling.py's restatement.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace mtl {
@@ -30,6 +41,9 @@ constexpr int kSampleThreads = 512;
 constexpr int kSampleMaxCand = 2048;
 constexpr int kSampleMaxRows = 40;
 constexpr int kSampleMaxExcl = 8;
+constexpr int kSliceThreads = 256;
+constexpr int kSliceMinCols = 16384;
+constexpr int kSliceMaxLen = 8192;  // values of one slice in shared memory (32 KB)
 
 struct SampleArgs {
   const uint16_t* logits;  // bf16, row r at logits + row_index[r] * ld
@@ -50,7 +64,28 @@ struct SampleArgs {
   uint32_t seed_lo, seed_hi, off_lo, off_hi;
   int64_t* out;
   int64_t out_add;  // added to the sampled column index
+  // sliced path (slices > 0): row r's slice s writes top_k candidates at
+  // cand_val/cand_id + (r * slices + s) * top_k
+  int slices, slice_len;
+  float* cand_val;
+  int32_t* cand_id;
 };
+
+// Slices for a row of `cols` values and a top-k of `top_k`: every slice at
+// least top_k long (the last one included) and at most kSliceMaxLen; 0 when
+// the row is short, has no top-k, or cannot be cut that way.
+inline int sample_slice_count(int cols, int top_k, int* slice_len) {
+  if (cols < kSliceMinCols || top_k <= 0 || top_k >= cols) return 0;
+  for (int ns = std::min(148, cols / std::max(top_k, 1024)); ns >= 2; --ns) {
+    const int sl = (cols + ns - 1) / ns;
+    if (sl > kSliceMaxLen) return 0;  // fewer slices only make them longer
+    if (cols - (ns - 1) * sl >= top_k) {
+      *slice_len = sl;
+      return ns;
+    }
+  }
+  return 0;
+}
 
 // Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as
 // easy as 1, 2, 3", SC 2011): 10 rounds of the 4x32 bijection with the
@@ -168,6 +203,132 @@ __device__ void scan_rows_sklansky(float* cs, int nc, int lognx) {
   }
 }
 
+// Radix-select step over a 256-bin histogram: the largest b in [1, 255] with
+// S(b) = sum_{b' >= b} hist[b'] >= need (0 if there is none), and how many
+// are still needed from bin b: out[0] = b, out[1] = need - S(b + 1).  The bin
+// totals are suffix-scanned by the first 256 threads; every thread of the
+// block calls this (blockDim.x a multiple of 32 and >= 256).
+__device__ void select_bin(const unsigned* hist, int need, int* out, int* wsum) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int b = 255 - tid;
+  const int v = tid < 256 ? (int)hist[b] : 0;
+  int inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= o) inc += u;
+  }
+  __syncthreads();  // wsum may still be read by an earlier call
+  if (tid < 256 && lane == 31) wsum[warp] = inc;
+  __syncthreads();
+  if (tid < 256) {
+    int pre = 0;
+    for (int w = 0; w < warp; ++w) pre += wsum[w];
+    const int S = pre + inc, Snext = S - v;
+    if (b >= 1 && S >= need && Snext < need) {
+      out[0] = b;
+      out[1] = need - Snext;
+    }
+    if (b == 1 && S < need) {
+      out[0] = 0;
+      out[1] = need - S;
+    }
+  }
+  __syncthreads();
+}
+
+// Exclusive block-wide prefix sum of x; *total = the sum over the block.
+__device__ int block_excl_scan(int x, int* wsum, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int inc = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= o) inc += u;
+  }
+  __syncthreads();
+  if (lane == 31) wsum[warp] = inc;
+  __syncthreads();
+  int pre = 0, tot = 0;
+  for (int w = 0; w < nw; ++w) {
+    const int t = wsum[w];
+    if (w < warp) pre += t;
+    tot += t;
+  }
+  *total = tot;
+  return pre + inc - x;
+}
+
+// One CTA per (slice, row): the slice's top_k largest values after
+// temperature, exclusions and penalty (ties at the threshold: lowest ids),
+// written in id order.
+__global__ void __launch_bounds__(kSliceThreads) sample_slices_kernel(const SampleArgs a) {
+  extern __shared__ float sv[];  // the slice's values
+  __shared__ unsigned hist[kSliceThreads / 32][256];
+  __shared__ int wsum[kSliceThreads / 32];
+  __shared__ int sel[2];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int sl = blockIdx.x, r = blockIdx.y, tid = threadIdx.x, warp = tid >> 5;
+  const uint16_t* row = a.logits + (size_t)a.row_index[r] * a.ld;
+  const int set = a.seen_set[r];
+  const int lo = sl * a.slice_len, len = min(a.cols, lo + a.slice_len) - lo;
+  const int k = a.top_k;  // 0 < k <= len (host)
+  for (int i = tid; i < len; i += kSliceThreads) sv[i] = row_value(a, row, lo + i, set);
+  uint32_t prefix = 0;
+  int need = k;
+  for (int pass = 0; pass < 2; ++pass) {
+    const int shift = pass == 0 ? 8 : 0;
+    for (int i = tid; i < (kSliceThreads / 32) * 256; i += kSliceThreads) (&hist[0][0])[i] = 0;
+    __syncthreads();
+    for (int i = tid; i < len; i += kSliceThreads) {
+      const uint32_t key = bf16_key(f32_to_bf16_bits(sv[i]));
+      if (pass == 0 || (key >> 8) == (prefix >> 8)) atomicAdd(&hist[warp][(key >> shift) & 0xFFu], 1u);
+    }
+    __syncthreads();
+    for (int b = tid; b < 256; b += kSliceThreads) {
+      unsigned t = 0;
+      for (int w = 0; w < kSliceThreads / 32; ++w) t += hist[w][b];
+      hist[0][b] = t;
+    }
+    __syncthreads();
+    select_bin(&hist[0][0], need, sel, wsum);
+    prefix |= (uint32_t)sel[0] << shift;
+    need = sel[1];
+  }
+  const uint32_t thr = prefix;
+  const int take_eq = need;
+  const int per = (len + kSliceThreads - 1) / kSliceThreads;
+  const int i0 = min(len, tid * per), i1 = min(len, i0 + per);
+  int my_gt = 0, my_eq = 0;
+  for (int i = i0; i < i1; ++i) {
+    const uint32_t key = bf16_key(f32_to_bf16_bits(sv[i]));
+    if (key > thr) ++my_gt;
+    else if (key == thr) ++my_eq;
+  }
+  int tot;
+  const int eq_before = block_excl_scan(my_eq, wsum, &tot);
+  int eq_left = max(0, min(my_eq, take_eq - eq_before));
+  int w = block_excl_scan(my_gt + eq_left, wsum, &tot);
+  float* ov = a.cand_val + ((size_t)r * a.slices + sl) * k;
+  int32_t* oi = a.cand_id + ((size_t)r * a.slices + sl) * k;
+  for (int i = i0; i < i1 && w < k; ++i) {
+    const uint32_t key = bf16_key(f32_to_bf16_bits(sv[i]));
+    bool keep = key > thr;
+    if (!keep && key == thr && eq_left > 0) {
+      keep = true;
+      --eq_left;
+    }
+    if (keep) {
+      ov[w] = sv[i];
+      oi[w] = lo + i;
+      ++w;
+    }
+  }
+}
+
+// CAND: read the row as the slices' candidates (values final, ids listed).
+template <bool CAND>
 __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(const SampleArgs a) {
   __shared__ float cv[kSampleMaxCand];    // candidate values (in id order)
   __shared__ int ci[kSampleMaxCand];      // candidate ids
@@ -178,12 +339,16 @@ __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(const Sampl
   __shared__ int scan[kSampleThreads];
   __shared__ float fred[kSampleThreads / 32];
   __shared__ int sh_int[4];
+  __shared__ int wsum[kSampleThreads / 32];
   pdl_launch_dependents();
   pdl_wait();
   const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint16_t* row = a.logits + (size_t)a.row_index[r] * a.ld;
   const int set = a.seen_set[r];
-  const int n = a.cols;
+  const int n = CAND ? a.slices * a.top_k : a.cols;
+  const float* cand_v = CAND ? a.cand_val + (size_t)r * n : nullptr;
+  const int32_t* cand_i = CAND ? a.cand_id + (size_t)r * n : nullptr;
+  auto value = [&](int c) { return CAND ? cand_v[c] : row_value(a, row, c, set); };
   // ---- threshold of the top-k (key of the k-th largest), radix select on 16 bits
   int k = (a.top_k > 0 && a.top_k < n) ? a.top_k : n;
   uint32_t thr = 0;  // candidates: key > thr, plus (k - count_gt) with key == thr in id order
@@ -196,23 +361,13 @@ __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(const Sampl
       for (int i = tid; i < 256; i += kSampleThreads) hist[i] = 0;
       __syncthreads();
       for (int c = tid; c < n; c += kSampleThreads) {
-        const uint32_t key = bf16_key(f32_to_bf16_bits(row_value(a, row, c, set)));
+        const uint32_t key = bf16_key(f32_to_bf16_bits(value(c)));
         if (pass == 0 || (key >> 8) == (prefix >> 8)) atomicAdd(&hist[(key >> shift) & 0xFFu], 1u);
       }
       __syncthreads();
-      if (tid == 0) {
-        int acc = 0, b = 255;
-        for (; b > 0; --b) {
-          if (acc + (int)hist[b] >= need) break;
-          acc += hist[b];
-        }
-        sh_int[0] = b;
-        sh_int[1] = need - acc;  // still needed from bin b
-      }
-      __syncthreads();
+      select_bin(hist, need, sh_int, wsum);  // sh_int[1]: still needed from bin sh_int[0]
       prefix |= (uint32_t)sh_int[0] << shift;
       need = sh_int[1];
-      __syncthreads();
     }
     thr = prefix;
     take_eq = need;  // elements with key == thr to take (lowest ids first)
@@ -222,7 +377,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(const Sampl
   const int c0 = min(n, tid * per), c1 = min(n, c0 + per);
   int my_gt = 0, my_eq = 0;
   for (int c = c0; c < c1; ++c) {
-    const uint32_t key = bf16_key(f32_to_bf16_bits(row_value(a, row, c, set)));
+    const uint32_t key = bf16_key(f32_to_bf16_bits(value(c)));
     if (k == n || key > thr) ++my_gt;
     else if (key == thr) ++my_eq;
   }
@@ -252,7 +407,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(const Sampl
   int eq_left = my_eq_take;
   if (total <= kSampleMaxCand) {
     for (int c = c0; c < c1; ++c) {
-      const float v = row_value(a, row, c, set);
+      const float v = value(c);
       const uint32_t key = bf16_key(f32_to_bf16_bits(v));
       bool keep = (k == n) || key > thr;
       if (!keep && key == thr && eq_left > 0) {
@@ -261,7 +416,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(const Sampl
       }
       if (keep) {
         cv[w] = v;
-        ci[w] = c;
+        ci[w] = CAND ? cand_i[c] : c;
         ++w;
       }
     }
@@ -360,7 +515,12 @@ __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(const Sampl
 }
 
 cudaError_t launch_sample_rows(const SampleArgs& a, cudaStream_t s) {
-  sample_rows_kernel<<<a.n_rows, kSampleThreads, 0, s>>>(a);
+  if (a.slices > 0) {
+    sample_slices_kernel<<<dim3(a.slices, a.n_rows), kSliceThreads, (size_t)a.slice_len * sizeof(float), s>>>(a);
+    sample_rows_kernel<true><<<a.n_rows, kSampleThreads, 0, s>>>(a);
+  } else {
+    sample_rows_kernel<false><<<a.n_rows, kSampleThreads, 0, s>>>(a);
+  }
   return cudaGetLastError();
 }
 

@@ -125,11 +125,14 @@ def greedy_feed(la: torch.Tensor, two: torch.Tensor, ids_row: torch.Tensor, pos_
 
 def sample_rows(logits: torch.Tensor, rows, *, temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0,
                 penalty: float = 1.0, seen_bits: torch.Tensor | None = None, seen_set=None, excluded=(),
-                seed: int = 0, offset: int = 0, out: torch.Tensor, out_add: int = 0, scan_rows=None) -> torch.Tensor:
+                seed: int = 0, offset: int = 0, out: torch.Tensor, out_add: int = 0, scan_rows=None,
+                sliced: bool = True) -> torch.Tensor:
     """One sampled token per listed row of bf16 ``logits`` [R, V] into out[0:len(rows)] (int64).
     ``scan_rows[i]``: rows of the reference's sample_token call that held
     row i (1 = a one-row call; default all 1), which fixes how its CUDA
-    cumsum rounds the top-p partial sums."""
+    cumsum rounds the top-p partial sums.  ``sliced``: long rows with a
+    top-k are selected by one CTA per slice (same draw; False = one CTA per
+    row)."""
     _bf16(logits, "logits")
     V = logits.shape[-1]
     rows = list(rows)
@@ -139,11 +142,26 @@ def sample_rows(logits: torch.Tensor, rows, *, temperature: float = 1.0, top_k: 
     exa = (ctypes.c_int32 * max(1, len(ex)))(*ex)
     words = seen_bits.shape[-1] if seen_bits is not None else 0
     sr = (ctypes.c_int32 * len(rows))(*(scan_rows if scan_rows is not None else [1] * len(rows)))
+    need = _lib.lib.mtl_sample_scratch_bytes(V, len(rows), int(top_k)) if sliced else 0
+    scratch = _sample_scratch(logits.device, need) if need else None
     _lib.call("mtl_sample_rows", logits.data_ptr(), V, V, len(rows), idx, ctypes.c_float(temperature), int(top_k),
               ctypes.c_float(top_p), ctypes.c_float(penalty), _p(seen_bits), words, sets, exa, len(ex), sr,
               ctypes.c_uint64(seed & 0xFFFFFFFFFFFFFFFF), ctypes.c_uint64(offset), ctypes.c_int64(out_add),
-              out.data_ptr(), _s())
+              out.data_ptr(), _p(scratch), need, _s())
     return out
+
+
+_SAMPLE_SCRATCH: dict = {}
+
+
+def _sample_scratch(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-device candidate buffer of the sliced sampling path (grows only;
+    the text head's row with top-k <= 2048 needs at most 2.4 MB)."""
+    buf = _SAMPLE_SCRATCH.get(device)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 148 * 2048 * 8), dtype=torch.uint8, device=device)
+        _SAMPLE_SCRATCH[device] = buf
+    return buf
 
 
 def rtn_quantize(w: torch.Tensor, group_size: int = 128) -> tuple[torch.Tensor, torch.Tensor]:

@@ -95,6 +95,82 @@ def test_candidates_match_reference_torch_ops_on_cuda(n_rows):
             assert sorted(vals[list(mine)]) == sorted(vals[list(theirs)]), (trial, r, sorted(mine ^ theirs))
 
 
+LONG_CASES = [
+    dict(cols=151936, n=1, top_k=50, top_p=1.0, temperature=1.5),               # text head, reference text defaults
+    dict(cols=151936, n=1, top_k=1, top_p=1.0, temperature=1.0),
+    dict(cols=151936, n=1, top_k=2048, top_p=0.9, temperature=0.8),             # the largest candidate set
+    dict(cols=151936, n=3, top_k=50, top_p=0.95, temperature=1.0, penalty=1.3, excluded=(151643, 151652, 7)),
+    dict(cols=20000, n=2, top_k=1000, top_p=1.0, temperature=1.0),              # few slices, long ones
+    dict(cols=65537, n=1, top_k=25, top_p=0.8, temperature=1.7, ties=True),     # ties across slice boundaries
+]
+
+
+@pytest.mark.parametrize("ci", range(len(LONG_CASES)))
+def test_sliced_long_rows(ci):
+    """Rows of >= 16384 columns with a top-k (the text head): one CTA per
+    slice selects the slice's top-k, then the candidates are sampled.  The
+    draw equals the one-CTA-per-row path bit for bit, and the oracle's."""
+    dev = require_cuda()
+    from moss_tts_lite_b200 import _lib, kernels
+    c = LONG_CASES[ci]
+    V, n = c["cols"], c["n"]
+    assert _lib.lib.mtl_sample_scratch_bytes(V, n, c["top_k"]) > 0
+    rng = np.random.default_rng(500 + ci)
+    x = (rng.standard_normal((n, V)) * 2).astype(np.float32)
+    x[:, rng.integers(0, V, 300)] = -np.inf
+    if c.get("ties"):
+        # 200 copies of the row maximum spread over every slice: the top-k
+        # keeps the lowest ids among them
+        x[:, np.sort(rng.choice(V, 200, replace=False))] = x.max() + 1.0
+    xb = f32_to_bf16(x)
+    xt = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).to(dev)
+    seen = set(rng.integers(0, V, 400).tolist()) | {7}
+    words = (V + 31) // 32
+    bits = np.zeros((1, words), np.int64)
+    for t in seen:
+        bits[0, t >> 5] |= 1 << (t & 31)
+    seen_dev = torch.from_numpy(bits.astype(np.uint32).view(np.int32)).to(dev)
+    pen = c.get("penalty", 1.0)
+    outs = {}
+    for sliced in (True, False):
+        out = torch.empty(n, dtype=torch.long, device=dev)
+        got = []
+        for off in range(1, 9):
+            kernels.sample_rows(xt, list(range(n)), temperature=c["temperature"], top_k=c["top_k"], top_p=c["top_p"],
+                                penalty=pen, seen_bits=seen_dev if pen != 1.0 else None, seen_set=[0] * n,
+                                excluded=c.get("excluded", ()), seed=77, offset=off, out=out, sliced=sliced)
+            got.append(out.cpu().tolist())
+        outs[sliced] = got
+    assert outs[True] == outs[False]
+    mism = 0
+    for oi, off in enumerate(range(1, 9)):
+        for r in range(n):
+            want = osmp.sample_row(xb[r], temperature=c["temperature"], top_k=c["top_k"], top_p=c["top_p"],
+                                   penalty=pen, seen=seen, excluded=c.get("excluded", ()), seed=77, offset=off,
+                                   row=r)
+            mism += int(outs[True][oi][r] != want)
+    assert mism <= 1, mism
+    assert _lib.device_status() == 0
+
+
+def test_sliced_scratch_too_small_is_an_error():
+    dev = require_cuda()
+    from moss_tts_lite_b200 import _lib
+    x = torch.zeros(1, 151936, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(1, dtype=torch.long, device=dev)
+    need = _lib.lib.mtl_sample_scratch_bytes(151936, 1, 50)
+    buf = torch.empty(need, dtype=torch.uint8, device=dev)
+    import ctypes
+    zero, one = (ctypes.c_int32 * 1)(0), (ctypes.c_int32 * 1)(1)
+    args = (x.data_ptr(), 151936, 151936, 1, zero, ctypes.c_float(1.0), 50, ctypes.c_float(1.0), ctypes.c_float(1.0),
+            None, 0, zero, zero, 0, one, 1, 1, 0, out.data_ptr())
+    stream = torch.cuda.current_stream().cuda_stream
+    assert _lib.lib.mtl_sample_rows(*args, buf.data_ptr(), need - 8, stream) == _lib.MTL_E_SCRATCH
+    assert _lib.lib.mtl_sample_rows(*args, buf.data_ptr(), need, stream) == _lib.MTL_OK
+    assert _lib.lib.mtl_sample_rows(*args, None, 0, stream) == _lib.MTL_OK
+    torch.cuda.synchronize()
+
+
 def test_draw_frequencies_follow_probabilities():
     dev = require_cuda()
     from moss_tts_lite_b200 import kernels
