@@ -19,8 +19,11 @@ other.  Here one decode step advances all B streams:
 Each stream's prompt is prefilled into its own cache slice with the
 prefill of the batch-1 engine.  With ``tc=False`` stream s's results equal a
 batch-1 decode of the same stream bit for bit (same kernels, same split-K
-plan); with the tensor-core tiles they agree to within the two W4 kernels'
-fp32 summation orders.
+plan) while the caches hold up to 256 positions (one attention split per
+head either way; past that the batched step splits each head's cache into
+fewer slices than the batch-1 step, which changes the fp32 merge order);
+with the tensor-core tiles they agree to within the two W4 kernels' fp32
+summation orders.
 """
 from __future__ import annotations
 
@@ -70,7 +73,11 @@ class BatchedFastMossTTS:
         self.h_final = torch.zeros(B, H, dtype=bf, device=dev)
         self.two = torch.zeros(B, 2, dtype=bf, device=dev)
         self.la = torch.zeros(B, N_VQ, AUDIO_VOCAB, dtype=bf, device=dev)
-        self.splits = eng.splits
+        # KV splits per (stream, head): about one CTA per SM over all streams
+        # (16 streams x 8 KV heads: one split, each CTA streams its whole
+        # cache slice; the batch-1 engine's 16 splits would launch 2048
+        # short CTAs, one per SM at a time)
+        self.splits = max(1, min(eng.splits, int(148 / (m.n_kv_heads * streams) + 0.5)))
         from . import _lib
         self.attn_scratch = torch.zeros(_lib.attn_scratch_bytes(B, m.n_heads, m.n_kv_heads, self.splits),
                                         dtype=torch.uint8, device=dev)

@@ -188,27 +188,34 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
     const bool bact = bm < M && bc < nch;    // this thread stages real values
     const uint16_t* xrow = a.x + (size_t)min(bm, M - 1) * a.ldx;
     pdl_wait();
-    // (a) RMSNorm statistics per batch row: warp w sums rows 4w..4w+3
+    // (a) RMSNorm statistics per batch row: the 8 lanes that stage row bm
+    //     sum its squares, four independent loads in flight per lane
     if (a.norm_w) {
-      for (int r = 0; r < 4; ++r) {
-        const int m = 4 * (warp - 2) + r;
-        float ss = 0.f;
-        if (m < M) {
-          const uint16_t* xr = a.x + (size_t)m * a.ldx;
-          for (int c = lane; c < K / 8; c += 32) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr) + c);
-            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+      float ss[4] = {0.f, 0.f, 0.f, 0.f};
+      if (bm < M) {
+        const uint4* xr = reinterpret_cast<const uint4*>(a.x + (size_t)bm * a.ldx);
+        const int nc = K / 8, j = lane & 7;
+        for (int c = j; c < nc; c += 32) {
+          uint4 v[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] = c + 8 * e < nc ? __ldg(xr + c + 8 * e) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t u[4] = {v[e].x, v[e].y, v[e].z, v[e].w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const float lo = __uint_as_float(u[q] << 16), hi = __uint_as_float(u[q] & 0xFFFF0000u);
-              ss = fmaf(lo, lo, ss);
-              ss = fmaf(hi, hi, ss);
+              ss[e] = fmaf(lo, lo, ss[e]);
+              ss[e] = fmaf(hi, hi, ss[e]);
             }
           }
         }
-        ss = warp_sum(ss);
-        if (lane == 0 && m < kTcbMaxM) rinv_s[m] = rsqrtf(ss / (float)K + a.norm_eps);
       }
+      float t = (ss[0] + ss[1]) + (ss[2] + ss[3]);
+      t += __shfl_xor_sync(0xFFFFFFFFu, t, 1);
+      t += __shfl_xor_sync(0xFFFFFFFFu, t, 2);
+      t += __shfl_xor_sync(0xFFFFFFFFu, t, 4);
+      if ((lane & 7) == 0 && bm < M) rinv_s[bm] = rsqrtf(t / (float)K + a.norm_eps);
       named_sync(1, 128);
     }
     const float rinv = a.norm_w && bm < M ? rinv_s[bm] : 0.f;
@@ -228,6 +235,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
     // normed bf16 chunks into B buffer `buf`, the row's group sum into sxs
     // (chunk sums added in chunk order, as the one-row kernel does)
     auto stage_b = [&](int buf, const uint4 (&xv)[2], const uint4 (&nv)[2]) {
+      float cs2[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t u[4] = {xv[h].x, xv[h].y, xv[h].z, xv[h].w};
@@ -246,17 +254,24 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
         float s8 = 0.f;
 #pragma unroll
         for (int q = 0; q < 4; ++q) s8 += __uint_as_float(u[q] << 16) + __uint_as_float(u[q] & 0xFFFF0000u);
-        if (bc + h < nch) {
+        if (bc + h < nch)
           *reinterpret_cast<uint4*>(bbuf + buf * bbytes + ((size_t)(bc + h) * kTcbMaxM + bm) * 16) =
               make_uint4(u[0], u[1], u[2], u[3]);
-          csum[bm * 16 + bc + h] = s8;
-        }
+        cs2[h] = s8;
       }
-      // the row's chunks sit in 8 lanes of this warp
-      __syncwarp();
+      // the row's chunk sums sit in 8 lanes of this warp (chunks 2j, 2j + 1
+      // in lane j): gather them, then add in chunk order
+      float cs[16];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        cs[2 * j] = __shfl_sync(0xFFFFFFFFu, cs2[0], (lane & ~7) + j);
+        cs[2 * j + 1] = __shfl_sync(0xFFFFFFFFu, cs2[1], (lane & ~7) + j);
+      }
       if ((lane & 7) == 0) {
         float s = 0.f;
-        for (int c = 0; c < nch; ++c) s += csum[bm * 16 + c];
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          if (c < nch) s += cs[c];
         sxs[buf * kTcbMaxM + bm] = s;
       }
     };
@@ -306,13 +321,17 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
         named_sync(1, 128);
         if (!last) return;
 #pragma unroll
-        for (int m = 0; m < kTcbMaxM; ++m)
-          if (m < M) {
-            float s = 0.f;
-            for (int j = 0; j <= c_hi - c_lo; ++j)
-              s += __ldcg(a.partials + (((size_t)blk * p.maxc + j) * kTcbMaxM + m) * kTcRows + row);
-            yacc[m] = s;
-          }
+        for (int m = 0; m < kTcbMaxM; ++m) yacc[m] = 0.f;
+        // contributor order per row; the rows' loads of one contributor are
+        // independent and issued together
+        for (int j = 0; j <= c_hi - c_lo; ++j) {
+          float v[kTcbMaxM];
+#pragma unroll
+          for (int m = 0; m < kTcbMaxM; ++m)
+            v[m] = m < M ? __ldcg(a.partials + (((size_t)blk * p.maxc + j) * kTcbMaxM + m) * kTcRows + row) : 0.f;
+#pragma unroll
+          for (int m = 0; m < kTcbMaxM; ++m) yacc[m] += v[m];
+        }
       }
 #pragma unroll
       for (int m = 0; m < kTcbMaxM; ++m) {

@@ -155,14 +155,17 @@ def test_argmax_masked_grid_matches_one_cta(cols):
     assert int(sc.count_nonzero()) == 0
 
 
-@pytest.mark.parametrize("s1,rep,streams,stable",[(1, 4, 1, False), (7, 4, 1, True), (64, 4, 1, False),
-                                                     (65, 8, 1, True), (130, 4, 1, False), (641, 4, 2, True),
-                                                     (2000, 4, 1, True), (4096, 2, 1, False), (3000, 8, 2, False)])
-def test_attention_decode_vs_oracle(s1, rep, streams, stable):
+@pytest.mark.parametrize("s1,rep,streams,stable,splits",
+                         [(1, 4, 1, False, 16), (7, 4, 1, True, 16), (64, 4, 1, False, 16), (65, 8, 1, True, 16),
+                          (130, 4, 1, False, 16), (641, 4, 2, True, 16), (2000, 4, 1, True, 16),
+                          (4096, 2, 1, False, 16), (3000, 8, 2, False, 16),
+                          (641, 4, 3, True, 1), (2000, 4, 2, True, 1), (3000, 8, 2, False, 3), (300, 4, 4, False, 1)])
+def test_attention_decode_vs_oracle(s1, rep, streams, stable, splits):
     """Fused q/k-norm + RoPE + append + split-KV attention against the oracle,
-    at cache lengths around the 64-position tiles, GQA ratios 2-8, two
-    streams, with the cache rows past pos poisoned with NaN (masked rows must
-    contribute exactly nothing)."""
+    at cache lengths around the 64-position tiles, GQA ratios 2-8, up to four
+    streams, 16 / 3 / 1 splits per head (one split: a CTA streams its whole
+    cache, as the batched step does), with the cache rows past pos poisoned
+    with NaN (masked rows must contribute exactly nothing)."""
     dev = require_cuda()
     from moss_tts_lite_b200 import _lib, kernels
     rng = np.random.default_rng(s1 + rep)
@@ -177,7 +180,6 @@ def test_attention_decode_vs_oracle(s1, rep, streams, stable):
     qn = f32_to_bf16((1 + 0.1 * rng.standard_normal(D)).astype(np.float32))
     kn = f32_to_bf16((1 + 0.1 * rng.standard_normal(D)).astype(np.float32))
     cos, sin = ost.rope_tables(max_seq, D)
-    splits = 16
     scratch = torch.zeros(_lib.attn_scratch_bytes(streams, nh, nkv, splits), dtype=torch.uint8, device=dev)
     kct, vct = _t(kc, dev, torch.bfloat16), _t(vc, dev, torch.bfloat16)
     out = torch.empty(streams, nh * D, dtype=torch.bfloat16, device=dev)
