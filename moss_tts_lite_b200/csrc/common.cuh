@@ -43,6 +43,12 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 __device__ __forceinline__ float round_bf16(float f) { return bf16_bits_to_f32(f32_to_bf16_bits(f)); }
+// Two floats rounded to bf16 (nearest even) by one packed conversion: lo in
+// bits 0-15, hi in bits 16-31.
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+  const __nv_bfloat162 r = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
 
 // --------------------------------------------------------------- mbarrier ---
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {

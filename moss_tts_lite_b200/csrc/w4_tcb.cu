@@ -78,6 +78,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "memory");
 }
 
+// tcgen05.wait::ld with the loaded registers as operands, so that no use of
+// them can be scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_ld16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
 __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_constant__ TcbArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const TcPlan& p = a.p;
@@ -243,11 +253,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
           const uint32_t nw[4] = {nv[h].x, nv[h].y, nv[h].z, nv[h].w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            // model.py:34-40: bf16(h * rsqrt(var + eps)), then bf16(weight * that)
-            const float v0 = round_bf16(__uint_as_float(nw[q] << 16) * round_bf16(__uint_as_float(u[q] << 16) * rinv));
-            const float v1 = round_bf16(__uint_as_float(nw[q] & 0xFFFF0000u) *
-                                        round_bf16(__uint_as_float(u[q] & 0xFFFF0000u) * rinv));
-            u[q] = (__float_as_uint(v0) >> 16) | (__float_as_uint(v1) & 0xFFFF0000u);
+            // model.py:34-40: bf16(h * rsqrt(var + eps)), then bf16(weight * that);
+            // each pair rounded by one packed conversion (low half = even k)
+            const uint32_t r = bf16x2_rn(__uint_as_float(u[q] << 16) * rinv, __uint_as_float(u[q] & 0xFFFF0000u) * rinv);
+            u[q] = bf16x2_rn(__uint_as_float(nw[q] << 16) * __uint_as_float(r << 16),
+                             __uint_as_float(nw[q] & 0xFFFF0000u) * __uint_as_float(r & 0xFFFF0000u));
           }
         }
         if (!bact) u[0] = u[1] = u[2] = u[3] = 0u;
@@ -260,20 +270,22 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
         cs2[h] = s8;
       }
       // the row's chunk sums sit in 8 lanes of this warp (chunks 2j, 2j + 1
-      // in lane j): gather them, then add in chunk order
-      float cs[16];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        cs[2 * j] = __shfl_sync(0xFFFFFFFFu, cs2[0], (lane & ~7) + j);
-        cs[2 * j + 1] = __shfl_sync(0xFFFFFFFFu, cs2[1], (lane & ~7) + j);
-      }
+      // in lane j): one lane reads the 16 back at once, then adds them in
+      // chunk order
+      if (bc < nch) *reinterpret_cast<float2*>(csum + bm * 16 + bc) = make_float2(cs2[0], cs2[1]);
+      __syncwarp();
       if ((lane & 7) == 0) {
+        const float4* cr = reinterpret_cast<const float4*>(csum + bm * 16);
+        const float4 c4[4] = {cr[0], cr[1], cr[2], cr[3]};
+        const float cs[16] = {c4[0].x, c4[0].y, c4[0].z, c4[0].w, c4[1].x, c4[1].y, c4[1].z, c4[1].w,
+                              c4[2].x, c4[2].y, c4[2].z, c4[2].w, c4[3].x, c4[3].y, c4[3].z, c4[3].w};
         float s = 0.f;
 #pragma unroll
         for (int c = 0; c < 16; ++c)
           if (c < nch) s += cs[c];
         sxs[buf * kTcbMaxM + bm] = s;
       }
+      __syncwarp();
     };
 
     constexpr int lag = kTcBufs - 1;
@@ -354,14 +366,19 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
         }
       }
     };
-    // accumulator of tile j (the oldest in flight) -> yacc
-    auto readback = [&](int j) {
+    // accumulator of tile j (the oldest in flight) -> yacc: the TMEM load is
+    // issued first (readback_issue, before the next tile's dequantisation)
+    // and completed by readback
+    uint32_t d[16];
+    auto readback_issue = [&](int j) {
       const int buf = j % kTcBufs;
       wait_or_bail(&dfull[buf], (j / kTcBufs) & 1);
       tc_fence_after();
-      uint32_t d[16];
       tmem_ld16(trow + (uint32_t)(dcol0 + 16 * buf), d);
-      tmem_wait_ld();
+    };
+    auto readback = [&](int j) {
+      const int buf = j % kTcBufs;
+      tmem_wait_ld16(d);
       float sx[kTcbMaxM];
 #pragma unroll
       for (int m = 0; m < kTcbMaxM; ++m) sx[m] = sxs[buf * kTcbMaxM + m];
@@ -394,6 +411,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
       // B of tile i (its x was loaded an iteration ago), then the next x
       stage_b(buf, xv, nv);
       if (i + 1 < nt) load_b(G + 1 == KT ? 0 : G + 1, xv, nv);
+      if (i >= lag) readback_issue(i - lag);
       wait_or_bail(&full[s], (st / S) & 1);
       const uint8_t* tile = ring + (size_t)s * stage_bytes + (size_t)(i % tps) * p.tile_bytes;
       const uint2* wp = reinterpret_cast<const uint2*>(tile) + row;
@@ -435,7 +453,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
         ++nb;
       }
     }
-    for (int j = max(0, nt - lag); j < nt; ++j) readback(j);
+    for (int j = max(0, nt - lag); j < nt; ++j) {
+      readback_issue(j);
+      readback(j);
+    }
     if (cur >= 0) flush(cur);
   }
   __syncwarp();
