@@ -473,8 +473,17 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
       const int blk = blk_first + bl;
       const int c_lo = cta_of_tile((long long)blk * KT, p.G, p.T);
       const int c_hi = cta_of_tile((long long)(blk + 1) * KT - 1, p.G, p.T);
+      // contributors in order; up to 8 partial loads issued before the adds
+      const int ncon = c_hi - c_lo + 1;
+      const float* pp = a.partials + (size_t)blk * p.maxc * per + r;
+      float pv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) pv[j] = j < ncon ? __ldcg(pp + (size_t)j * per) : 0.f;
       float v = 0.f;
-      for (int j = 0; j <= c_hi - c_lo; ++j) v += __ldcg(a.partials + ((size_t)blk * p.maxc + j) * per + r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j < ncon) v += pv[j];
+      for (int j = 8; j < ncon; ++j) v += __ldcg(pp + (size_t)j * per);
       fin[i] = v;
     }
     consumer_sync();

@@ -132,6 +132,11 @@ __device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// tcgen05.wait::ld with the loaded register as an operand (no use of it can
+// be scheduled before the wait).
+__device__ __forceinline__ void tmem_wait_ld1(uint32_t& r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r) : : "memory");
+}
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 // D[tmem] (+)= A[tmem] . B[smem desc], issued by one thread
@@ -383,8 +388,17 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tc_kernel(const __grid_const
         const int last = imisc[2];
         named_sync(1, 128);  // imisc[2] is reused by the next flush
         if (!last) return;
+        // contributors in order; up to 8 partial loads issued before the adds
+        const int ncon = c_hi - c_lo + 1;
+        const float* pp = a.partials + (size_t)blk * p.maxc * kTcRows + row;
+        float pv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) pv[j] = j < ncon ? __ldcg(pp + (size_t)j * kTcRows) : 0.f;
         float s = 0.f;
-        for (int j = 0; j <= c_hi - c_lo; ++j) s += __ldcg(a.partials + ((size_t)blk * p.maxc + j) * kTcRows + row);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (j < ncon) s += pv[j];
+        for (int j = 8; j < ncon; ++j) s += __ldcg(pp + (size_t)j * kTcRows);
         v = s;
       }
       if (a.epi == kEpiSwiGLU) {
@@ -403,13 +417,20 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tc_kernel(const __grid_const
         a.y[n] = f32_to_bf16_bits(v);
       }
     };
-    // accumulator of tile j (the oldest in flight) -> y
-    auto readback = [&](int j) {
+    // accumulator of tile j (the oldest in flight) -> y: the TMEM load is
+    // issued before the next tile's dequantisation (readback_issue) and
+    // completed after it (readback)
+    uint32_t draw = 0;
+    auto readback_issue = [&](int j) {
       const int buf = j % kTcBufs;
       wait_or_bail(&dfull[buf], (j / kTcBufs) & 1);
       tc_fence_after();
-      const float d = __uint_as_float(tmem_ld1(trow + (uint32_t)(dcol0 + 16 * buf)));
-      tmem_wait_ld();
+      draw = tmem_ld1(trow + (uint32_t)(dcol0 + 16 * buf));
+    };
+    auto readback = [&](int j) {
+      const int buf = j % kTcBufs;
+      tmem_wait_ld1(draw);
+      const float d = __uint_as_float(draw);
       tc_fence_before();
       mbar_arrive(&dfree[buf]);
       if (qB[0] != cur) {
@@ -430,6 +451,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tc_kernel(const __grid_const
 
     for (int i = 0; i < nt; ++i) {
       const int st = i / tps, s = st % S, buf = i % kTcBufs;
+      if (i >= lag) readback_issue(i - lag);
       wait_or_bail(&full[s], (st / S) & 1);
       const uint8_t* tile = ring + (size_t)s * stage_bytes + (size_t)(i % tps) * p.tile_bytes;
       const uint2* wp = reinterpret_cast<const uint2*>(tile) + row;
@@ -474,7 +496,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tc_kernel(const __grid_const
         ++nb;
       }
     }
-    for (int j = max(0, nt - lag); j < nt; ++j) readback(j);
+    for (int j = max(0, nt - lag); j < nt; ++j) {
+      readback_issue(j);
+      readback(j);
+    }
     if (cur >= 0) flush(cur, yacc);  // a bail is reported by the device status word
   }
   __syncwarp();
