@@ -147,6 +147,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
       int issued = 0;
       for (int st = 0; st < nst; ++st) {
         const int s = st % S;
+        // the first stage lands before the rest are requested: every CTA's
+        // first tile is served ahead of the other CTAs' later stages
+        if (st == 1 && !mbar_wait(&full[0], 0)) break;
         if (st >= S && !mbar_wait(&empty[s], ((st / S) - 1) & 1)) break;
         const int ntile = min(tps, nt - st * tps);
         const uint32_t bytes = (uint32_t)(ntile * p.tile_bytes);
