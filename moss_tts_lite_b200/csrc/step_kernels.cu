@@ -106,10 +106,20 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) bf16_gemv_kernel
   for (int m = 0; m < a.M; ++m) {
     const uint16_t* xr = a.x + (size_t)m * a.K;
     float ss = 0.f;
-    for (int k = tid; k < a.K; k += kGemvThreads) {
-      const float v = bf16_bits_to_f32(xr[k]);
-      xs[(size_t)m * a.K + k] = v;
-      ss = fmaf(v, v, ss);
+    // elements tid, tid + 256, ... in order; eight loads issued before use
+    for (int k0 = tid; k0 < a.K; k0 += 8 * kGemvThreads) {
+      uint16_t xb[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xb[e] = k0 + e * kGemvThreads < a.K ? xr[k0 + e * kGemvThreads] : (uint16_t)0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int k = k0 + e * kGemvThreads;
+        if (k < a.K) {
+          const float v = bf16_bits_to_f32(xb[e]);
+          xs[(size_t)m * a.K + k] = v;
+          ss = fmaf(v, v, ss);
+        }
+      }
     }
     if (a.norm_w) {
       ss = warp_sum(ss);
@@ -122,11 +132,20 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) bf16_gemv_kernel
       float ss = 0.f;
       for (int w = 0; w < kGemvThreads / 32; ++w) ss += red[w][m];
       const float rinv = rsqrtf(ss / (float)a.K + a.eps);
-      for (int k = tid; k < a.K; k += kGemvThreads) {
-        // model.py:34-40
-        const float v = round_bf16(bf16_bits_to_f32(a.norm_w[k]) * round_bf16(xs[(size_t)m * a.K + k] * rinv));
-        xs[(size_t)m * a.K + k] = v;
-        if (a.x_normed && blockIdx.x == 0) a.x_normed[(size_t)m * a.K + k] = f32_to_bf16_bits(v);
+      for (int k0 = tid; k0 < a.K; k0 += 8 * kGemvThreads) {
+        uint16_t nb[8];  // norm weights of this thread's next eight elements, loaded together
+#pragma unroll
+        for (int e = 0; e < 8; ++e) nb[e] = k0 + e * kGemvThreads < a.K ? __ldg(a.norm_w + k0 + e * kGemvThreads) : (uint16_t)0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int k = k0 + e * kGemvThreads;
+          if (k < a.K) {
+            // model.py:34-40
+            const float v = round_bf16(bf16_bits_to_f32(nb[e]) * round_bf16(xs[(size_t)m * a.K + k] * rinv));
+            xs[(size_t)m * a.K + k] = v;
+            if (a.x_normed && blockIdx.x == 0) a.x_normed[(size_t)m * a.K + k] = f32_to_bf16_bits(v);
+          }
+        }
       }
     }
     __syncthreads();

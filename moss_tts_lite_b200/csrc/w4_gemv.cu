@@ -35,8 +35,12 @@ namespace mtl {
 
 namespace {
 
+// The CTA whose range [T c / G, T (c + 1) / G) holds tile t.  32-bit
+// arithmetic ((t + 1) G <= T G < 2^32, checked by w4_plan): the fixup calls
+// this on its critical path, where an emulated 64-bit divide costs hundreds
+// of cycles.
 __host__ __device__ __forceinline__ int cta_of_tile(long long t, int G, int T) {
-  return (int)(((t + 1) * (long long)G - 1) / (long long)T);
+  return (int)(((uint32_t)(t + 1) * (uint32_t)G - 1u) / (uint32_t)T);
 }
 
 __host__ __device__ __forceinline__ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -92,8 +96,9 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
   const W4Plan& p = a.p;
   const int M = a.M, g = a.g, KT = p.KT;
   const int cta = blockIdx.x;
-  const int t0 = (int)(((long long)p.T * cta) / p.G);
-  const int t1 = (int)(((long long)p.T * (cta + 1)) / p.G);
+  // stream-K range of this CTA (32-bit: T G < 2^32, checked by the plan)
+  const int t0 = (int)(((uint32_t)p.T * (uint32_t)cta) / (uint32_t)p.G);
+  const int t1 = (int)(((uint32_t)p.T * (uint32_t)(cta + 1)) / (uint32_t)p.G);
   const int nt = t1 - t0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.stages, tps = p.tps;
@@ -204,14 +209,25 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
       float ss = 0.f;
       const uint16_t* xr = a.x + (size_t)m * a.ldx;
       if (a.xvec) {
-        for (int c = tid; c < a.K / 8; c += kW4CThreads) {
-          const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr) + c);
-          const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+        // chunks tid, tid + 256, ... in order; four loads issued before use
+        const int nc = a.K / 8;
+        for (int c0 = tid; c0 < nc; c0 += 4 * kW4CThreads) {
+          uint4 v[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float lo = __uint_as_float(u[q] << 16), hi = __uint_as_float(u[q] & 0xFFFF0000u);
-            ss = fmaf(lo, lo, ss);
-            ss = fmaf(hi, hi, ss);
+          for (int e = 0; e < 4; ++e)
+            v[e] = c0 + e * kW4CThreads < nc ? __ldg(reinterpret_cast<const uint4*>(xr) + c0 + e * kW4CThreads)
+                                             : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (c0 + e * kW4CThreads < nc) {
+              const uint32_t u[4] = {v[e].x, v[e].y, v[e].z, v[e].w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float lo = __uint_as_float(u[q] << 16), hi = __uint_as_float(u[q] & 0xFFFF0000u);
+                ss = fmaf(lo, lo, ss);
+                ss = fmaf(hi, hi, ss);
+              }
+            }
           }
         }
       } else {
@@ -294,8 +310,14 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
   for (int i = tid; i < p.nblk_max * kW4Warps * kNT * M; i += kW4CThreads) part[i] = 0.f;
   consumer_sync();
   for (int job = tid; job < ng * M; job += kW4CThreads) {
+    // the 16-value block sums in order; all loads issued before the adds
+    float bv[16];
+#pragma unroll
+    for (int b = 0; b < 16; ++b) bv[b] = b < nb16 ? bsum[job * nb16 + b] : 0.f;
     float s = 0.f;
-    for (int b = 0; b < nb16; ++b) s += bsum[job * nb16 + b];
+#pragma unroll
+    for (int b = 0; b < 16; ++b)
+      if (b < nb16) s += bv[b];
     gsum[job] = s;
   }
   consumer_sync();
@@ -530,10 +552,11 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
 }  // namespace
 
 int w4_plan(int M, int K, int N, int g, int fmt, int num_sms, W4Plan* out) {
-  if (M < 1 || M > kW4MaxM || K <= 0 || N <= 0 || (N % kNT) || (K % g) || (g % 16)) return -1;
+  if (M < 1 || M > kW4MaxM || K <= 0 || N <= 0 || (N % kNT) || (K % g) || (g % 16) || g > 256) return -1;
   W4Plan p{};
   p.KT = K / g;
   p.nblocks = N / kNT;
+  if ((long long)p.nblocks * p.KT * 2 * num_sms >= (1ll << 32)) return -1;  // cta_of_tile's 32-bit range
   p.T = p.nblocks * p.KT;
   p.tile_bytes = tile_bytes(g, fmt);
   // ~16 KB per bulk copy (large copies stream markedly better than 4 KB ones)

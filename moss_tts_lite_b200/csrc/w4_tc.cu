@@ -80,8 +80,10 @@ inline int tc_tile_bytes(int g) { return kTcRows * g / 2 + kTcRows * 4; }
 
 namespace {
 
+// The CTA whose stream-K range holds tile t (32-bit: (t + 1) G <= T G < 2^32,
+// checked by w4_tc_plan).
 __host__ __device__ __forceinline__ int tc_cta_of_tile(long long t, int G, int T) {
-  return (int)(((t + 1) * (long long)G - 1) / (long long)T);
+  return (int)(((uint32_t)(t + 1) * (uint32_t)G - 1u) / (uint32_t)T);
 }
 __host__ __device__ __forceinline__ size_t tc_align(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -168,8 +170,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tc_kernel(const __grid_const
   const TcPlan& p = a.p;
   const int K = a.K, g = a.g, KT = p.KT, KS = g >> 4;
   const int cta = blockIdx.x;
-  const int t0 = (int)(((long long)p.T * cta) / p.G);
-  const int t1 = (int)(((long long)p.T * (cta + 1)) / p.G);
+  // stream-K range of this CTA (32-bit: T G < 2^32, checked by the plan)
+  const int t0 = (int)(((uint32_t)p.T * (uint32_t)cta) / (uint32_t)p.G);
+  const int t1 = (int)(((uint32_t)p.T * (uint32_t)(cta + 1)) / (uint32_t)p.G);
   const int nt = t1 - t0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.stages, tps = p.tps;
@@ -576,6 +579,7 @@ int w4_tc_plan(int K, int N, int g, int num_sms, TcPlan* out) {
   TcPlan p{};
   p.KT = K / g;
   p.nblocks = N / kTcRows;
+  if ((long long)p.nblocks * p.KT * 2 * num_sms >= (1ll << 32)) return -1;  // tc_cta_of_tile's 32-bit range
   p.T = p.nblocks * p.KT;
   p.tile_bytes = tc_tile_bytes(g);
   p.tps = 1;

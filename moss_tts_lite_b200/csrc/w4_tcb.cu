@@ -93,8 +93,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
   const TcPlan& p = a.p;
   const int K = a.K, g = a.g, KT = p.KT, KS = g >> 4, M = a.M;
   const int cta = blockIdx.x;
-  const int t0 = (int)(((long long)p.T * cta) / p.G);
-  const int t1 = (int)(((long long)p.T * (cta + 1)) / p.G);
+  // stream-K range of this CTA (32-bit: T G < 2^32, checked by the plan)
+  const int t0 = (int)(((uint32_t)p.T * (uint32_t)cta) / (uint32_t)p.G);
+  const int t1 = (int)(((uint32_t)p.T * (uint32_t)(cta + 1)) / (uint32_t)p.G);
   const int nt = t1 - t0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.stages, tps = p.tps;
