@@ -73,3 +73,31 @@ def test_linear_rejects_null_and_small_scratch():
     rc = _lib.lib.mtl_w4a16_linear(fake, 4096, 1, 4096, 4096, 128, 0, fake, 0, None, None,
                                    ctypes.c_float(1e-6), 9, None, fake, 4096, fake, 1 << 30, None)
     assert rc == -1 and "epilogue" in _lib.last_error()
+
+
+@pytest.mark.parametrize("cols,rows,top_k,slices", [
+    (151936, 1, 50, 148),     # the text head at the reference's text top-k: 148 slices of 1027
+    (151936, 1, 2048, 72),    # the largest candidate set: every slice (the last included) >= 2048
+    (151936, 3, 1, 148),
+    (20000, 2, 1000, 19),
+    (16384, 1, 16, 16),
+    (1025, 32, 50, 0),        # audio rows: one CTA per row, no scratch
+    (151936, 1, 0, 0),        # no top-k: no slicing
+    (151936, 1, 151936, 0),
+])
+def test_sample_scratch_bytes(cols, rows, top_k, slices):
+    """mtl_sample_scratch_bytes (host only): (value, id) per candidate of
+    every slice; slices of equal length with the last one at least top_k."""
+    from moss_tts_lite_b200 import _lib
+    got = _lib.lib.mtl_sample_scratch_bytes(cols, rows, top_k)
+    assert got == rows * slices * top_k * 8
+    if slices:
+        sl = -(-cols // slices)
+        assert cols - (slices - 1) * sl >= top_k and sl <= 8192
+
+
+def test_plan_rejects_tile_counts_past_32_bit_owner_math():
+    """The stream-K owner arithmetic is 32-bit: T x CTAs < 2^32 or the plan fails."""
+    from moss_tts_lite_b200 import _lib
+    with pytest.raises(_lib.MtlError):
+        _lib.w4_plan(1, 16384 * 128, 64 * 8192, 32, 0)
