@@ -685,6 +685,7 @@ def main():
     ap.add_argument("--profile-gemv", action="store_true", help="small config-0 GEMV case for ncu")
     ap.add_argument("--profile-attn", action="store_true", help="decode attention alone (config 2 heads)")
     ap.add_argument("--profile-attn-launches", action="store_true", help="4 plain attention launches (ncu case)")
+    ap.add_argument("--attn-len", type=int, default=136, help="cache length of the plain attention launches")
     ap.add_argument("--profile-heads", action="store_true", help="text-head bf16 GEMV alone (ncu case)")
     ap.add_argument("--profile-cfg4", action="store_true", help="2 batched configuration-4 steps in an NVTX range")
     args = ap.parse_args()
@@ -698,7 +699,8 @@ def main():
         profile_gemv()
         return
     if args.profile_attn or args.profile_attn_launches:
-        profile_attn(timed=args.profile_attn)
+        lengths = (args.attn_len,) + tuple(L for L in (136, 1024, 4096, 8191) if L != args.attn_len)
+        profile_attn(timed=args.profile_attn, lengths=lengths)
         return
     ctx = _Dist()
     if args.impl == "reference":
