@@ -6,9 +6,9 @@
  *
  * All tensor pointers are device pointers unless stated otherwise.  bf16
  * and fp16 values are passed as uint16_t bit patterns.  Nothing here
- * synchronises the stream or allocates device memory, so every entry point
- * except the mtl_w4_plan/mtl_device_status helpers can be captured in a
- * CUDA graph.
+ * synchronises the stream or allocates device memory; the entry points that
+ * take caller buffers (all but the mtl_w4_plan/mtl_device_status helpers and
+ * mtl_w4a16_linear_noalloc) can be captured in a CUDA graph.
  */
 #ifndef MTL_B200_H
 #define MTL_B200_H

@@ -80,7 +80,7 @@ extern "C" int mtl_w4a16_linear_noalloc(const uint16_t* x, int ldx, int M, int K
     return fail(MTL_E_CUDA, "mtl_w4a16_linear_noalloc: cannot resolve the device scratch array (error %d)", err);
   // The split-K counters must start at zero.  A completed launch leaves them
   // zero, but clear them anyway so an interrupted earlier call cannot leak
-  // into this one (a memset node: no allocation, capturable).
+  // into this one (a memset on the caller's stream allocates nothing).
   cudaError_t e = cudaMemsetAsync(scratch, 0, counters_bytes(N), stream);
   if (e != cudaSuccess) return cuda_fail(e, "mtl_w4a16_linear_noalloc: clear counters");
   return mtl_w4a16_linear(x, ldx, M, K, N, group_size, param_fmt, tiles, zero_offset, k_perm, norm_w, norm_eps,
