@@ -405,14 +405,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   // ---- the last split to finish merges all splits in split order
   __syncthreads();
   if (tid == 0) {
-    __threadfence();
+    // release this split's records (ordered before by the barrier) and, for
+    // the last split, acquire the others'
     int* ctr = a.counters + (size_t)st * a.nkv + h;
-    const int old = atomicAdd(ctr, 1);
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(ctr) : "memory");
     sh_flag[1] = (old == a.splits - 1);
-    if (sh_flag[1]) {
-      __threadfence();
-      *ctr = 0;
-    }
+    if (sh_flag[1]) *ctr = 0;  // re-armed for the next launch
   }
   __syncthreads();
   if (!sh_flag[1]) return;
