@@ -408,20 +408,27 @@ def cpu_baseline(reps: int = 3):
 
 # ------------------------------------------------------------------- main
 class _Dist:
+    """One process per GPU (torchrun env): the replicas share nothing on the
+    data path; the process group only aligns the timed regions (barrier) and
+    takes the max over ranks of the device times.  NCCL on the GPU box; gloo
+    (host tensors) for the CPU tests of this logic."""
+
     def __init__(self):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         self.pg = None
+        self.device = "cuda"
 
-    def init(self):
+    def init(self, backend: str = "nccl"):
         if self.world > 1:
             import datetime
             import torch.distributed as dist
             import torch
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                    device_id=torch.device("cuda", self.local))
+            kw = {"device_id": torch.device("cuda", self.local)} if backend == "nccl" else {}
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
             self.pg = dist
+            self.device = "cuda" if backend == "nccl" else "cpu"
 
     def barrier(self):
         if self.pg is not None:
@@ -431,7 +438,7 @@ class _Dist:
         if self.pg is None:
             return v
         import torch
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        t = torch.tensor([v], dtype=torch.float64, device=self.device)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
