@@ -111,11 +111,13 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ model
-def build_fast(dev, seed: int):
-    """Random-init (seeded) full-size synthetic model -> FastMossTTS(quant='w4')."""
+def synth_weights(dev, seed: int) -> dict:
+    """Seeded random-init checkpoint of the configuration-2 model under the
+    reference key names (model.py:55-105): the seven linears of every layer,
+    the text embedding / head and the 32 audio embeddings / heads ~ N(0, 0.02)
+    in bf16, norm weights 1."""
     import torch
-    from moss_tts_lite_b200.fast import FastMossTTS
-    from moss_tts_lite_b200.model import N_VQ, MossTTSModel
+    from moss_tts_lite_b200.model import N_VQ
     c = CFG
     H, D = c["hidden"], c["head_dim"]
     g = torch.Generator(device=dev)
@@ -144,9 +146,18 @@ def build_fast(dev, seed: int):
     w["lm_heads.0.weight"] = r(c["vocab"], H)
     for i in range(N_VQ):
         w[f"lm_heads.{i + 1}.weight"] = r(1025, H)
-    model = MossTTSModel(w, device=dev, max_seq_len=MAX_SEQ)
+    return w
+
+
+def build_fast(dev, seed: int, max_seq: int = None):
+    """Random-init (seeded) full-size synthetic model -> FastMossTTS(quant='w4')."""
+    import torch
+    from moss_tts_lite_b200.fast import FastMossTTS
+    from moss_tts_lite_b200.model import MossTTSModel
+    w = synth_weights(dev, seed)
+    model = MossTTSModel(w, device=dev, max_seq_len=max_seq or MAX_SEQ)
     del w
-    fast = FastMossTTS(model, quant="w4", w4_group_size=c["group_size"])
+    fast = FastMossTTS(model, quant="w4", w4_group_size=CFG["group_size"])
     torch.cuda.synchronize()
     return fast
 
@@ -636,33 +647,7 @@ def run_reference_gpu(args, ctx):
     dev = torch.device("cuda", ctx.local)
     torch.cuda.set_device(dev)
     c = CFG
-    H, D = c["hidden"], c["head_dim"]
-    g = torch.Generator(device=dev)
-    g.manual_seed(c["seed"])
-
-    def r(*shape):
-        return (torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * c["std"]).to(torch.bfloat16)
-
-    ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=dev)  # noqa: E731
-    w = {"language_model.embed_tokens.weight": r(c["vocab"], H), "language_model.norm.weight": ones(H)}
-    for li in range(c["n_layers"]):
-        p = f"language_model.layers.{li}"
-        w[f"{p}.input_layernorm.weight"] = ones(H)
-        w[f"{p}.post_attention_layernorm.weight"] = ones(H)
-        w[f"{p}.self_attn.q_proj.weight"] = r(c["n_heads"] * D, H)
-        w[f"{p}.self_attn.k_proj.weight"] = r(c["n_kv"] * D, H)
-        w[f"{p}.self_attn.v_proj.weight"] = r(c["n_kv"] * D, H)
-        w[f"{p}.self_attn.o_proj.weight"] = r(H, c["n_heads"] * D)
-        w[f"{p}.self_attn.q_norm.weight"] = ones(D)
-        w[f"{p}.self_attn.k_norm.weight"] = ones(D)
-        w[f"{p}.mlp.gate_proj.weight"] = r(c["inter"], H)
-        w[f"{p}.mlp.up_proj.weight"] = r(c["inter"], H)
-        w[f"{p}.mlp.down_proj.weight"] = r(H, c["inter"])
-    for i in range(32):
-        w[f"emb_ext.{i}.weight"] = r(1025, H)
-    w["lm_heads.0.weight"] = r(c["vocab"], H)
-    for i in range(32):
-        w[f"lm_heads.{i + 1}.weight"] = r(1025, H)
+    w = synth_weights(dev, c["seed"])
     model = RefModel(w, device=dev, dtype=torch.bfloat16, max_seq_len=MAX_SEQ)
     del w
     fast = RefFast(model, quant="w4", w4_group_size=c["group_size"])
@@ -710,6 +695,8 @@ def main():
         profile_attn(timed=args.profile_attn, lengths=lengths)
         return
     ctx = _Dist()
+    if ctx.world > 1 and args.gpus != ctx.world:
+        raise SystemExit(f"--gpus {args.gpus} does not match the {ctx.world} ranks torchrun started")
     if args.impl == "reference":
         run_reference_arm(args, ctx)
         return
@@ -730,11 +717,11 @@ def main():
     ms, clocks = time_decode_loop(fast, steps, warmup, ctx)
     ms = ctx.max(ms)
     ms_per_step = ms / steps
-    value = args.gpus * steps / (ms * 1e-3)
+    value = ctx.world * steps / (ms * 1e-3)
     bytes_per_launch, s_per_launch, launches = time_w4_gemvs(fast)
     e2e, e2e_steps, e2e_relaunches = time_e2e(fast, prompt.to("cpu"), steps, warmup)
     e2e_all = ctx.max(-(e2e or 0.0))  # slowest rank
-    e2e_val = args.gpus * (-e2e_all) if e2e else None
+    e2e_val = ctx.world * (-e2e_all) if e2e else None
     peak, peak_kind = _peaks()
     achieved = bytes_per_launch / s_per_launch / 1e9
     traffic = _ncu_traffic()

@@ -621,6 +621,12 @@ def generate_fast(
     audio_do_sample = audio_temperature > 0
     if not audio_do_sample:
         audio_temperature = 1
+    if text_do_sample:
+        from .sampling import check_top_k
+        check_top_k(text_top_k, model.text_vocab, "generate_fast text decisions")
+    if audio_do_sample:
+        from .sampling import check_top_k
+        check_top_k(audio_top_k, AUDIO_VOCAB, "generate_fast audio decisions")
     cfg = fsm.GenConfig.make(text_do_sample, audio_do_sample, watchdog, watchdog_silence_frames,
                              watchdog_max_segment_frames, max_requested_pause_s)
     st = fsm.FsmState.from_prompt(input_ids[0, :, 0].tolist())

@@ -1,12 +1,18 @@
 """MOSS-TTS backbone container and eager decode on the B200 kernels.
 
-Mirrors ``moss_tts_lite.model`` (constants, ``HiddenState`` and
-``MossTTSModel``, model.py:10-295): same constructor, same tensors under the
-same attribute names (so ``FastMossTTS`` accepts either this class or the
-reference's), same ``prefill / step / text_logits / text_logits_2way /
-audio_logits`` signatures and errors.  The difference is where the math runs:
-``step`` and ``prefill`` drive this package's sm_100a kernels (bf16 weights)
-instead of torch ops.
+Interface-compatible with ``moss_tts_lite.model`` (model.py:10-295): the
+special-token constants, ``HiddenState`` and a ``MossTTSModel`` that takes a
+checkpoint dict under the reference's key names and exposes its tensors under
+the reference's attribute names (``embed_tokens``, ``layers[i]["q"]``,
+``emb_ext``, ``head_audio``, ``k_cache`` ...), so ``FastMossTTS`` accepts
+either this class or the reference's.  ``prefill`` / ``step`` /
+``text_logits`` / ``text_logits_2way`` / ``audio_logits`` keep their
+signatures; the arithmetic runs on this package's sm_100a kernels (bf16
+weights).
+
+The container itself is table-driven: ``_LAYER_TENSORS`` maps every per-layer
+slot to its checkpoint key, ``ModelDims`` derives the architecture from the
+tensor shapes once, and every tensor is placed on the device by one helper.
 """
 from __future__ import annotations
 
@@ -33,6 +39,33 @@ RMS_EPS = 1e-6
 
 LIN_NAMES = ("q", "k", "v", "o", "gate", "up", "down")
 
+# per-layer slot -> checkpoint key suffix under "language_model.layers.<i>."
+_LAYER_TENSORS = {
+    "input_layernorm": "input_layernorm.weight",
+    "q": "self_attn.q_proj.weight",
+    "k": "self_attn.k_proj.weight",
+    "v": "self_attn.v_proj.weight",
+    "o": "self_attn.o_proj.weight",
+    "q_norm": "self_attn.q_norm.weight",
+    "k_norm": "self_attn.k_norm.weight",
+    "post_attention_layernorm": "post_attention_layernorm.weight",
+    "gate": "mlp.gate_proj.weight",
+    "up": "mlp.up_proj.weight",
+    "down": "mlp.down_proj.weight",
+}
+_LAYER_PREFIX = "language_model.layers."
+_EMBED_KEY = "language_model.embed_tokens.weight"
+_FINAL_NORM_KEY = "language_model.norm.weight"
+_TEXT_HEAD_KEY = "lm_heads.0.weight"
+
+
+def _audio_emb_key(c: int) -> str:
+    return f"emb_ext.{c}.weight"
+
+
+def _audio_head_key(c: int) -> str:
+    return f"lm_heads.{c + 1}.weight"
+
 
 @dataclass
 class HiddenState:
@@ -41,22 +74,54 @@ class HiddenState:
     last_hidden: torch.Tensor
 
 
+@dataclass(frozen=True)
+class ModelDims:
+    """Architecture read off the checkpoint's tensor shapes."""
+
+    n_layers: int
+    hidden_size: int
+    text_vocab: int
+    head_dim: int
+    n_heads: int
+    n_kv_heads: int
+
+    @staticmethod
+    def infer(weights: dict) -> "ModelDims":
+        ids = set()
+        for key in weights:
+            if key.startswith(_LAYER_PREFIX):
+                ids.add(int(key[len(_LAYER_PREFIX):].split(".", 1)[0]))
+        n = len(ids)
+        if sorted(ids) != list(range(n)):
+            raise ValueError(f"layer indices must run 0..n-1 without gaps, found {sorted(ids)}")
+        vocab, hidden = (int(d) for d in weights[_EMBED_KEY].shape)
+        l0 = _LAYER_PREFIX + "0."
+        hd = int(weights[l0 + _LAYER_TENSORS["q_norm"]].shape[0])
+        nh = int(weights[l0 + _LAYER_TENSORS["q"]].shape[0]) // hd
+        nkv = int(weights[l0 + _LAYER_TENSORS["k"]].shape[0]) // hd
+        if nkv <= 0 or nh % nkv:
+            raise ValueError(f"{nh} query heads cannot be grouped over {nkv} key/value heads")
+        return ModelDims(n, hidden, vocab, hd, nh, nkv)
+
+
 def rope_tables(n: int, dev, dtype, head_dim: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """RoPE cos/sin for ``n`` positions: the fp32 chain of model.py:115-124
-    (theta 1e6), cast to ``dtype``.  Set-up only."""
-    inv = 1.0 / (ROPE_THETA ** (torch.arange(0, head_dim, 2, dtype=torch.float32, device=dev) / head_dim))
-    pos = torch.arange(n, device=dev, dtype=torch.float32)
-    freqs = torch.outer(pos, inv)
-    emb2 = torch.cat((freqs, freqs), dim=-1)
-    return emb2.cos().to(dtype), emb2.sin().to(dtype)
+    """RoPE cos/sin for ``n`` positions.  The values must equal the
+    reference's bit for bit (model.py:115-124), so the fp32 chain is the
+    same: inverse frequencies theta^(-2i/d), outer product with the position,
+    the half repeated, cos/sin in fp32, then the cast.  Set-up only."""
+    exponents = torch.arange(0, head_dim, 2, dtype=torch.float32, device=dev) / head_dim
+    inv_freq = 1.0 / (ROPE_THETA ** exponents)
+    angles = torch.outer(torch.arange(n, device=dev, dtype=torch.float32), inv_freq)
+    angles = torch.cat((angles, angles), dim=-1)
+    return angles.cos().to(dtype), angles.sin().to(dtype)
 
 
 class MossTTSModel:
     """MossTTSDelayModel weights + KV cache, decoded by the sm_100a kernels.
 
-    ``weights`` uses the checkpoint key names of model.py:55-105.  Only
-    ``dtype=torch.bfloat16`` on a CUDA device is served (the kernels are
-    bf16 / sm_100a only)."""
+    ``weights`` is a checkpoint dict under the reference key names
+    (``language_model.*``, ``emb_ext.<c>``, ``lm_heads.<i>``).  Only
+    ``dtype=torch.bfloat16`` on a CUDA device is served."""
 
     def __init__(self, weights: dict, device="cuda", dtype=torch.bfloat16, max_seq_len=8192):
         dev = torch.device(device)
@@ -64,83 +129,62 @@ class MossTTSModel:
             raise ValueError("moss_tts_lite_b200.MossTTSModel runs on CUDA (sm_100a) only")
         if dtype != torch.bfloat16:
             raise ValueError("moss_tts_lite_b200.MossTTSModel computes in bfloat16 only")
-        self.device = dev
-        self.dtype = dtype
-        self.max_seq_len = max_seq_len
-        layer_ids = sorted({int(k.split(".")[2]) for k in weights if k.startswith("language_model.layers.")})
-        self.n_layers = len(layer_ids)
-        if layer_ids != list(range(self.n_layers)):
-            raise ValueError(f"unexpected layer ids {layer_ids}")
-        emb = weights["language_model.embed_tokens.weight"]
-        self.hidden_size = int(emb.shape[1])
-        self.text_vocab = int(emb.shape[0])
-        self.head_dim = int(weights["language_model.layers.0.self_attn.q_norm.weight"].shape[0])
-        self.n_heads = int(weights["language_model.layers.0.self_attn.q_proj.weight"].shape[0]) // self.head_dim
-        self.n_kv_heads = int(weights["language_model.layers.0.self_attn.k_proj.weight"].shape[0]) // self.head_dim
-        if self.n_heads % self.n_kv_heads != 0:
-            raise ValueError("num_attention_heads must be divisible by num_key_value_heads")
-        self.n_rep = self.n_heads // self.n_kv_heads
+        dims = ModelDims.infer(weights)
+        self.dims = dims
+        self.device, self.dtype, self.max_seq_len = dev, dtype, int(max_seq_len)
+        self.n_layers, self.hidden_size, self.text_vocab = dims.n_layers, dims.hidden_size, dims.text_vocab
+        self.head_dim, self.n_heads, self.n_kv_heads = dims.head_dim, dims.n_heads, dims.n_kv_heads
+        self.n_rep = dims.n_heads // dims.n_kv_heads
 
-        def T(name: str) -> torch.Tensor:
-            t = weights[name]
-            if t.device != dev or t.dtype != dtype:
-                t = t.to(device=dev, dtype=dtype)
-            return t.contiguous()
-
-        self.embed_tokens = T("language_model.embed_tokens.weight")
-        self.final_norm = T("language_model.norm.weight")
-        self.layers = []
-        for i in layer_ids:
-            p = f"language_model.layers.{i}"
-            self.layers.append({
-                "input_layernorm": T(f"{p}.input_layernorm.weight"),
-                "q": T(f"{p}.self_attn.q_proj.weight"),
-                "k": T(f"{p}.self_attn.k_proj.weight"),
-                "v": T(f"{p}.self_attn.v_proj.weight"),
-                "o": T(f"{p}.self_attn.o_proj.weight"),
-                "q_norm": T(f"{p}.self_attn.q_norm.weight"),
-                "k_norm": T(f"{p}.self_attn.k_norm.weight"),
-                "post_attention_layernorm": T(f"{p}.post_attention_layernorm.weight"),
-                "gate": T(f"{p}.mlp.gate_proj.weight"),
-                "up": T(f"{p}.mlp.up_proj.weight"),
-                "down": T(f"{p}.mlp.down_proj.weight"),
-            })
-        # The 32 audio embedding tables live in one buffer (the embedding
-        # kernel indexes it as [32 * 1025, H]); emb_ext are views into it.
-        self.emb_audio = torch.stack([T(f"emb_ext.{i}.weight") for i in range(N_VQ)], 0).contiguous()
-        self.emb_ext = [self.emb_audio[i] for i in range(N_VQ)]
-        self.head_text = T("lm_heads.0.weight")
-        self.head_audio = torch.stack([weights[f"lm_heads.{i + 1}.weight"] for i in range(N_VQ)], dim=0) \
-            .to(device=dev, dtype=dtype).contiguous()
+        place = self._placer(weights)
+        self.embed_tokens = place(_EMBED_KEY)
+        self.final_norm = place(_FINAL_NORM_KEY)
+        self.layers = [{slot: place(f"{_LAYER_PREFIX}{li}.{key}") for slot, key in _LAYER_TENSORS.items()}
+                       for li in range(dims.n_layers)]
+        # the 32 audio embedding tables and heads each live in one stacked
+        # buffer (the kernels index them as [32 * 1025, H]); emb_ext are views
+        self.emb_audio = torch.stack([place(_audio_emb_key(c)) for c in range(N_VQ)]).contiguous()
+        self.emb_ext = list(self.emb_audio.unbind(0))
+        self.head_text = place(_TEXT_HEAD_KEY)
+        self.head_audio = torch.stack([place(_audio_head_key(c)) for c in range(N_VQ)]).contiguous()
         self.head_2way = self.head_text[[AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_DELAY_SLOT_TOKEN_ID]].contiguous()
-        self.rope_cos, self.rope_sin = rope_tables(max_seq_len, dev, dtype, self.head_dim)
-        self.k_cache = torch.zeros(self.n_layers, self.n_kv_heads, max_seq_len, self.head_dim,
-                                   dtype=dtype, device=dev)
-        self.v_cache = torch.zeros_like(self.k_cache)
+        self.rope_cos, self.rope_sin = rope_tables(self.max_seq_len, dev, dtype, dims.head_dim)
+        self.k_cache, self.v_cache = self._new_cache(self.max_seq_len)
         self._seq = 0
         self._engine = None
 
+    def _placer(self, weights: dict):
+        dev, dtype = self.device, self.dtype
+
+        def place(key: str) -> torch.Tensor:
+            if key not in weights:
+                raise KeyError(f"checkpoint has no tensor {key!r}")
+            return weights[key].to(device=dev, dtype=dtype).contiguous()
+        return place
+
+    def _new_cache(self, positions: int):
+        shape = (self.n_layers, self.n_kv_heads, positions, self.head_dim)
+        k = torch.zeros(shape, dtype=self.dtype, device=self.device)
+        return k, torch.zeros_like(k)
+
     # ---------------------------------------------------------------- state
     def ensure_seq_len(self, n: int) -> int:
-        """Grow the KV cache + rope tables so ``n`` positions fit (model.py:126-147)."""
-        n = int(n)
-        if n <= self.max_seq_len:
-            return self.max_seq_len
-        if self._seq > self.max_seq_len:
-            raise RuntimeError(f"live sequence {self._seq} exceeds cache {self.max_seq_len}; cannot grow")
-        old = self.max_seq_len
-        ck = torch.zeros(self.n_layers, self.n_kv_heads, n, self.head_dim, dtype=self.dtype, device=self.device)
-        cv = torch.zeros_like(ck)
-        ck[:, :, :old].copy_(self.k_cache)
-        cv[:, :, :old].copy_(self.v_cache)
-        cos, sin = rope_tables(n, self.device, self.dtype, self.head_dim)
-        cos[:old].copy_(self.rope_cos)
-        sin[:old].copy_(self.rope_sin)
-        self.k_cache, self.v_cache = ck, cv
-        self.rope_cos, self.rope_sin = cos, sin
-        self.max_seq_len = n
-        self._engine = None
-        return n
+        """Make room for ``n`` positions (reference model.py:126-147): a larger
+        cache with the live rows carried over, and RoPE tables recomputed for
+        the new length (the fp32 chain gives the old rows the same values)."""
+        want = int(n)
+        if want > self.max_seq_len:
+            if self._seq > self.max_seq_len:
+                raise RuntimeError(f"cannot grow: {self._seq} live positions do not fit the current "
+                                   f"cache of {self.max_seq_len}")
+            k, v = self._new_cache(want)
+            k[:, :, :self.max_seq_len] = self.k_cache
+            v[:, :, :self.max_seq_len] = self.v_cache
+            self.k_cache, self.v_cache = k, v
+            self.rope_cos, self.rope_sin = rope_tables(want, self.device, self.dtype, self.head_dim)
+            self.max_seq_len = want
+            self._engine = None
+        return self.max_seq_len
 
     @property
     def seq_len(self) -> int:
@@ -156,72 +200,70 @@ class MossTTSModel:
             self._engine = _StepEngine(self, bf16_linears(self))
         return self._engine
 
-    def _check_ids(self, ids: torch.Tensor, t: int) -> torch.Tensor:
-        if ids.shape[0] != 1 or ids.shape[-1] != N_VQ + 1 or ids.shape[1] != t:
-            raise ValueError(f"expected input ids [1, {t}, {N_VQ + 1}], got {tuple(ids.shape)}")
-        if self._seq + t > self.max_seq_len:
-            raise ValueError(f"seq len {self._seq + t} exceeds KV cache {self.max_seq_len}")
-        return ids.to(device=self.device, dtype=torch.long)
+    def _rows(self, ids: torch.Tensor, start: int) -> torch.Tensor:
+        """Validated id rows [L, 33] on the device for positions start.. ."""
+        shape = tuple(ids.shape)
+        if len(shape) != 3 or shape[0] != 1 or shape[2] != N_VQ + 1:
+            raise ValueError(f"input ids must be [1, L, {N_VQ + 1}], got {shape}")
+        if start + shape[1] > self.max_seq_len:
+            raise ValueError(f"{start + shape[1]} positions do not fit the KV cache of {self.max_seq_len}")
+        return ids[0].to(device=self.device, dtype=torch.long)
 
     @torch.inference_mode()
     def prefill(self, input_ids: torch.Tensor) -> HiddenState:
-        """input_ids [1, L, 33] -> final-normed hidden [1, L, H] (model.py:206-219)."""
-        if input_ids.dim() != 3 or input_ids.shape[0] != 1 or input_ids.shape[-1] != N_VQ + 1:
-            raise ValueError(f"expected input ids [1, L, {N_VQ + 1}], got {tuple(input_ids.shape)}")
-        t = int(input_ids.shape[1])
+        """Prompt [1, L, 33] from position 0 -> final-normed hidden [1, L, H]
+        (reference model.py:206-219)."""
         self.reset()
-        ids = self._check_ids(input_ids, t)
-        h = self._eng().prefill_rows(ids[0])
-        self._seq = t
-        return HiddenState(h.view(1, t, self.hidden_size))
+        rows = self._rows(input_ids, 0)
+        h = self._eng().prefill_rows(rows)
+        self._seq = int(rows.shape[0])
+        return HiddenState(h.view(1, self._seq, self.hidden_size))
 
     @torch.inference_mode()
     def step(self, row: torch.Tensor) -> HiddenState:
-        """One decode step (model.py:221-233): row [1, 1, 33] or [1, 33]."""
-        if row.dim() == 2:
-            row = row.unsqueeze(0)
-        ids = self._check_ids(row, 1)
-        h = self._eng().decode_row(ids[0, 0], self._seq)
+        """One decode step at the current position (reference model.py:221-233);
+        ``row`` is [1, 1, 33] or [1, 33]."""
+        rows = self._rows(row.view(1, -1, row.shape[-1]) if row.dim() == 2 else row, self._seq)
+        if rows.shape[0] != 1:
+            raise ValueError(f"step takes one row, got {rows.shape[0]}")
+        h = self._eng().decode_row(rows[0], self._seq)
         self._seq += 1
         return HiddenState(h.view(1, 1, self.hidden_size))
 
     # ---------------------------------------------------------------- heads
-    def _as_vec(self, h) -> torch.Tensor:
-        if isinstance(h, HiddenState):
-            h = h.last_hidden
-        if h.dim() == 3:
-            if h.shape[0] != 1:
-                raise ValueError("batch must be 1")
-            return h[0]
-        if h.dim() == 2 and h.shape[0] == 1:
-            return h
-        if h.dim() == 1:
-            return h.view(1, -1)
-        raise ValueError(f"unsupported hidden shape {tuple(h.shape)}")
+    def _head_input(self, h) -> tuple[torch.Tensor, bool]:
+        """Hidden states as rows [R, H], and whether they denote one position
+        (the result then drops its row dimension).  Accepted: [1, L, H],
+        [1, H] and [H] (reference model.py:240-295)."""
+        t = h.last_hidden if isinstance(h, HiddenState) else h
+        if t.dim() == 3 and t.shape[0] != 1:
+            raise ValueError("batch must be 1")
+        if t.dim() == 2 and t.shape[0] != 1 or t.dim() not in (1, 2, 3):
+            raise ValueError(f"unsupported hidden shape {tuple(t.shape)}")
+        rows = t.reshape(-1, t.shape[-1])
+        return rows.contiguous(), rows.shape[0] == 1
 
-    def _head(self, h, W: torch.Tensor, pad: bool = False) -> torch.Tensor:
+    def _apply_head(self, h, weight: torch.Tensor, pad: bool) -> tuple[torch.Tensor, bool]:
         from . import kernels
-        x = self._as_vec(h).contiguous()
-        rows = x.shape[0]
-        out = torch.empty(rows, W.shape[0], dtype=self.dtype, device=self.device)
-        for r0 in range(0, rows, 4):
-            r1 = min(rows, r0 + 4)
-            kernels.bf16_linear(x[r0:r1], W, out[r0:r1], pad_period=AUDIO_VOCAB if pad else 0,
+        x, single = self._head_input(h)
+        out = torch.empty(x.shape[0], weight.shape[0], dtype=self.dtype, device=self.device)
+        for r in range(0, x.shape[0], 4):   # the head GEMV serves up to 4 rows per launch
+            kernels.bf16_linear(x[r:r + 4], weight, out[r:r + 4], pad_period=AUDIO_VOCAB if pad else 0,
                                 pad_col=AUDIO_PAD_CODE)
-        return out
+        return out, single
 
     def text_logits(self, h) -> torch.Tensor:
-        """Full text head (model.py:240-253)."""
-        out = self._head(h, self.head_text)
-        return out[0] if out.shape[0] == 1 else out
+        """Full text head (reference model.py:240-253)."""
+        out, single = self._apply_head(h, self.head_text, pad=False)
+        return out[0] if single else out
 
     def text_logits_2way(self, h) -> torch.Tensor:
-        """The two audio-phase text logits (model.py:255-268)."""
-        out = self._head(h, self.head_2way)
-        return out[0] if out.shape[0] == 1 else out
+        """The two audio-phase text logits, GEN slot then DELAY slot (reference model.py:255-268)."""
+        out, single = self._apply_head(h, self.head_2way, pad=False)
+        return out[0] if single else out
 
     def audio_logits(self, h) -> torch.Tensor:
-        """32 audio heads, column 1024 = -inf (model.py:270-295)."""
-        out = self._head(h, self.head_audio.view(N_VQ * AUDIO_VOCAB, self.hidden_size), pad=True)
+        """32 audio heads with column 1024 at -inf (reference model.py:270-295)."""
+        out, single = self._apply_head(h, self.head_audio.view(N_VQ * AUDIO_VOCAB, self.hidden_size), pad=True)
         out = out.view(-1, N_VQ, AUDIO_VOCAB)
-        return out[0] if out.shape[0] == 1 else out
+        return out[0] if single else out

@@ -21,6 +21,25 @@ from .model import (AUDIO_DELAY_SLOT_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_PA
 
 _offsets = itertools.count(1)
 
+# Candidates one sampling CTA ranks after the top-k (kSampleMaxCand in
+# csrc/sampling.cu): a top-k of at most this many over any row, or a row of
+# at most this many columns with no top-k.
+SAMPLE_MAX_CANDIDATES = 2048
+
+
+def check_top_k(top_k, cols: int, what: str) -> None:
+    """Reject, before any device work, a sampled decision the fused sampler
+    does not serve: no top-k (or one beyond SAMPLE_MAX_CANDIDATES) over a row
+    of more than SAMPLE_MAX_CANDIDATES columns, e.g. top-p alone over the
+    151,936-way text head (the reference then sorts the whole vocabulary,
+    sampling.py:101-113)."""
+    k = int(top_k or 0)
+    n = k if 0 < k < cols else cols
+    if n > SAMPLE_MAX_CANDIDATES:
+        raise NotImplementedError(
+            f"{what}: sampling over {n} candidates (top_k={top_k}, {cols} columns) is not supported; "
+            f"use a top_k of at most {SAMPLE_MAX_CANDIDATES} (the reference text default is 50) or greedy")
+
 
 def sample_token(logits: torch.Tensor, prev_tokens: torch.Tensor | None = None, repetition_penalty: float = 1.0,
                  top_p=None, top_k=None, do_sample=True, seed: int | None = None) -> torch.Tensor:
@@ -38,14 +57,20 @@ def sample_token(logits: torch.Tensor, prev_tokens: torch.Tensor | None = None, 
     if not do_sample:
         kernels.argmax_rows(x, out)
         return out.view(logits.shape[:-1])
+    check_top_k(top_k, V, "sample_token")
     seen = None
     if prev_tokens is not None and repetition_penalty != 1.0:
+        # the union of the history's ids as a bit set, built on the device
+        # (ids outside [0, V) land in a spare slot that is dropped)
         words = (V + 31) // 32
-        bits = torch.zeros(words * 32, dtype=torch.bool)
-        ids = torch.unique(prev_tokens.reshape(-1).cpu())
-        bits[ids[(ids >= 0) & (ids < V)]] = True
-        w = (bits.view(words, 32).to(torch.int64) << torch.arange(32)).sum(1)
-        seen = w.to(torch.int64).to(torch.int32).view(1, words).to(x.device)
+        ids = prev_tokens.reshape(-1).to(device=x.device, dtype=torch.long)
+        ids = torch.where((ids >= 0) & (ids < V), ids, torch.full_like(ids, words * 32))
+        bits = torch.zeros(words * 32 + 1, dtype=torch.bool, device=x.device)
+        bits.index_fill_(0, ids, True)
+        shifts = torch.arange(32, device=x.device, dtype=torch.int64)
+        w = (bits[:words * 32].view(words, 32).to(torch.int64) << shifts).sum(1)
+        w = torch.where(w >= 1 << 31, w - (1 << 32), w)   # two's-complement int32 words
+        seen = w.to(torch.int32).view(1, words)
     kernels.sample_rows(x, list(range(R)), temperature=1.0, top_k=top_k or 0,
                         top_p=1.0 if top_p is None else float(top_p), penalty=repetition_penalty,
                         seen_bits=seen, seen_set=[0] * R, excluded=(),

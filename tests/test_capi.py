@@ -101,3 +101,16 @@ def test_plan_rejects_tile_counts_past_32_bit_owner_math():
     from moss_tts_lite_b200 import _lib
     with pytest.raises(_lib.MtlError):
         _lib.w4_plan(1, 16384 * 128, 64 * 8192, 32, 0)
+
+
+def test_sampling_limits_rejected_up_front():
+    """A sampled decision the fused sampler does not serve is refused before
+    any device work: top-p alone (or a top-k beyond 2048) over the text head."""
+    from moss_tts_lite_b200.sampling import SAMPLE_MAX_CANDIDATES, check_top_k
+    check_top_k(50, 151936, "text")                 # the reference text default
+    check_top_k(SAMPLE_MAX_CANDIDATES, 151936, "text")
+    check_top_k(None, 1025, "audio")                # no top-k over an audio row
+    check_top_k(0, 2, "two-way")
+    for k in (None, 0, -1, SAMPLE_MAX_CANDIDATES + 1, 151936):
+        with pytest.raises(NotImplementedError, match="not supported"):
+            check_top_k(k, 151936, "text")
