@@ -28,7 +28,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -37,7 +36,7 @@ sys.path.insert(0, ROOT)
 
 CFG = dict(hidden=4096, n_layers=36, n_heads=32, n_kv=8, head_dim=128, inter=12288, vocab=151936,
            group_size=128, prompt_len=128, std=0.02, seed=0)
-METRIC = "W4 decode steps/s at batch 1 (CUDA graph)"
+METRIC = "W4 decode steps/s at batch 1 (CUDA graph); int4 GEMV HBM GB/s vs B200 peak"
 MAX_SEQ = 8192
 
 
@@ -60,54 +59,67 @@ def _ncu_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled every 10 ms by a
+    host thread through NVML while the timed region runs (reads only; no
+    setting of the GPU is touched).  Falls back to `nvidia-smi -lms 200`
+    when NVML is unavailable."""
+
+    PERIOD_S = 0.01
+    # NVML clocks-event reason bits (nvml.h: nvmlClocksEventReason*)
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap"}
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
-        self.path = f"/tmp/mtl_clocks_{os.getpid()}.csv"
+        self.samples = []
+        self.max_mhz = None
+        self.err = None
+        self._stop = None
+        self._thread = None
+
+    def _run(self):
+        import pynvml
+        h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        while not self._stop.is_set():
+            try:
+                sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                rs = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+                self.samples.append((sm, rs))
+            except Exception as e:  # noqa: BLE001
+                self.err = str(e)
+            self._stop.wait(self.PERIOD_S)
 
     def __enter__(self):
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        import threading
         try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=self.f, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            idx = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+            # NVML counts all GPUs; map the visible ordinal when it is numeric
+            if idx and idx[0].strip().isdigit() and self.index < len(idx):
+                self.index = int(idx[self.index])
+        except Exception as e:  # noqa: BLE001
+            self.err = f"nvml unavailable: {e}"
+            return self
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
-            self.f.close()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
 
     def summary(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        rows = []
-        try:
-            for line in open(self.path):
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
-        except Exception:
-            pass
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [self.err or "no samples"],
+                    "samples": 0}
+        reasons = sorted({name for _, rs in self.samples for bit, name in self.REASONS.items() if rs & bit})
+        return {"sm_mhz": statistics.median(v for v, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples), "period_ms": self.PERIOD_S * 1e3,
+                "source": "nvml"}
 
 
 # ------------------------------------------------------------------ model
@@ -247,16 +259,20 @@ def time_w4_gemvs(fast, reps: int = 5):
 
 
 def time_e2e(fast, prompt, steps: int, warmup: int):
-    """generate_fast (public API, greedy) wall-clock steps/s over steps warmup..warmup+steps."""
+    """generate_fast (public API, greedy) wall-clock steps/s over steps
+    warmup..warmup+steps, and the phase mix of those steps (audio-phase steps
+    run the 2-way head, text-phase steps the 1.245 GB text head)."""
     from moss_tts_lite_b200.fast import generate_fast
     st = {}
     res = generate_fast(fast, {"input_ids": prompt}, max_new_tokens=warmup + steps + 1, greedy=True,
                         watchdog=False, stats=st)
     wall = st.get("step_wall_s", [])
     n = min(len(wall) - 1, warmup + steps)
+    phases = st.get("audio_phase", [])[warmup:n]
+    mix = {"audio_phase_steps": int(sum(phases)), "text_phase_steps": int(len(phases) - sum(phases))}
     if n <= warmup:
-        return None, res.n_steps, st.get("relaunches")
-    return (n - warmup) / (wall[n] - wall[warmup]), res.n_steps, st.get("relaunches")
+        return None, res.n_steps, st.get("relaunches"), mix
+    return (n - warmup) / (wall[n] - wall[warmup]), res.n_steps, st.get("relaunches"), mix
 
 
 def time_cfg3(fast, prompt_len: int = 4096, steps: int = 1024, seed: int = 3):
@@ -272,10 +288,6 @@ def time_cfg3(fast, prompt_len: int = 4096, steps: int = 1024, seed: int = 3):
     ids[0, :, 0] = torch.randint(0, 151643, (prompt_len,), generator=g)
     ids[0, :, 1:] = torch.randint(0, 1024, (prompt_len, N_VQ), generator=g)
     ids[0, -1, 0] = AUDIO_START_TOKEN_ID
-    # one untimed prefill of the same length first: the first call in a
-    # process also loads and selects the library GEMM / attention kernels
-    fast.prefill(ids.to(fast.m.device))
-    torch.cuda.synchronize()
     st = {}
     t0 = time.perf_counter()
     res = generate_fast(fast, {"input_ids": ids}, max_new_tokens=steps, seed=seed, audio_temperature=0.8,
@@ -290,7 +302,8 @@ def time_cfg3(fast, prompt_len: int = 4096, steps: int = 1024, seed: int = 3):
                         f"cache {prompt_len + 1}..{prompt_len + n}",
             "e2e_steps_per_s": e2e, "device_ms_per_step_median": (statistics.median(dev) if dev else None),
             "audio_phase_frac": (sum(phase) / len(phase) if phase else None), "steps": res.n_steps,
-            "prefill_s": (st.get("prefill_ms") or 0.0) / 1e3, "prefill_note": "after one untimed prefill call",
+            "prefill_s": (st.get("prefill_ms") or 0.0) / 1e3,
+            "prefill_note": "first prefill call at this prompt length (no warm-up call)",
             "wall_s": t1 - t0,
             # audio-phase step bytes: weights + heads (3,883,599,872 B) + 147,456 B of K/V per cached position
             "roofline_ms_per_step_at_mean_cache": (3883599872 + 147456 * (prompt_len + n / 2)) / (_peaks()[0] * 1e6)}
@@ -331,7 +344,7 @@ def time_cfg4(fast, streams: int = 16, prompt_len: int = 256, steps: int = 2048,
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / n
-    out = {"workload": f"cfg4: {streams} streams x {prompt_len}-row prompts (chunked W4 prefill per stream), "
+    out = {"workload": f"cfg4: {streams} streams x {prompt_len}-row prompts (prefill per stream), "
                        f"{steps} batched greedy audio-phase steps, one graph per step",
            "streams": streams, "steps": steps, "device_ms_per_step": ms, "steps_per_s": 1e3 / ms,
            "frames_per_s": streams * 1e3 / ms, "prefill_s": prefill_s,
@@ -341,80 +354,361 @@ def time_cfg4(fast, streams: int = 16, prompt_len: int = 256, steps: int = 2048,
     return out
 
 
-class CpuStep:
-    """The numpy oracle decode step on the host cores, bounded sample: 2 of
-    the 36 layers at the cfg2 shapes (fp32 BLAS on precomputed effective
-    weights, KV length 129) plus embedding and audio-phase heads; one
-    sample() times them once and scales the layers to the full model."""
+def _host_threads() -> int:
+    """Host cores this process may use (affinity), whatever OMP_NUM_THREADS
+    torchrun set: the CPU baselines use all of them."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:  # noqa: BLE001
+        return os.cpu_count() or 1
 
-    NL = 2
 
-    def __init__(self):
+def _ref_package():
+    """The unmodified reference package (a copy under baseline/_ref), or None."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if os.path.isdir(ref_dir) and ref_dir not in sys.path:
+        sys.path.append(ref_dir)
+    try:
+        import moss_tts_lite.gptq  # noqa: F401
+        import moss_tts_lite.model  # noqa: F401
+        return sys.modules["moss_tts_lite"]
+    except Exception:  # noqa: BLE001
+        return None
+
+
+class CpuRefStep:
+    """The reference's own eager decoder on the host cores: moss_tts_lite.
+    model.MossTTSModel (device='cpu', bf16) at the configuration-2 shapes, all
+    36 layers, one audio-phase decode step = step(row) + text_logits_2way +
+    audio_logits, starting at cache length 129.  bf16 random weights stand in
+    for the dequantised effective weights (the reference's CPU W4 path runs
+    them as bf16 F.linear); four distinct layer weight sets (1.5 GB) are
+    cycled over the 36 layers to bound host memory, so every layer still
+    streams its 386 MB of weights from DRAM (the set exceeds any LLC).  The
+    K/V cache rows 0..127 are random (their values do not change the work)."""
+
+    DISTINCT = 4
+
+    def __init__(self, threads: int, steps: int):
+        import torch
+        ref = _ref_package()
+        if ref is None:
+            raise RuntimeError("reference package not importable")
+        torch.set_num_threads(threads)
+        self.cores = torch.get_num_threads()
+        c = CFG
+        H, D = c["hidden"], c["head_dim"]
+        g = torch.Generator().manual_seed(1)
+
+        def r(*shape):
+            return (torch.randn(*shape, generator=g) * c["std"]).to(torch.bfloat16)
+        ones = lambda n: torch.ones(n, dtype=torch.bfloat16)  # noqa: E731
+        sets = []
+        for _ in range(self.DISTINCT):
+            sets.append({"self_attn.q_proj.weight": r(c["n_heads"] * D, H), "self_attn.k_proj.weight": r(c["n_kv"] * D, H),
+                         "self_attn.v_proj.weight": r(c["n_kv"] * D, H), "self_attn.o_proj.weight": r(H, c["n_heads"] * D),
+                         "mlp.gate_proj.weight": r(c["inter"], H), "mlp.up_proj.weight": r(c["inter"], H),
+                         "mlp.down_proj.weight": r(H, c["inter"])})
+        w = {"language_model.embed_tokens.weight": r(c["vocab"], H), "language_model.norm.weight": ones(H)}
+        for li in range(c["n_layers"]):
+            p = f"language_model.layers.{li}"
+            for k, t in sets[li % self.DISTINCT].items():
+                w[f"{p}.{k}"] = t
+            for k, n in (("input_layernorm", H), ("post_attention_layernorm", H), ("self_attn.q_norm", D),
+                         ("self_attn.k_norm", D)):
+                w[f"{p}.{k}.weight"] = ones(n)
+        for i in range(32):
+            w[f"emb_ext.{i}.weight"] = r(1025, H)
+            w[f"lm_heads.{i + 1}.weight"] = r(1025, H)
+        w["lm_heads.0.weight"] = r(c["vocab"], H)
+        L = c["prompt_len"]
+        self.m = ref.model.MossTTSModel(w, device="cpu", dtype=torch.bfloat16, max_seq_len=L + steps + 8)
+        del w
+        self.m.k_cache[:, :, :L].copy_(torch.randn(self.m.k_cache[:, :, :L].shape, generator=g))
+        self.m.v_cache[:, :, :L].copy_(torch.randn(self.m.v_cache[:, :, :L].shape, generator=g))
+        self.m._seq = L
+        self.row = torch.cat([torch.tensor([ref.model.AUDIO_GEN_SLOT_TOKEN_ID]),
+                              torch.randint(0, 1024, (32,), generator=g)]).view(1, 1, 33)
+        self.kind = "reference"
+        self.sample_desc = (f"reference moss_tts_lite.model.MossTTSModel on the host cores (torch CPU, bf16, "
+                            f"{self.cores} threads): one audio-phase decode step = step(row) + text_logits_2way + "
+                            f"audio_logits over all {c['n_layers']} layers at cache length {L + 1}+ "
+                            f"({self.DISTINCT} distinct layer weight sets cycled over the layers)")
+
+    def sample(self) -> float:
+        import torch
+        with torch.inference_mode():
+            t0 = time.perf_counter()
+            h = self.m.step(self.row)
+            self.m.text_logits_2way(h)
+            self.m.audio_logits(h)
+            return time.perf_counter() - t0
+
+
+class CpuOracleStep:
+    """Fallback when the reference package is absent: the numpy oracle (the
+    CPU restatement of the reference decoder) over all 36 layers at the
+    configuration-2 shapes (fp32 BLAS on effective weights; four distinct
+    layer weight sets cycled over the layers), embedding and audio-phase
+    heads, cache length 129."""
+
+    DISTINCT = 4
+
+    def __init__(self, threads: int, steps: int):
         import numpy as np
         from oracle import step as ost
         from oracle.bf16 import f32_to_bf16
+        try:
+            from threadpoolctl import threadpool_limits
+            self._limits = threadpool_limits(threads)
+        except Exception:  # noqa: BLE001
+            self._limits = None
+        self.cores = threads
         c = CFG
         H, D = c["hidden"], c["head_dim"]
         rng = np.random.default_rng(1)
 
         def r(*shape):
             return f32_to_bf16((rng.standard_normal(shape, dtype=np.float32) * np.float32(c["std"])))
-
+        one = lambda n: f32_to_bf16(np.ones(n, np.float32))  # noqa: E731
         w = {"language_model.embed_tokens.weight": np.zeros((c["vocab"], H), np.uint16),
-             "language_model.norm.weight": f32_to_bf16(np.ones(H, np.float32))}
-        for li in range(self.NL):
+             "language_model.norm.weight": one(H)}
+        for li in range(self.DISTINCT):
             p = f"language_model.layers.{li}"
-            w[f"{p}.input_layernorm.weight"] = f32_to_bf16(np.ones(H, np.float32))
-            w[f"{p}.post_attention_layernorm.weight"] = f32_to_bf16(np.ones(H, np.float32))
+            w[f"{p}.input_layernorm.weight"] = one(H)
+            w[f"{p}.post_attention_layernorm.weight"] = one(H)
             w[f"{p}.self_attn.q_proj.weight"] = r(c["n_heads"] * D, H)
             w[f"{p}.self_attn.k_proj.weight"] = r(c["n_kv"] * D, H)
             w[f"{p}.self_attn.v_proj.weight"] = r(c["n_kv"] * D, H)
             w[f"{p}.self_attn.o_proj.weight"] = r(H, c["n_heads"] * D)
-            w[f"{p}.self_attn.q_norm.weight"] = f32_to_bf16(np.ones(D, np.float32))
-            w[f"{p}.self_attn.k_norm.weight"] = f32_to_bf16(np.ones(D, np.float32))
+            w[f"{p}.self_attn.q_norm.weight"] = one(D)
+            w[f"{p}.self_attn.k_norm.weight"] = one(D)
             w[f"{p}.mlp.gate_proj.weight"] = r(c["inter"], H)
             w[f"{p}.mlp.up_proj.weight"] = r(c["inter"], H)
             w[f"{p}.mlp.down_proj.weight"] = r(H, c["inter"])
         for i in range(32):
             w[f"emb_ext.{i}.weight"] = r(1025, H)
-        w["lm_heads.0.weight"] = np.zeros((c["vocab"], H), np.uint16)
-        for i in range(32):
             w[f"lm_heads.{i + 1}.weight"] = r(1025, H)
+        w["lm_heads.0.weight"] = np.zeros((c["vocab"], H), np.uint16)
         self.ost = ost
-        self.om = ost.OracleModel(w, max_seq_len=c["prompt_len"] + 8, fp32_linears=True)
+        self.om = ost.OracleModel(w, max_seq_len=c["prompt_len"] + steps + 8, fp32_linears=True)
         self.om.seq = c["prompt_len"]
         self.row = np.concatenate([[ost.AUDIO_GEN_SLOT_TOKEN_ID], rng.integers(0, 1024, 32)]).astype(np.int64)
-        try:
-            from threadpoolctl import threadpool_info
-            self.cores = max(int(i.get("num_threads", 1)) for i in threadpool_info()) or (os.cpu_count() or 1)
-        except Exception:
-            self.cores = os.cpu_count() or 1
-        self.sample_desc = (f"numpy oracle step at cfg2 shapes: {self.NL} of {CFG['n_layers']} layers timed (fp32 "
-                            f"BLAS, effective weights precomputed, KV length {CFG['prompt_len'] + 1}) + embedding + "
-                            f"audio-phase heads per sample, layers scaled to {CFG['n_layers']}")
+        self.kind = "port"
+        self.sample_desc = (f"numpy oracle decode step at the configuration-2 shapes on {threads} BLAS threads: all "
+                            f"{c['n_layers']} layers ({self.DISTINCT} distinct weight sets cycled), fp32 products "
+                            f"on effective weights, embedding + audio-phase heads, cache length {c['prompt_len'] + 1}")
 
     def sample(self) -> float:
-        """Seconds of one full decode step (estimated from this sample)."""
         om, ost = self.om, self.ost
         t0 = time.perf_counter()
         h = om.embed_rows(self.row.reshape(1, -1))
-        t1 = time.perf_counter()
-        for li in range(self.NL):
-            h = om.layer(li, h, om.seq)
-        t2 = time.perf_counter()
+        for li in range(CFG["n_layers"]):
+            h = om.layer(li % self.DISTINCT, h, om.seq)
         hf = ost.rms_norm(h, om.final_norm)
         om.text_logits_2way(hf)
         om.audio_logits(hf)
-        t3 = time.perf_counter()
-        return (t1 - t0) + (t3 - t2) + (t2 - t1) * CFG["n_layers"] / self.NL
+        return time.perf_counter() - t0
 
 
-def cpu_baseline(reps: int = 3):
-    """(steps/s, cores, sample description) of the CPU oracle step."""
-    cs = CpuStep()
-    cs.sample()  # warm
+def cpu_step_runner(steps: int):
+    """The reference's own decoder on CPU when its package is present, else
+    the oracle port; all host cores."""
+    threads = _host_threads()
+    try:
+        return CpuRefStep(threads, steps)
+    except Exception:  # noqa: BLE001
+        return CpuOracleStep(threads, steps)
+
+
+def cpu_baseline(reps: int = 8):
+    """(steps/s, cores, kind, sample description) of the CPU decode step:
+    median of `reps` timed steps after two warm-up steps."""
+    cs = cpu_step_runner(reps + 2)
+    cs.sample()
+    cs.sample()
     per_step = statistics.median(cs.sample() for _ in range(reps))
-    return 1.0 / per_step, cs.cores, cs.sample_desc + f", median of {reps} samples"
+    return 1.0 / per_step, cs.cores, cs.kind, cs.sample_desc + f", median of {reps} steps"
+
+
+def cpu_linears(shapes, reps: int = 5):
+    """CPU baseline of W4 linears as the reference computes them on the host:
+    moss_tts_lite.gptq.effective_weight (dequantise the codes and (scale,
+    zero) to fp32) followed by the matmul, per projection, all host cores;
+    median of `reps` runs of the whole list.  Returns (seconds, threads, kind)."""
+    import torch
+    threads = _host_threads()
+    torch.set_num_threads(threads)
+    ref = _ref_package()
+    g = torch.Generator().manual_seed(2)
+    cases = []
+    for K, N in shapes:
+        q = torch.randint(0, 16, (N, K), generator=g, dtype=torch.uint8)
+        s = torch.rand(N, K // 128, generator=g) * 0.01 + 1e-3
+        mn = -8 * s
+        qsz = torch.stack([s, mn + 8.0 * s], -1).bfloat16().transpose(0, 1).contiguous()
+        cases.append((q, qsz, torch.randn(1, K, generator=g)))
+    if ref is not None:
+        eff = ref.gptq.effective_weight
+        kind = "reference"
+    else:
+        from oracle.w4 import ref_effective_weight
+
+        def eff(q, qsz, g):
+            return torch.from_numpy(ref_effective_weight(q.numpy(), qsz.view(torch.int16).numpy().view("uint16"), g))
+        kind = "port"
+
+    def run():
+        t0 = time.perf_counter()
+        for q, qsz, x in cases:
+            x @ eff(q, qsz, 128).t()
+        return time.perf_counter() - t0
+    run()
+    return statistics.median(run() for _ in range(reps)), threads, kind
+
+
+# --------------------------------------------------- configurations 0 and 1
+CFG1_SHAPES = [("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 4096),
+               ("gate", 4096, 12288), ("up", 4096, 12288), ("down", 12288, 4096)]
+
+
+def _gptq_bytes(K: int, N: int, g: int = 128) -> int:
+    """Algorithmic bytes of one AutoGPTQ W4 linear at batch 1: qweight + qzeros +
+    scales + x + y."""
+    return K * N // 2 + (K // g) * N // 2 + (K // g) * N * 2 + 2 * K + 2 * N
+
+
+def _gptq_linear(dev, K: int, N: int, gen, g: int = 128):
+    """A QuantLinear with the benchmark's distributions (codes and zeros
+    uniform 0..15: random 32-bit words; scales |N(0,1)| * 0.01 + 1e-3 fp16),
+    generated on the device."""
+    import torch
+    from moss_tts_lite_b200.quant import QuantLinear
+    qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), generator=gen, device=dev, dtype=torch.int32)
+    qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // g, N // 8), generator=gen, device=dev, dtype=torch.int32)
+    sc = (torch.randn(K // g, N, generator=gen, device=dev).abs() * 0.01 + 1e-3).half()
+    return QuantLinear.from_tensors(qw, qz, sc, group_size=g)
+
+
+def _graph_time(body, reps: int = 5) -> float:
+    """Seconds per replay of a CUDA graph of `body` (warmed up; CUDA events)."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        body()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        body()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e-3 / reps
+
+
+def time_cfg0_cfg1(dev, cpu: bool):
+    """Configuration 0 (one AutoGPTQ W4 linear 4096 -> 12288 at batch 1) and
+    configuration 1 (one layer's seven W4 GPTQ projections) through
+    QuantLinear.  Device: launches chained in a CUDA graph over several weight
+    copies (inputs larger than L2), achieved = algorithmic bytes / time.
+    End to end: QuantLinear.forward on a pinned host activation, the output
+    copied back, synchronised per call.  CPU: the reference's
+    effective_weight + matmul on the host cores."""
+    import torch
+    peak, peak_kind = _peaks()
+    gen = torch.Generator(device=dev).manual_seed(0)
+    out = {}
+    # ---- configuration 0
+    K, N = 4096, 12288
+    lins = [_gptq_linear(dev, K, N, gen) for _ in range(8)]            # 209 MB > L2
+    x = torch.randn(1, K, generator=gen, device=dev).to(torch.bfloat16)
+    y = torch.empty(1, N, dtype=torch.bfloat16, device=dev)
+
+    def body0():
+        for i in range(64):
+            lins[i % 8].w.linear(x, out=y)
+    t0 = _graph_time(body0) / 64
+    b0 = _gptq_bytes(K, N)
+    xh = torch.randn(1, K).to(torch.bfloat16).pin_memory()
+    yh = torch.empty(1, N, dtype=torch.bfloat16).pin_memory()
+    for _ in range(5):
+        yh.copy_(lins[0](xh.to(dev, non_blocking=True)), non_blocking=True)
+    torch.cuda.synchronize()
+    reps = 200
+    ts = time.perf_counter()
+    for i in range(reps):
+        yh.copy_(lins[i % 8](xh.to(dev, non_blocking=True)), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e2e0 = (time.perf_counter() - ts) / reps
+    out["cfg0"] = {"workload": "cfg0: AutoGPTQ W4A16 linear 4096 -> 12288, g128, batch 1 (QuantLinear)",
+                   "us_per_launch": t0 * 1e6, "bytes_per_launch": b0, "achieved_gbs": b0 / t0 / 1e9,
+                   "frac": b0 / t0 / 1e9 / peak, "peak_gbs": peak, "peak_kind": peak_kind,
+                   "timing": "64 launches in one CUDA graph over 8 weight copies (209 MB > L2)",
+                   "e2e_us_per_call": e2e0 * 1e6,
+                   "e2e": "QuantLinear.forward: pinned host x -> device, linear, y -> pinned host, synchronised"}
+    del lins
+    # ---- configuration 1
+    layers = [[_gptq_linear(dev, k, n, gen) for _, k, n in CFG1_SHAPES] for _ in range(4)]   # 402 MB > L2
+    xs = {k: torch.randn(1, k, generator=gen, device=dev).to(torch.bfloat16) for k in (4096, 12288)}
+    ys = {n: torch.empty(1, n, dtype=torch.bfloat16, device=dev) for n in (1024, 4096, 12288)}
+
+    def body1():
+        for i in range(16):
+            for lin, (_, k, n) in zip(layers[i % 4], CFG1_SHAPES):
+                lin.w.linear(xs[k], out=ys[n])
+    t1 = _graph_time(body1) / 16
+    b1 = sum(_gptq_bytes(k, n) for _, k, n in CFG1_SHAPES)
+    out["cfg1"] = {"workload": "cfg1: one layer's seven AutoGPTQ W4A16 projections (q, k, v, o, gate, up, down), "
+                               "g128, batch 1, seven QuantLinear launches",
+                   "us_per_layer": t1 * 1e6, "bytes_per_layer": b1, "achieved_gbs": b1 / t1 / 1e9,
+                   "frac": b1 / t1 / 1e9 / peak, "peak_kind": peak_kind,
+                   "timing": "16 layers in one CUDA graph over 4 layer copies (402 MB > L2)"}
+    del layers
+    torch.cuda.empty_cache()
+    if cpu:
+        s0, th, kind = cpu_linears([(K, N)])
+        s1, _, _ = cpu_linears([(k, n) for _, k, n in CFG1_SHAPES])
+        out["cfg0"]["cpu_baseline"] = {"us_per_call": s0 * 1e6, "cores": th, "kind": kind,
+                                       "sample": "moss_tts_lite.gptq.effective_weight + matmul, median of 5"}
+        out["cfg1"]["cpu_baseline"] = {"us_per_layer": s1 * 1e6, "cores": th, "kind": kind,
+                                       "sample": "effective_weight + matmul per projection, median of 5"}
+    return out
+
+
+def reference_gpu_rate(dev, steps: int, warmup: int):
+    """The reference's own W4 fast path on this GPU (the 5x denominator):
+    moss_tts_lite.model.MossTTSModel + fast.FastMossTTS(quant='w4', g128,
+    tinygemm) + generate_fast(greedy) on the same synthetic model and prompt;
+    steps/s from generate_fast's own per-step CUDA-event stats after
+    `warmup` steps.  None when the reference package is absent."""
+    import torch
+    ref = _ref_package()
+    if ref is None:
+        return None
+    import moss_tts_lite.fast as rfast
+    w = synth_weights(dev, CFG["seed"])
+    model = ref.model.MossTTSModel(w, device=dev, dtype=torch.bfloat16, max_seq_len=MAX_SEQ)
+    del w
+    fast = rfast.FastMossTTS(model, quant="w4", w4_group_size=CFG["group_size"])
+    st = {}
+    res = rfast.generate_fast(fast, {"input_ids": make_prompt(CFG["seed"]).to(dev)},
+                              max_new_tokens=warmup + steps + 1, greedy=True, watchdog=False, stats=st)
+    ms = st["step_ms"][warmup:warmup + steps]
+    out = {"value": 1000.0 / (sum(ms) / len(ms)), "unit": "steps/s", "steps": len(ms), "warmup": warmup,
+           "steps_generated": res.n_steps,
+           "what": "reference moss_tts_lite FastMossTTS(quant='w4', g128, tinygemm) + generate_fast(greedy), "
+                   "same synthetic model and prompt, this GPU, its per-step CUDA-event stats"}
+    del fast, model
+    torch.cuda.empty_cache()
+    return out
 
 
 # ------------------------------------------------------------------- main
@@ -459,24 +753,26 @@ class _Dist:
 
 
 def run_reference_arm(args, ctx):
-    """--impl reference: the CPU restatement of the reference path (numpy
-    oracle) on the host cores; rank 0 only.  Each step is one bounded sample
-    of the decode step (CpuStep.sample), so K steps take K x ~0.5 s."""
+    """--impl reference: the reference's own decoder on the host cores (its
+    MossTTSModel on device='cpu' when the package is present under
+    baseline/_ref, else the numpy oracle port), all host threads whatever
+    OMP_NUM_THREADS says; rank 0 only (the other ranks return at once).
+    One step = one audio-phase decode step over all 36 layers."""
     if ctx.rank != 0:
         return
-    cs = CpuStep()
+    cs = cpu_step_runner(args.steps + max(1, args.warmup))
     for _ in range(max(1, args.warmup)):
         cs.sample()
-    vals = [1.0 / cs.sample() for _ in range(args.steps)]
-    cores, sample = cs.cores, cs.sample_desc
-    v = statistics.median(vals)
+    secs = [cs.sample() for _ in range(args.steps)]
+    v = len(secs) / sum(secs)
     line = {"metric": METRIC, "value": v, "unit": "steps/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "vs_baseline": None, "dtype": "bf16" if cs.kind == "reference" else "f32", "data": "synthetic",
             "config": {"workload": "cfg2: full synthetic MOSS-TTS-shaped W4 decode step, batch 1",
                        "model": "synthetic MOSS-TTS (36L, h4096, 32/8 heads, ffn 12288)"},
             "impl": "reference",
-            "cpu_baseline": {"value": v, "unit": "steps/s", "cores": cores, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": v, "unit": "steps/s", "cores": cs.cores, "kind": cs.kind,
+                             "sample": cs.sample_desc},
             "e2e": {"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -672,6 +968,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="mtl", choices=["mtl", "reference", "reference-gpu"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true", help="skip the in-process reference GPU arm")
+    ap.add_argument("--no-cfg01", action="store_true", help="skip the configuration-0/1 linear measurements")
     ap.add_argument("--no-cfg3", action="store_true", help="skip the long-context sampled configuration-3 run")
     ap.add_argument("--no-cfg4", action="store_true", help="skip the 16-stream batched configuration-4 run")
     ap.add_argument("--profile-gemv", action="store_true", help="small config-0 GEMV case for ncu")
@@ -707,55 +1005,73 @@ def main():
     torch.cuda.set_device(ctx.local)
     ctx.init()
     dev = torch.device("cuda", ctx.local)
+    steps, warmup = args.steps, max(3, args.warmup)
+    # the reference's own W4 fast path on this GPU first (rank 0), freed before ours is built
+    ref_gpu = None
+    if ctx.rank == 0 and not args.no_reference_gpu:
+        ref_gpu = reference_gpu_rate(dev, steps=min(steps, 40), warmup=5)
+    ctx.barrier()
     t_build = time.time()
     fast = build_fast(dev, seed=CFG["seed"] + ctx.rank)
     prompt = make_prompt(CFG["seed"] + ctx.rank)
     fast.prefill(prompt.to(dev))
     fast.capture()
     build_s = time.time() - t_build
-    steps, warmup = args.steps, max(3, args.warmup)
     ms, clocks = time_decode_loop(fast, steps, warmup, ctx)
     ms = ctx.max(ms)
     ms_per_step = ms / steps
     value = ctx.world * steps / (ms * 1e-3)
     bytes_per_launch, s_per_launch, launches = time_w4_gemvs(fast)
-    e2e, e2e_steps, e2e_relaunches = time_e2e(fast, prompt.to("cpu"), steps, warmup)
+    e2e, e2e_steps, e2e_relaunches, e2e_mix = time_e2e(fast, prompt.to("cpu"), steps, warmup)
     e2e_all = ctx.max(-(e2e or 0.0))  # slowest rank
     e2e_val = ctx.world * (-e2e_all) if e2e else None
     peak, peak_kind = _peaks()
     achieved = bytes_per_launch / s_per_launch / 1e9
     traffic = _ncu_traffic()
+    single = ctx.world == 1
+    cfg01 = None
+    if ctx.rank == 0 and not args.no_cfg01:
+        cfg01 = time_cfg0_cfg1(dev, cpu=single and not args.no_cpu_baseline)
     cfg3 = None
-    if ctx.rank == 0 and args.gpus == 1 and not args.no_cfg3:
+    if not args.no_cfg3:
         cfg3 = time_cfg3(fast)
+        cfg3_e2e = ctx.max(-(cfg3["e2e_steps_per_s"] or 0.0))
+        cfg3["e2e_steps_per_s_all_gpus"] = ctx.world * (-cfg3_e2e)
     cfg4 = None
-    if ctx.rank == 0 and args.gpus == 1 and not args.no_cfg4:
+    if not args.no_cfg4:
         cfg4 = time_cfg4(fast)
+        cfg4_ms = ctx.max(cfg4["device_ms_per_step"])
+        cfg4["frames_per_s_all_gpus"] = ctx.world * cfg4["streams"] * 1e3 / cfg4_ms
+        cfg4["n_gpus"] = ctx.world
     cpu = None
-    if ctx.rank == 0 and args.gpus == 1 and not args.no_cpu_baseline:
-        v, cores, sample = cpu_baseline()
-        cpu = {"value": v, "unit": "steps/s", "cores": cores, "kind": "port", "sample": sample}
+    if ctx.rank == 0 and single and not args.no_cpu_baseline:
+        v, cores, kind, sample = cpu_baseline()
+        cpu = {"value": v, "unit": "steps/s", "cores": cores, "kind": kind, "sample": sample}
     if ctx.rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": args.gpus, "steps": steps,
+            "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": ctx.world, "steps": steps,
             "warmup": warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "cfg2: full synthetic MOSS-TTS-shaped W4 decode step, batch 1",
                        "model": "synthetic MOSS-TTS (36L, h4096, 32/8 heads x128, ffn 12288, vocab 151936 + "
                                 "32x1025 codebooks, RTN W4 g128, random-init seed 0)",
-                       "global_batch": args.gpus, "seq_len": CFG["prompt_len"], "parallelism": f"replicas{args.gpus}",
+                       "global_batch": ctx.world, "seq_len": CFG["prompt_len"],
+                       "parallelism": f"replicas{ctx.world}",
                        "phase": "audio (2-way text head + 32 audio heads), greedy tokens fed back on device",
                        "l2": "inputs larger than L2 (~3.9 GB of weights per step)",
-                       "weights": "int4 codes + bf16 (scale, zero) per 128-group; activations bf16, fp32 accumulate",
+                       "weights": "int4 codes + bf16 (scale, zero) per 128-group; operand bf16((q-8)*scale+zero) "
+                                  "as the reference's int4 GEMM; activations bf16, fp32 accumulate",
                        "build_s": round(build_s, 1)},
             # per step: the 33 decisions come back to the host (pinned, 264 B);
             # the next input row is built on the device from them (as the
-            # reference builds current_input_ids), so no per-step h2d copy;
-            # the prompt crosses once per call
+            # reference builds current_input_ids on the device), so no
+            # per-step h2d copy; the prompt crosses once per call
             "e2e": {"value": e2e_val, "unit": "steps/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 33 * 8, "h2d_prompt_bytes": int(prompt.numel()) * 8,
                     "api": "moss_tts_lite_b200.fast.generate_fast(greedy=True)",
-                    "steps_generated": e2e_steps, "speculation_relaunches": e2e_relaunches},
+                    "steps_generated": e2e_steps, "speculation_relaunches": e2e_relaunches,
+                    "phase_mix": e2e_mix,
+                    "note": "next input row built on the device from the read-back decisions (no per-step h2d)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          # ncu DRAM bytes of the config-0 capture, scaled by its
@@ -767,8 +1083,15 @@ def main():
             "gpu_launches": steps * (1 + 5 * CFG["n_layers"] + 2 + 1),
             "clocks": clocks,
         }
+        if ref_gpu is not None:
+            line["reference_gpu"] = ref_gpu
+            line["reference_gpu"]["ratio_device"] = (value / ctx.world) / ref_gpu["value"]
+            if e2e_val:
+                line["reference_gpu"]["ratio_e2e"] = (e2e_val / ctx.world) / ref_gpu["value"]
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if cfg01 is not None:
+            line.update(cfg01)
         if cfg3 is not None:
             line["cfg3"] = cfg3
         if cfg4 is not None:

@@ -120,7 +120,11 @@ int mtl_w4_unpack_codes(const void* tiles, int K, int N, int group_size, int par
  *            blocks (block b = gate[32b..32b+32) then up[32b..32b+32)) and
  *            writes N/2 outputs per row
  *   y        bf16 [M, ldy]
- *   scratch  device buffer of >= scratch_bytes from mtl_w4_plan, zeroed once
+ *   scratch  device buffer of >= scratch_bytes from mtl_w4_plan, zeroed once;
+ *            every completed launch leaves its split-K counters at zero
+ *            again.  A launch that gave up on a bounded wait (a nonzero
+ *            mtl_device_status) may leave counters set: zero the scratch
+ *            again before reusing it after such a status.
  *   zero_offset  MTL_FMT_GPTQ only: added to every stored zero (0 or 1). */
 int mtl_w4a16_linear(const uint16_t* x, int ldx, int M, int K, int N, int group_size, int param_fmt,
                      const void* tiles, int zero_offset, const int32_t* k_perm, const uint16_t* norm_w,
@@ -135,7 +139,9 @@ int mtl_w4a16_linear(const uint16_t* x, int ldx, int M, int K, int N, int group_
  * mtl_w4a16_linear minus the scratch buffer: the split-K scratch is a fixed
  * 1 MiB device array inside the library (held on every GPU that loads the
  * library until exit); shapes needing more (mtl_w4_plan) fail with
- * MTL_E_SCRATCH.  All calls share that array: calls that can overlap on the
+ * MTL_E_SCRATCH.  Every argument is checked before anything is enqueued;
+ * each call then clears the array's split-K counters on `stream` before its
+ * launch.  All calls share that array: calls that can overlap on the
  * GPU (unordered streams) race, calls ordered on one stream are fine.  The
  * first call on each device resolves the array's address (with that device
  * current); make it before any stream capture.  Allocates nothing. */
@@ -143,6 +149,21 @@ int mtl_w4a16_linear_noalloc(const uint16_t* x, int ldx, int M, int K, int N, in
                              const void* tiles, int zero_offset, const int32_t* k_perm, const uint16_t* norm_w,
                              float norm_eps, int epilogue, const uint16_t* residual, uint16_t* y, int ldy,
                              mtl_stream_t stream);
+
+/* y = epilogue(x . W^T) for a prompt of M rows on the 5th-generation tensor
+ * cores (tcgen05 GEMM, the prefill path).  Replaces
+ * torch._weight_int4pack_mm(x, packed, g, qsz) at M = prompt length as
+ * FastMossTTS._layer_q runs it (moss_tts_lite/fast.py:218-270).
+ *   tiles     reference-format tiles from mtl_w4_pack_ref (the same packed
+ *             weights the decode GEMV reads); W = bf16((q-8)*scale+zero)
+ *   x         bf16 [M, ldx], 16-byte aligned, ldx % 8 == 0
+ *   epilogue  MTL_EPI_STORE / _RESIDUAL (residual bf16 [M, ldr], may alias
+ *             y) / _SWIGLU (gate/up interleaved in 32-column blocks, N/2
+ *             outputs per row)
+ *   group_size 64/128/256, K % 64 == 0, N % 128 == 0 (else MTL_E_UNSUPPORTED).
+ * Needs no scratch. */
+int mtl_w4a16_gemm(const uint16_t* x, int ldx, int M, int K, int N, int group_size, const void* tiles, int epilogue,
+                   const uint16_t* residual, int ldr, uint16_t* y, int ldy, mtl_stream_t stream);
 
 /* ------------------------------------------------------ decoder step ops */
 

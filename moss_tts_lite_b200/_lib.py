@@ -53,6 +53,8 @@ SIGNATURES = {
     "mtl_w4a16_linear_noalloc": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p,
                                           _c_int, _c_void_p, _c_void_p, _c_float, _c_int, _c_void_p, _c_void_p,
                                           _c_int, _c_void_p]),
+    "mtl_w4a16_gemm": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_int, _c_void_p,
+                                _c_int, _c_void_p, _c_int, _c_void_p]),
     "mtl_embed_sum": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_void_p, _c_int, _c_void_p, _c_void_p]),
     "mtl_attn_scratch_bytes": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_size_p]),
     "mtl_attn_decode": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,

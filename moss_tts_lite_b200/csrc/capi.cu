@@ -42,6 +42,9 @@ int w4_tcb_plan(int K, int N, int g, int num_sms, TcPlan* out);
 cudaError_t w4_tcb_launch(const TcbArgs& a, cudaStream_t stream, int use_pdl);
 cudaError_t w4_tc_pack(const uint8_t* q, const uint16_t* qsz, int K, int N, int g, uint8_t* tiles, cudaStream_t s);
 cudaError_t w4_tc_unpack_codes(const uint8_t* tiles, int K, int N, int g, uint8_t* codes, cudaStream_t s);
+cudaError_t w4_gemm_launch(const uint16_t* x, int ldx, int L, int K, int N, int g, const uint8_t* tiles, int epi,
+                           const uint16_t* residual, int ldr, uint16_t* y, int ldy, int num_sms, cudaStream_t s,
+                           int use_pdl);
 }  // namespace mtl
 
 namespace {
@@ -250,12 +253,18 @@ int mtl_w4_dequant(const void* tiles, int K, int N, int group_size, int param_fm
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4_dequant");
 }
 
-int mtl_w4a16_linear(const uint16_t* x, int ldx, int M, int K, int N, int group_size, int param_fmt,
-                     const void* tiles, int zero_offset, const int32_t* k_perm, const uint16_t* norm_w,
-                     float norm_eps, int epilogue, const uint16_t* residual, uint16_t* y, int ldy, void* scratch,
-                     size_t scratch_bytes, mtl_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+// Every argument check of mtl_w4a16_linear except those on the scratch
+// buffer: no device work happens before these pass.  On success *need is
+// the scratch the call requires (mtl_w4_plan).
+int check_w4_linear_args(const uint16_t* x, int ldx, int M, int K, int N, int group_size, int param_fmt,
+                         const void* tiles, int zero_offset, const int32_t* k_perm, const uint16_t* norm_w,
+                         int epilogue, const uint16_t* residual, const uint16_t* y, int ldy, size_t* need) {
   if (int r = check_w4_shape(K, N, group_size, param_fmt)) return r;
-  if (!x || !tiles || !y || !scratch) return fail(MTL_E_INVALID, "mtl_w4a16_linear: NULL pointer");
+  if (!x || !tiles || !y) return fail(MTL_E_INVALID, "mtl_w4a16_linear: NULL pointer");
   if (M < 1) return fail(MTL_E_INVALID, "M=%d must be >= 1", M);
   if (ldx < K) return fail(MTL_E_INVALID, "ldx=%d < K=%d", ldx, K);
   if (epilogue != MTL_EPI_STORE && epilogue != MTL_EPI_RESIDUAL && epilogue != MTL_EPI_SWIGLU)
@@ -265,17 +274,33 @@ int mtl_w4a16_linear(const uint16_t* x, int ldx, int M, int K, int N, int group_
   if (epilogue == MTL_EPI_RESIDUAL && !residual) return fail(MTL_E_INVALID, "residual epilogue needs residual");
   if (zero_offset < 0 || zero_offset > 1) return fail(MTL_E_INVALID, "zero_offset must be 0 or 1");
   if (!aligned(tiles, 16)) return fail(MTL_E_ALIGN, "tiles must be 16-byte aligned");
-  if (!aligned(scratch, 256)) return fail(MTL_E_ALIGN, "scratch must be 256-byte aligned");
   if (!aligned(x, 2) || !aligned(y, 2)) return fail(MTL_E_ALIGN, "x/y must be 2-byte aligned");
+  if (param_fmt == MTL_FMT_TC) {
+    if (zero_offset != 0 || k_perm) return fail(MTL_E_UNSUPPORTED, "MTL_FMT_TC has no zero offset or k_perm");
+    if (!aligned(x, 16) || (ldx % 8) || (norm_w && !aligned(norm_w, 16)))
+      return fail(MTL_E_ALIGN, "MTL_FMT_TC needs 16-byte aligned x rows and norm_w");
+  }
+  return mtl_w4_plan(M, K, N, group_size, param_fmt, nullptr, need);
+}
+
+}  // namespace
+
+extern "C" {
+
+int mtl_w4a16_linear(const uint16_t* x, int ldx, int M, int K, int N, int group_size, int param_fmt,
+                     const void* tiles, int zero_offset, const int32_t* k_perm, const uint16_t* norm_w,
+                     float norm_eps, int epilogue, const uint16_t* residual, uint16_t* y, int ldy, void* scratch,
+                     size_t scratch_bytes, mtl_stream_t stream) {
   size_t need = 0;
-  if (int r = mtl_w4_plan(M, K, N, group_size, param_fmt, nullptr, &need)) return r;
+  if (int r = check_w4_linear_args(x, ldx, M, K, N, group_size, param_fmt, tiles, zero_offset, k_perm, norm_w,
+                                   epilogue, residual, y, ldy, &need))
+    return r;
+  if (!scratch) return fail(MTL_E_INVALID, "mtl_w4a16_linear: NULL pointer");
+  if (!aligned(scratch, 256)) return fail(MTL_E_ALIGN, "scratch must be 256-byte aligned");
   if (scratch_bytes < need) return fail(MTL_E_SCRATCH, "scratch %zu < required %zu bytes", scratch_bytes, need);
 
   if (param_fmt == MTL_FMT_TC) {
     // tensor-core kernel: one launch per activation row (batch-1 decode path)
-    if (zero_offset != 0 || k_perm) return fail(MTL_E_UNSUPPORTED, "MTL_FMT_TC has no zero offset or k_perm");
-    if (!aligned(x, 16) || (ldx % 8) || (norm_w && !aligned(norm_w, 16)))
-      return fail(MTL_E_ALIGN, "MTL_FMT_TC needs 16-byte aligned x rows and norm_w");
     mtl::TcArgs a{};
     if (get_tc_plan(K, N, group_size, &a.p)) return fail(MTL_E_UNSUPPORTED, "no tensor-core plan");
     a.K = K;
@@ -352,6 +377,27 @@ int mtl_w4a16_linear(const uint16_t* x, int ldx, int M, int K, int N, int group_
     if (e != cudaSuccess) return cuda_fail(e, "mtl_w4a16_linear launch");
   }
   return MTL_OK;
+}
+
+int mtl_w4a16_gemm(const uint16_t* x, int ldx, int M, int K, int N, int group_size, const void* tiles, int epilogue,
+                   const uint16_t* residual, int ldr, uint16_t* y, int ldy, mtl_stream_t stream) {
+  if (int r = check_w4_shape(K, N, group_size, MTL_FMT_REF)) return r;
+  if (!x || !tiles || !y) return fail(MTL_E_INVALID, "mtl_w4a16_gemm: NULL pointer");
+  if (M < 1) return fail(MTL_E_INVALID, "M=%d must be >= 1", M);
+  if (group_size < 64) return fail(MTL_E_UNSUPPORTED, "mtl_w4a16_gemm: group_size %d (64/128/256 served)", group_size);
+  if (K % 64 || N % 128) return fail(MTL_E_UNSUPPORTED, "mtl_w4a16_gemm: K=%d N=%d (K %% 64, N %% 128 must be 0)", K, N);
+  if (ldx < K || (ldx % 8)) return fail(MTL_E_INVALID, "ldx=%d (>= K, multiple of 8)", ldx);
+  if (epilogue != MTL_EPI_STORE && epilogue != MTL_EPI_RESIDUAL && epilogue != MTL_EPI_SWIGLU)
+    return fail(MTL_E_INVALID, "unknown epilogue %d", epilogue);
+  const int nout = epilogue == MTL_EPI_SWIGLU ? N / 2 : N;
+  if (ldy < nout) return fail(MTL_E_INVALID, "ldy=%d < %d outputs", ldy, nout);
+  if (epilogue == MTL_EPI_RESIDUAL && (!residual || ldr < N))
+    return fail(MTL_E_INVALID, "residual epilogue needs residual with ldr >= N");
+  if (!aligned(x, 16) || !aligned(tiles, 16)) return fail(MTL_E_ALIGN, "x and tiles must be 16-byte aligned");
+  if (!aligned(y, 2)) return fail(MTL_E_ALIGN, "y must be 2-byte aligned");
+  cudaError_t e = mtl::w4_gemm_launch(x, ldx, M, K, N, group_size, static_cast<const uint8_t*>(tiles), epilogue,
+                                      residual, ldr, y, ldy, num_sms(), stream, use_pdl() ? 1 : 0);
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4a16_gemm");
 }
 
 int mtl_embed_sum(const int64_t* ids, int M, const uint16_t* emb_text, int text_vocab, const uint16_t* emb_audio,

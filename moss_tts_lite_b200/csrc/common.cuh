@@ -119,6 +119,24 @@ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint3
   return d;
 }
 
+// bf16x2 fused multiply-add, one rounding per half (fma.rn.bf16x2).
+__device__ __forceinline__ uint32_t bf16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Reference-format dequantisation of two codes, as torch's int4 GEMM
+// (_weight_int4pack_mm, called at moss_tts_lite/fast.py:118) forms its
+// operand: w = bf16((q - 8) * scale + zero), one rounding.  `biased` is the
+// bf16 pair (128 + q_lo, 128 + q_hi) from lop3_and_or(..., 0x43004300);
+// 128 + q - 136 = q - 8 is exact in bf16, then one bf16 FMA with the
+// column's (scale, scale) and (zero, zero) pairs.
+__device__ __forceinline__ uint32_t w4_ref_pair(uint32_t biased, uint32_t scale2, uint32_t zero2) {
+  const uint32_t q8 = bf16x2_fma(biased, 0x3F803F80u, 0xC308C308u);  // * 1.0 + (-136)
+  return bf16x2_fma(q8, scale2, zero2);
+}
+
 // m16n8k16 fp16 MMA with fp32 accumulate (register-sourced operands).
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                               uint32_t b0, uint32_t b1) {

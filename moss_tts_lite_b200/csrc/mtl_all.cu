@@ -5,6 +5,7 @@
 #include "w4_tcb.cu"
 #include "step_kernels.cu"
 #include "attn_decode.cu"
+#include "w4_gemm.cu"
 #include "sampling.cu"
 #include "capi.cu"
 #include "noalloc.cu"

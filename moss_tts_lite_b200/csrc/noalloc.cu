@@ -12,8 +12,8 @@
 // Limits and sharing:
 //  * the array holds kNoAllocScratchBytes (1 MiB) on every GPU that loads
 //    the library, for as long as the library stays loaded;
-//  * shapes whose scratch (mtl_w4_plan) exceeds that are rejected with
-//    MTL_E_SCRATCH before any device work;
+//  * every argument is checked before any device work; shapes whose scratch
+//    (mtl_w4_plan) exceeds the array are rejected with MTL_E_SCRATCH;
 //  * every call shares the one array: calls that may run at the same time on
 //    the GPU (different streams without ordering) race and must not be used;
 //    calls ordered on one stream are fine;
@@ -69,8 +69,11 @@ extern "C" int mtl_w4a16_linear_noalloc(const uint16_t* x, int ldx, int M, int K
                                         int param_fmt, const void* tiles, int zero_offset, const int32_t* k_perm,
                                         const uint16_t* norm_w, float norm_eps, int epilogue,
                                         const uint16_t* residual, uint16_t* y, int ldy, mtl_stream_t stream) {
+  // every argument is checked before anything is put on the caller's stream
   size_t need = 0;
-  if (int r = mtl_w4_plan(M, K, N, group_size, param_fmt, nullptr, &need)) return r;
+  if (int r = check_w4_linear_args(x, ldx, M, K, N, group_size, param_fmt, tiles, zero_offset, k_perm, norm_w,
+                                   epilogue, residual, y, ldy, &need))
+    return r;
   if (need > mtl::kNoAllocScratchBytes)
     return fail(MTL_E_SCRATCH, "mtl_w4a16_linear_noalloc: shape needs %zu scratch bytes, the fixed device array holds %zu",
                 need, mtl::kNoAllocScratchBytes);
@@ -78,10 +81,13 @@ extern "C" int mtl_w4a16_linear_noalloc(const uint16_t* x, int ldx, int M, int K
   void* scratch = mtl::noalloc_scratch_ptr(&err);
   if (!scratch)
     return fail(MTL_E_CUDA, "mtl_w4a16_linear_noalloc: cannot resolve the device scratch array (error %d)", err);
-  // The split-K counters must start at zero.  A completed launch leaves them
-  // zero, but clear them anyway so an interrupted earlier call cannot leak
-  // into this one (a memset on the caller's stream allocates nothing).
-  cudaError_t e = cudaMemsetAsync(scratch, 0, counters_bytes(N), stream);
+  // The split-K counters at the head of the array must start at zero.  A
+  // completed launch leaves them zero, but clear them anyway so that an
+  // interrupted earlier call cannot leak into this one (a memset on the
+  // caller's stream allocates nothing).  The two tile formats keep one
+  // counter per 64- or 128-column block.
+  const size_t cbytes = param_fmt == MTL_FMT_TC ? tc_counters_bytes(N) : counters_bytes(N);
+  cudaError_t e = cudaMemsetAsync(scratch, 0, cbytes, stream);
   if (e != cudaSuccess) return cuda_fail(e, "mtl_w4a16_linear_noalloc: clear counters");
   return mtl_w4a16_linear(x, ldx, M, K, N, group_size, param_fmt, tiles, zero_offset, k_perm, norm_w, norm_eps,
                           epilogue, residual, y, ldy, scratch, mtl::kNoAllocScratchBytes, stream);

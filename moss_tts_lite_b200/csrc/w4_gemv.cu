@@ -2,10 +2,12 @@
 //
 // Replaces torch._weight_int4pack_mm as called by the reference at
 // moss_tts_lite/fast.py:118 (FastMossTTS._linear), gptq.py:582
-// (kernel_linear) and fast_native.py:169 (_lin_fused): y = x . W_eff^T with
-// W_eff = (q - 8) * scale + zero per group (gptq.py:87-97), fp32
-// accumulation, bf16 output.  The AutoGPTQ face computes
-// W_eff = (q - z) * s with the same kernel.
+// (kernel_linear) and fast_native.py:169 (_lin_fused): y = x . W^T, fp32
+// accumulation, bf16 output.  Reference format: W = bf16((q - 8) * scale +
+// zero) per group (gptq.py:87-97), rounded to bf16 once as torch's int4 GEMM
+// forms its operand, so the products are those of the reference's kernel and
+// only the fp32 summation order differs.  AutoGPTQ format: W = (q - z) * s,
+// exact (the group affine is applied in fp32).
 //
 // Design (HBM-bound at batch 1):
 //  * weights stream through a shared-memory ring filled by 1-D bulk copies
@@ -17,10 +19,12 @@
 //    CTA streams the same number of bytes whatever N and K are;
 //  * codes go register -> bf16 pairs (128 + q) with three shifts and four
 //    LOP3 per 8 codes and into m16n8k16 bf16 MMAs whose B operand is the
-//    bf16 activation itself (batch in the MMA N dimension).  The per-group
-//    affine is applied after the group's MMAs: y += A (D - 128 Sx) + B Sx,
-//    where A/B are the group's scale/offset and Sx the group's sum of
-//    activations.  Products of bf16 values are exact in fp32;
+//    bf16 activation itself (batch in the MMA N dimension).  Reference
+//    format: each pair becomes bf16((q - 8) s + z) by two bf16x2 FMAs
+//    (exact q - 8, then one rounding) and the MMAs accumulate a column
+//    block over all its groups.  AutoGPTQ format: the per-group affine is
+//    applied after the group's MMAs, y += s (D - (z + 128) Sx) with Sx the
+//    group's activation sum (products of bf16 values are exact in fp32);
 //  * split-K partials from different CTAs are combined by the last CTA to
 //    arrive at a column block, in fixed contributor order (deterministic),
 //    followed by the fused epilogue (store / residual add / SwiGLU).
@@ -297,37 +301,46 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
         u[q] = (__float_as_uint(v0) >> 16) | (__float_as_uint(v1) & 0xFFFF0000u);
       }
     }
-#pragma unroll
-    for (int q = 0; q < 8; ++q) bs += __uint_as_float(u[q] << 16) + __uint_as_float(u[q] & 0xFFFF0000u);
     uint16_t* dst = xs + ((size_t)slot * M + m) * g + b * 16;
     *reinterpret_cast<uint4*>(dst) = make_uint4(u[0], u[4], u[1], u[5]);
     *reinterpret_cast<uint4*>(dst + 8) = make_uint4(u[2], u[6], u[3], u[7]);
-    bsum[(slot * M + m) * nb16 + b] = bs;
+    if (FMT != kFmtRef) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) bs += __uint_as_float(u[q] << 16) + __uint_as_float(u[q] & 0xFFFF0000u);
+      bsum[(slot * M + m) * nb16 + b] = bs;
+    }
   };
   if (tid < njobs) stage_job(tid, a.xvec != 0, xc[0], nwc[0]);
   if (tid + kW4CThreads < njobs) stage_job(tid + kW4CThreads, a.xvec != 0, xc[1], nwc[1]);
   for (int job = tid + 2 * kW4CThreads; job < njobs; job += kW4CThreads) stage_job(job, false, xc[0], nwc[0]);
   for (int i = tid; i < p.nblk_max * kW4Warps * kNT * M; i += kW4CThreads) part[i] = 0.f;
   consumer_sync();
-  for (int job = tid; job < ng * M; job += kW4CThreads) {
-    // the 16-value block sums in order; all loads issued before the adds
-    float bv[16];
+  if (FMT != kFmtRef) {
+    // group sums of the activations for the GPTQ affine: the 16-value block
+    // sums in order, all loads issued before the adds
+    for (int job = tid; job < ng * M; job += kW4CThreads) {
+      float bv[16];
 #pragma unroll
-    for (int b = 0; b < 16; ++b) bv[b] = b < nb16 ? bsum[job * nb16 + b] : 0.f;
-    float s = 0.f;
+      for (int b = 0; b < 16; ++b) bv[b] = b < nb16 ? bsum[job * nb16 + b] : 0.f;
+      float s = 0.f;
 #pragma unroll
-    for (int b = 0; b < 16; ++b)
-      if (b < nb16) s += bv[b];
-    gsum[job] = s;
+      for (int b = 0; b < 16; ++b)
+        if (b < nb16) s += bv[b];
+      gsum[job] = s;
+    }
+    consumer_sync();
   }
-  consumer_sync();
 
   // ------------------------------------------------------------ main loop
   const int gr = lane >> 2, tq = lane & 3;
   const int mrow = min(gr, M - 1);
   const int KS = g >> 4;
   const int blk_first = t0 / KT;
-  float yacc[4][4];
+  // Column-block accumulators.  Reference format: the MMAs take the bf16
+  // effective weights themselves, so a block accumulates over all its groups
+  // in two chains (even / odd k16-steps).  GPTQ format: per-group MMA sums
+  // of (128 + q) x, folded into yacc by the group affine.
+  float yacc[4][4], yacc2[4][4];
   int cur = -1;
   bool bail = false;
 
@@ -339,7 +352,7 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
       for (int e = 0; e < 4; ++e) {
         const int col = 16 * j + gr + ((e & 2) ? 8 : 0);
         const int m = 2 * tq + (e & 1);
-        if (m < M) dst[col * M + m] = yacc[j][e];
+        if (m < M) dst[col * M + m] = (FMT == kFmtRef) ? yacc[j][e] + yacc2[j][e] : yacc[j][e];
       }
   };
 
@@ -358,7 +371,7 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
 #pragma unroll
       for (int j = 0; j < 4; ++j)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) yacc[j][e] = 0.f;
+        for (int e = 0; e < 4; ++e) yacc[j][e] = yacc2[j][e] = 0.f;
     }
     if (!mbar_wait(&full[s], q & 1)) {
       bail = true;
@@ -367,61 +380,90 @@ __global__ void __launch_bounds__((kW4Warps + 1) * 32, 2) w4_gemv_kernel(const W
     const uint8_t* tile = ring + (size_t)s * stage_bytes + (size_t)(i & (tps - 1)) * p.tile_bytes;
     const uint4* wt = reinterpret_cast<const uint4*>(tile);
     const uint16_t* xg = xs + ((size_t)slot * M + mrow) * g + 4 * tq;
-    // even and odd k16-steps accumulate separately: eight independent MMA
-    // chains per warp instead of four
-    float d[4][4], d2[4][4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) d[j][e] = d2[j][e] = 0.f;
-#pragma unroll 2
-    for (int ks = 0; ks < KS; ks += 2) {
-      const uint4 wv = wt[ks * 32 + lane];
-      const uint4 wv2 = wt[(ks + 1) * 32 + lane];
-      const uint2 bx = *reinterpret_cast<const uint2*>(xg + ks * 16);
-      const uint2 bx2 = *reinterpret_cast<const uint2*>(xg + (ks + 1) * 16);
-      const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
-      const uint32_t wr2[4] = {wv2.x, wv2.y, wv2.z, wv2.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t w = wr[j], v = wr2[j];
-        mma_bf16_16816(d[j], lop3_and_or(w, 0x000F000Fu, 0x43004300u), lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u),
-                       lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u), lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u),
-                       bx.x, bx.y);
-        mma_bf16_16816(d2[j], lop3_and_or(v, 0x000F000Fu, 0x43004300u), lop3_and_or(v >> 4, 0x000F000Fu, 0x43004300u),
-                       lop3_and_or(v >> 8, 0x000F000Fu, 0x43004300u), lop3_and_or(v >> 12, 0x000F000Fu, 0x43004300u),
-                       bx2.x, bx2.y);
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) d[j][e] += d2[j][e];
-    // group affine: D = sum x (128 + q)  =>  y += A (D - 128 Sx) + B Sx = A D + C Sx
-    const float sx0 = gsum[slot * M + min(2 * tq, M - 1)];
-    const float sx1 = gsum[slot * M + min(2 * tq + 1, M - 1)];
     const uint8_t* prm = tile + kNT * g / 2;
+    if (FMT == kFmtRef) {
+      // (scale, scale) and (zero, zero) bf16 pairs of this lane's 8 columns
+      // 16 j + gr (+ 8): rows r0 / r1 of the A fragments
+      uint32_t sc2[4][2], zr2[4][2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        const int col = 16 * j + gr + 8 * hr;
-        float A, C;
-        if (FMT == kFmtRef) {
-          // gptq.py:87-97: w = (q - 8) scale + zero, so C = B - 128 A = zero - 136 scale
-          const uint32_t pw = reinterpret_cast<const uint32_t*>(prm)[col];
-          A = __uint_as_float(pw * 65536u);
-          C = fmaf(-136.f, A, __uint_as_float(pw & 0xFFFF0000u));
-        } else {
-          // w = (q - (z + zero_offset)) s, so C = -(z + zero_offset + 128) s
-          A = __half2float(reinterpret_cast<const __half*>(prm)[col]);
+        for (int hr = 0; hr < 2; ++hr) {
+          const uint32_t pw = reinterpret_cast<const uint32_t*>(prm)[16 * j + gr + 8 * hr];
+          sc2[j][hr] = __byte_perm(pw, 0u, 0x1010);
+          zr2[j][hr] = __byte_perm(pw, 0u, 0x3232);
+        }
+#pragma unroll 2
+      for (int ks = 0; ks < KS; ks += 2) {
+        const uint4 wv = wt[ks * 32 + lane];
+        const uint4 wv2 = wt[(ks + 1) * 32 + lane];
+        const uint2 bx = *reinterpret_cast<const uint2*>(xg + ks * 16);
+        const uint2 bx2 = *reinterpret_cast<const uint2*>(xg + (ks + 1) * 16);
+        const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
+        const uint32_t wr2[4] = {wv2.x, wv2.y, wv2.z, wv2.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t w = wr[j], v = wr2[j];
+          mma_bf16_16816(yacc[j], w4_ref_pair(lop3_and_or(w, 0x000F000Fu, 0x43004300u), sc2[j][0], zr2[j][0]),
+                         w4_ref_pair(lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u), sc2[j][1], zr2[j][1]),
+                         w4_ref_pair(lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u), sc2[j][0], zr2[j][0]),
+                         w4_ref_pair(lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u), sc2[j][1], zr2[j][1]),
+                         bx.x, bx.y);
+          mma_bf16_16816(yacc2[j], w4_ref_pair(lop3_and_or(v, 0x000F000Fu, 0x43004300u), sc2[j][0], zr2[j][0]),
+                         w4_ref_pair(lop3_and_or(v >> 4, 0x000F000Fu, 0x43004300u), sc2[j][1], zr2[j][1]),
+                         w4_ref_pair(lop3_and_or(v >> 8, 0x000F000Fu, 0x43004300u), sc2[j][0], zr2[j][0]),
+                         w4_ref_pair(lop3_and_or(v >> 12, 0x000F000Fu, 0x43004300u), sc2[j][1], zr2[j][1]),
+                         bx2.x, bx2.y);
+        }
+      }
+    } else {
+      // even and odd k16-steps accumulate separately: eight independent MMA
+      // chains per warp instead of four
+      float d[4][4], d2[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) d[j][e] = d2[j][e] = 0.f;
+#pragma unroll 2
+      for (int ks = 0; ks < KS; ks += 2) {
+        const uint4 wv = wt[ks * 32 + lane];
+        const uint4 wv2 = wt[(ks + 1) * 32 + lane];
+        const uint2 bx = *reinterpret_cast<const uint2*>(xg + ks * 16);
+        const uint2 bx2 = *reinterpret_cast<const uint2*>(xg + (ks + 1) * 16);
+        const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
+        const uint32_t wr2[4] = {wv2.x, wv2.y, wv2.z, wv2.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t w = wr[j], v = wr2[j];
+          mma_bf16_16816(d[j], lop3_and_or(w, 0x000F000Fu, 0x43004300u), lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u),
+                         lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u), lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u),
+                         bx.x, bx.y);
+          mma_bf16_16816(d2[j], lop3_and_or(v, 0x000F000Fu, 0x43004300u), lop3_and_or(v >> 4, 0x000F000Fu, 0x43004300u),
+                         lop3_and_or(v >> 8, 0x000F000Fu, 0x43004300u), lop3_and_or(v >> 12, 0x000F000Fu, 0x43004300u),
+                         bx2.x, bx2.y);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) d[j][e] += d2[j][e];
+      // group affine: D = sum x (128 + q)  =>  w = (q - (z + zero_offset)) s gives
+      // y += s D + C Sx with C = -(z + zero_offset + 128) s
+      const float sx0 = gsum[slot * M + min(2 * tq, M - 1)];
+      const float sx1 = gsum[slot * M + min(2 * tq + 1, M - 1)];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+          const int col = 16 * j + gr + 8 * hr;
+          const float A = __half2float(reinterpret_cast<const __half*>(prm)[col]);
           const uint32_t zw = reinterpret_cast<const uint32_t*>(prm + 128)[col >> 3];
           const int z = (int)((zw >> (4 * (col & 7))) & 0xFu) + a.zero_offset;
-          C = -(float)(z + 128) * A;
+          const float C = -(float)(z + 128) * A;
+          yacc[j][2 * hr + 0] = fmaf(A, d[j][2 * hr + 0], fmaf(C, sx0, yacc[j][2 * hr + 0]));
+          yacc[j][2 * hr + 1] = fmaf(A, d[j][2 * hr + 1], fmaf(C, sx1, yacc[j][2 * hr + 1]));
         }
-        yacc[j][2 * hr + 0] = fmaf(A, d[j][2 * hr + 0], fmaf(C, sx0, yacc[j][2 * hr + 0]));
-        yacc[j][2 * hr + 1] = fmaf(A, d[j][2 * hr + 1], fmaf(C, sx1, yacc[j][2 * hr + 1]));
-      }
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     // next tile of this warp: kW4Warps further along

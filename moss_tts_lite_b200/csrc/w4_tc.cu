@@ -2,8 +2,9 @@
 //
 // Replaces torch._weight_int4pack_mm for one activation row as the reference
 // calls it in its decode step (moss_tts_lite/fast.py:118, gptq.py:582,
-// fast_native.py:169): y = x . W_eff^T, W_eff = (q - 8) * scale + zero per
-// group (gptq.py:87-97), fp32 accumulation, bf16 output, with the same fused
+// fast_native.py:169): y = x . W^T, W = bf16((q - 8) * scale + zero) per
+// group (gptq.py:87-97; rounded once to bf16, as torch's int4 GEMM forms its
+// operand), fp32 accumulation, bf16 output, with the same fused
 // RMSNorm prologue and store / residual / SwiGLU epilogues as the
 // register-MMA kernel in w4_gemv.cu.
 //
@@ -15,7 +16,9 @@
 //   A (weights)      TMEM, 128 lanes (rows) x 8 columns per k16 step, written
 //                    by the dequantising warps with tcgen05.st: each thread
 //                    owns one output row and turns 16 int4 codes into eight
-//                    bf16 pairs (128 + q) with one shift + LOP3 per pair;
+//                    bf16 pairs of effective weights (one shift + LOP3 per
+//                    pair for 128 + q, then two bf16x2 FMAs: q - 8, exact,
+//                    and (q - 8) scale + zero, one rounding);
 //   B (activations)  shared memory, K-major, no swizzle.  Only column 0 of
 //                    the N = 16 MMA is used: with the k-chunk stride (LBO) set
 //                    to 16 bytes the canonical core matrices overlap and row 0
@@ -25,8 +28,7 @@
 //                    read);
 //   D (fp32)         TMEM, 128 lanes x 16 columns, one group of k per MMA
 //                    chain; the dequantising warps read column 0 back
-//                    (tcgen05.ld) and apply the group affine in fp32:
-//                    y += A (D - 128 Sx) + B Sx (Sx = the group's sum of x).
+//                    (tcgen05.ld) and add it to the row's fp32 sum.
 //
 // Pipeline per CTA (2 per SM): warp 0 streams tiles with 1-D bulk copies into
 // a shared-memory ring (before the programmatic-dependent-launch wait: the
@@ -88,7 +90,7 @@ __host__ __device__ __forceinline__ int tc_cta_of_tile(long long t, int G, int T
 __host__ __device__ __forceinline__ size_t tc_align(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct TcSmem {
-  size_t bar, misc, ring, xs, bs, gsum, total;
+  size_t bar, misc, ring, xs, total;
 };
 __host__ __device__ inline TcSmem tc_smem(const TcPlan& p, int K, int g) {
   TcSmem L;
@@ -102,11 +104,6 @@ __host__ __device__ inline TcSmem tc_smem(const TcPlan& p, int K, int g) {
   o = tc_align(o, 128);
   L.xs = o;
   o += (size_t)(K + 128) * 2;  // + overreach of the last overlapping core matrix
-  o = tc_align(o, 16);
-  L.bs = o;
-  o += (size_t)(K / 8) * 4;
-  L.gsum = o;
-  o += (size_t)(K / g) * 4;
   L.total = tc_align(o, 128);
   return L;
 }
@@ -188,8 +185,6 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tc_kernel(const __grid_const
   float* red = reinterpret_cast<float*>(smem + L.misc) + 8;  // [4] norm partials
   uint8_t* ring = smem + L.ring;
   uint16_t* xs = reinterpret_cast<uint16_t*>(smem + L.xs);
-  float* bs = reinterpret_cast<float*>(smem + L.bs);
-  float* gsum = reinterpret_cast<float*>(smem + L.gsum);
   const int acols = KS * 8;                       // TMEM columns of one A buffer
   const int dcol0 = kTcBufs * acols;              // first accumulator column
 
@@ -324,38 +319,23 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tc_kernel(const __grid_const
             u[q] = (__float_as_uint(v0) >> 16) | (__float_as_uint(v1) & 0xFFFF0000u);
           }
         }
-        float s8 = 0.f;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) s8 += __uint_as_float(u[q] << 16) + __uint_as_float(u[q] & 0xFFFF0000u);
         reinterpret_cast<uint4*>(xs)[c] = make_uint4(u[0], u[1], u[2], u[3]);
-        bs[c] = s8;
       }
     }
     if (lt < 16) reinterpret_cast<uint4*>(xs + K)[lt] = make_uint4(0, 0, 0, 0);
     fence_proxy_async_smem_tc();  // xs is read by the tensor cores (async proxy)
     named_sync(1, 128);
     named_sync(2, 160);           // the MMA issuer may start
-    for (int G = lt; G < KT; G += 128) {
-      float s = 0.f;
-      for (int c = G * (g / 8); c < (G + 1) * (g / 8); ++c) s += bs[c];
-      gsum[G] = s;
-    }
-    named_sync(1, 128);
 
     // (c) main loop: dequantise tile i, then read back tile i - lag
     constexpr int lag = kTcBufs - 1;
     int G = t0 % KT, nb = t0 / KT;
     int cur = -1;
     float yacc = 0.f;
-    // affine (A, C, Sx) and column block of the tiles whose MMAs are in
-    // flight, oldest first
-    float qA[lag], qC[lag], qS[lag];
+    // column block of the tiles whose MMAs are in flight, oldest first
     int qB[lag];
 #pragma unroll
-    for (int k = 0; k < lag; ++k) {
-      qA[k] = qC[k] = qS[k] = 0.f;
-      qB[k] = -1;
-    }
+    for (int k = 0; k < lag; ++k) qB[k] = -1;
     bool bail = false;
     // A wait that times out sets `bail` (and the CTA flag, so that the other
     // threads stop waiting too) but the warp-collective tcgen05 ld/st and
@@ -441,15 +421,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tc_kernel(const __grid_const
         cur = qB[0];
         yacc = 0.f;
       }
-      // y += A (D - 128 Sx) + B Sx = A D + C Sx, C = B - 128 A
-      yacc = fmaf(qA[0], d, fmaf(qC[0], qS[0], yacc));
+      yacc += d;   // the group's products of bf16 effective weights, summed in fp32
 #pragma unroll
-      for (int k = 0; k + 1 < lag; ++k) {
-        qA[k] = qA[k + 1];
-        qC[k] = qC[k + 1];
-        qS[k] = qS[k + 1];
-        qB[k] = qB[k + 1];
-      }
+      for (int k = 0; k + 1 < lag; ++k) qB[k] = qB[k + 1];
     };
 
     for (int i = 0; i < nt; ++i) {
@@ -459,27 +433,27 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tc_kernel(const __grid_const
       const uint8_t* tile = ring + (size_t)s * stage_bytes + (size_t)(i % tps) * p.tile_bytes;
       const uint2* wp = reinterpret_cast<const uint2*>(tile) + row;
       const uint32_t at = trow + (uint32_t)(buf * acols);
+      // this row's (scale, scale) and (zero, zero) bf16 pairs of the group
+      const uint32_t pw = reinterpret_cast<const uint32_t*>(tile + kTcRows * g / 2)[row];
+      const uint32_t sc2 = __byte_perm(pw, 0u, 0x1010), zr2 = __byte_perm(pw, 0u, 0x3232);
       // A buffer `buf` is free: the MMAs of tile i - kTcBufs completed
-      // (observed by its read-back in iteration i - 1)
+      // (observed by its read-back in iteration i - 1).  A = the bf16
+      // effective weights bf16((q - 8) scale + zero) (gptq.py:87-97, rounded
+      // once as torch's int4 GEMM rounds its operand)
 #pragma unroll 4
       for (int ks = 0; ks < KS; ++ks) {
         const uint2 w = wp[ks * kTcRows];
         uint32_t r[8];
-        r[0] = lop3_and_or(w.x, 0x000F000Fu, 0x43004300u);
-        r[1] = lop3_and_or(w.x >> 4, 0x000F000Fu, 0x43004300u);
-        r[2] = lop3_and_or(w.x >> 8, 0x000F000Fu, 0x43004300u);
-        r[3] = lop3_and_or(w.x >> 12, 0x000F000Fu, 0x43004300u);
-        r[4] = lop3_and_or(w.y, 0x000F000Fu, 0x43004300u);
-        r[5] = lop3_and_or(w.y >> 4, 0x000F000Fu, 0x43004300u);
-        r[6] = lop3_and_or(w.y >> 8, 0x000F000Fu, 0x43004300u);
-        r[7] = lop3_and_or(w.y >> 12, 0x000F000Fu, 0x43004300u);
+        r[0] = w4_ref_pair(lop3_and_or(w.x, 0x000F000Fu, 0x43004300u), sc2, zr2);
+        r[1] = w4_ref_pair(lop3_and_or(w.x >> 4, 0x000F000Fu, 0x43004300u), sc2, zr2);
+        r[2] = w4_ref_pair(lop3_and_or(w.x >> 8, 0x000F000Fu, 0x43004300u), sc2, zr2);
+        r[3] = w4_ref_pair(lop3_and_or(w.x >> 12, 0x000F000Fu, 0x43004300u), sc2, zr2);
+        r[4] = w4_ref_pair(lop3_and_or(w.y, 0x000F000Fu, 0x43004300u), sc2, zr2);
+        r[5] = w4_ref_pair(lop3_and_or(w.y >> 4, 0x000F000Fu, 0x43004300u), sc2, zr2);
+        r[6] = w4_ref_pair(lop3_and_or(w.y >> 8, 0x000F000Fu, 0x43004300u), sc2, zr2);
+        r[7] = w4_ref_pair(lop3_and_or(w.y >> 12, 0x000F000Fu, 0x43004300u), sc2, zr2);
         tmem_st8(at + 8 * ks, r);
       }
-      // group affine of this tile (gptq.py:87-97: w = (q - 8) scale + zero)
-      const uint32_t pw = reinterpret_cast<const uint32_t*>(tile + kTcRows * g / 2)[row];
-      const float A = __uint_as_float(pw << 16);
-      const float C = fmaf(-136.f, A, __uint_as_float(pw & 0xFFFF0000u));
-      const float sx = gsum[G];
       mbar_arrive(&empty[s]);
       tmem_wait_st();
       tc_fence_before();
@@ -488,12 +462,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tc_kernel(const __grid_const
       if (i >= lag) readback(i - lag);
 #pragma unroll
       for (int k = 0; k < lag; ++k)
-        if (k == slot) {
-          qA[k] = A;
-          qC[k] = C;
-          qS[k] = sx;
-          qB[k] = nb;
-        }
+        if (k == slot) qB[k] = nb;
       if (++G == KT) {
         G = 0;
         ++nb;

@@ -4,18 +4,17 @@
 // (the batched multi-stream decode step and short prompts).
 //
 // Per tile (128 output rows x one group of k), as in w4_tc.cu: the four
-// dequantising warps write A = bf16 (128 + q) pairs into TMEM, one thread
-// issues g/16 MMAs M = 128, N = 16, K = 16, and the accumulator comes back
-// two tiles later (tcgen05.ld, 16 columns = 16 batch rows) for the group
-// affine y[m] += A D[m] + C Sx[m].  What changes is B: instead of one
-// activation vector staged once, each tile's [16 rows x g] slice of the
-// activations is staged by the dequantising warps into a B buffer in the
-// canonical K-major layout (core matrices of 8 rows x 16 bytes; k-chunk
-// stride 256 bytes, 8-row stride 128 bytes), RMSNorm applied when fused,
-// one tile ahead of its MMAs (its global loads are issued a tile earlier).
-// The group sums Sx[m] of the slice are reduced with warp shuffles: thread
-// (warp w, lane l) stages chunks c = 2 (l % 8) and c + 1 of row
-// m = 4 w + l / 8, so each row's chunks sit in 8 lanes of one warp.
+// dequantising warps write A = the bf16 effective weights bf16((q - 8) scale
+// + zero) into TMEM, one thread issues g/16 MMAs M = 128, N = 16, K = 16, and
+// the accumulator comes back two tiles later (tcgen05.ld, 16 columns = 16
+// batch rows) and is added to the rows' fp32 sums.  What changes is B:
+// instead of one activation vector staged once, each tile's [16 rows x g]
+// slice of the activations is staged by the dequantising warps into a B
+// buffer in the canonical K-major layout (core matrices of 8 rows x 16
+// bytes; k-chunk stride 256 bytes, 8-row stride 128 bytes), RMSNorm applied
+// when fused, one tile ahead of its MMAs (its global loads are issued a tile
+// earlier).  Thread (warp w, lane l) stages chunks c = 2 (l % 8) and c + 1 of
+// row m = 4 w + l / 8.
 //
 // Batch rows beyond M are zero in B and never read.  The split-K partials
 // are [block][contributor][row m][128] floats; the last CTA to arrive at a
@@ -109,8 +108,6 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + L.misc);
   int* imisc = reinterpret_cast<int*>(smem + L.misc);        // [1] bail, [2] last-arriver flag
   float* rinv_s = reinterpret_cast<float*>(smem + L.misc) + 128;  // [16]
-  float* sxs = reinterpret_cast<float*>(smem + L.misc) + 160;     // [kTcBufs][16] group sums of x
-  float* csum = reinterpret_cast<float*>(smem + L.misc) + 256;    // [16 rows][16 chunks] of the tile being staged
   uint8_t* ring = smem + L.ring;
   uint8_t* bbuf = smem + L.bbuf;
   const size_t bbytes = (size_t)kTcbMaxM * g * 2;  // one B buffer
@@ -246,10 +243,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
         }
       }
     };
-    // normed bf16 chunks into B buffer `buf`, the row's group sum into sxs
-    // (chunk sums added in chunk order, as the one-row kernel does)
+    // normed bf16 chunks into B buffer `buf`
     auto stage_b = [&](int buf, const uint4 (&xv)[2], const uint4 (&nv)[2]) {
-      float cs2[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t u[4] = {xv[h].x, xv[h].y, xv[h].z, xv[h].w};
@@ -265,31 +260,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
           }
         }
         if (!bact) u[0] = u[1] = u[2] = u[3] = 0u;
-        float s8 = 0.f;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) s8 += __uint_as_float(u[q] << 16) + __uint_as_float(u[q] & 0xFFFF0000u);
         if (bc + h < nch)
           *reinterpret_cast<uint4*>(bbuf + buf * bbytes + ((size_t)(bc + h) * kTcbMaxM + bm) * 16) =
               make_uint4(u[0], u[1], u[2], u[3]);
-        cs2[h] = s8;
       }
-      // the row's chunk sums sit in 8 lanes of this warp (chunks 2j, 2j + 1
-      // in lane j): one lane reads the 16 back at once, then adds them in
-      // chunk order
-      if (bc < nch) *reinterpret_cast<float2*>(csum + bm * 16 + bc) = make_float2(cs2[0], cs2[1]);
-      __syncwarp();
-      if ((lane & 7) == 0) {
-        const float4* cr = reinterpret_cast<const float4*>(csum + bm * 16);
-        const float4 c4[4] = {cr[0], cr[1], cr[2], cr[3]};
-        const float cs[16] = {c4[0].x, c4[0].y, c4[0].z, c4[0].w, c4[1].x, c4[1].y, c4[1].z, c4[1].w,
-                              c4[2].x, c4[2].y, c4[2].z, c4[2].w, c4[3].x, c4[3].y, c4[3].z, c4[3].w};
-        float s = 0.f;
-#pragma unroll
-        for (int c = 0; c < 16; ++c)
-          if (c < nch) s += cs[c];
-        sxs[buf * kTcbMaxM + bm] = s;
-      }
-      __syncwarp();
     };
 
     constexpr int lag = kTcBufs - 1;
@@ -298,13 +272,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
     float yacc[kTcbMaxM];
 #pragma unroll
     for (int m = 0; m < kTcbMaxM; ++m) yacc[m] = 0.f;
-    float qA[lag], qC[lag];
     int qB[lag];
 #pragma unroll
-    for (int k = 0; k < lag; ++k) {
-      qA[k] = qC[k] = 0.f;
-      qB[k] = -1;
-    }
+    for (int k = 0; k < lag; ++k) qB[k] = -1;
     bool bail = false;
     volatile int* vbail = imisc + 1;
     auto wait_or_bail = [&](uint64_t* bar, uint32_t parity) {
@@ -383,9 +353,6 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
     auto readback = [&](int j) {
       const int buf = j % kTcBufs;
       tmem_wait_ld16(d);
-      float sx[kTcbMaxM];
-#pragma unroll
-      for (int m = 0; m < kTcbMaxM; ++m) sx[m] = sxs[buf * kTcbMaxM + m];
       tc_fence_before();
       mbar_arrive(&dfree[buf]);
       if (qB[0] != cur) {
@@ -394,23 +361,19 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
 #pragma unroll
         for (int m = 0; m < kTcbMaxM; ++m) yacc[m] = 0.f;
       }
-      // y += A (D - 128 Sx) + B Sx = A D + C Sx, C = B - 128 A
+      // the group's products of bf16 effective weights, summed in fp32
 #pragma unroll
-      for (int m = 0; m < kTcbMaxM; ++m) yacc[m] = fmaf(qA[0], __uint_as_float(d[m]), fmaf(qC[0], sx[m], yacc[m]));
+      for (int m = 0; m < kTcbMaxM; ++m) yacc[m] += __uint_as_float(d[m]);
 #pragma unroll
-      for (int k = 0; k + 1 < lag; ++k) {
-        qA[k] = qA[k + 1];
-        qC[k] = qC[k + 1];
-        qB[k] = qB[k + 1];
-      }
+      for (int k = 0; k + 1 < lag; ++k) qB[k] = qB[k + 1];
     };
 
     uint4 xv[2], nv[2];
     if (nt > 0) load_b(G, xv, nv);
     for (int i = 0; i < nt; ++i) {
       const int st = i / tps, s = st % S, buf = i % kTcBufs;
-      // every thread is done with iteration i - 1, whose read-back used the
-      // group sums (and waited for the MMAs) of buffer `buf`: refill it
+      // every thread is done with iteration i - 1, whose read-back waited
+      // for the MMAs of buffer `buf`: refill its B
       named_sync(1, 128);
       // B of tile i (its x was loaded an iteration ago), then the next x
       stage_b(buf, xv, nv);
@@ -420,24 +383,24 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
       const uint8_t* tile = ring + (size_t)s * stage_bytes + (size_t)(i % tps) * p.tile_bytes;
       const uint2* wp = reinterpret_cast<const uint2*>(tile) + row;
       const uint32_t at = trow + (uint32_t)(buf * acols);
+      // A = the bf16 effective weights bf16((q - 8) scale + zero) of this row
+      // (gptq.py:87-97, one rounding as torch's int4 GEMM forms its operand)
+      const uint32_t pw = reinterpret_cast<const uint32_t*>(tile + kTcRows * g / 2)[row];
+      const uint32_t sc2 = __byte_perm(pw, 0u, 0x1010), zr2 = __byte_perm(pw, 0u, 0x3232);
 #pragma unroll 4
       for (int ks = 0; ks < KS; ++ks) {
         const uint2 w = wp[ks * kTcRows];
         uint32_t r[8];
-        r[0] = lop3_and_or(w.x, 0x000F000Fu, 0x43004300u);
-        r[1] = lop3_and_or(w.x >> 4, 0x000F000Fu, 0x43004300u);
-        r[2] = lop3_and_or(w.x >> 8, 0x000F000Fu, 0x43004300u);
-        r[3] = lop3_and_or(w.x >> 12, 0x000F000Fu, 0x43004300u);
-        r[4] = lop3_and_or(w.y, 0x000F000Fu, 0x43004300u);
-        r[5] = lop3_and_or(w.y >> 4, 0x000F000Fu, 0x43004300u);
-        r[6] = lop3_and_or(w.y >> 8, 0x000F000Fu, 0x43004300u);
-        r[7] = lop3_and_or(w.y >> 12, 0x000F000Fu, 0x43004300u);
+        r[0] = w4_ref_pair(lop3_and_or(w.x, 0x000F000Fu, 0x43004300u), sc2, zr2);
+        r[1] = w4_ref_pair(lop3_and_or(w.x >> 4, 0x000F000Fu, 0x43004300u), sc2, zr2);
+        r[2] = w4_ref_pair(lop3_and_or(w.x >> 8, 0x000F000Fu, 0x43004300u), sc2, zr2);
+        r[3] = w4_ref_pair(lop3_and_or(w.x >> 12, 0x000F000Fu, 0x43004300u), sc2, zr2);
+        r[4] = w4_ref_pair(lop3_and_or(w.y, 0x000F000Fu, 0x43004300u), sc2, zr2);
+        r[5] = w4_ref_pair(lop3_and_or(w.y >> 4, 0x000F000Fu, 0x43004300u), sc2, zr2);
+        r[6] = w4_ref_pair(lop3_and_or(w.y >> 8, 0x000F000Fu, 0x43004300u), sc2, zr2);
+        r[7] = w4_ref_pair(lop3_and_or(w.y >> 12, 0x000F000Fu, 0x43004300u), sc2, zr2);
         tmem_st8(at + 8 * ks, r);
       }
-      // group affine of this tile (gptq.py:87-97: w = (q - 8) scale + zero)
-      const uint32_t pw = reinterpret_cast<const uint32_t*>(tile + kTcRows * g / 2)[row];
-      const float A = __uint_as_float(pw << 16);
-      const float C = fmaf(-136.f, A, __uint_as_float(pw & 0xFFFF0000u));
       mbar_arrive(&empty[s]);
       fence_proxy_async_smem_tc();  // B is read by the tensor cores (async proxy)
       tmem_wait_st();
@@ -447,11 +410,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) w4_tcb_kernel(const __grid_cons
       if (i >= lag) readback(i - lag);
 #pragma unroll
       for (int k = 0; k < lag; ++k)
-        if (k == slot) {
-          qA[k] = A;
-          qC[k] = C;
-          qB[k] = nb;
-        }
+        if (k == slot) qB[k] = nb;
       if (++G == KT) {
         G = 0;
         ++nb;

@@ -21,15 +21,16 @@ same bf16 rounding points as the reference:
   (model.py:240-295, fast.py:174-194).
 
 Weights are carried as bf16 bit patterns (uint16). A linear may instead be a
-W4 record ``(q uint8 [N, K], qsz bf16 bits [K/g, N, 2], g)``; its effective
-weight is ``oracle.w4.ref_effective_weight``.
+W4 record ``(q uint8 [N, K], qsz bf16 bits [K/g, N, 2], g)``; its weight is
+``oracle.w4.ref_operand_weight`` (the effective weight rounded to bf16, the
+operand of the reference's int4 GEMM).
 """
 from __future__ import annotations
 
 import numpy as np
 
 from .bf16 import bf16_to_f32, f32_to_bf16, round_bf16
-from .w4 import ref_effective_weight
+from .w4 import ref_operand_weight
 
 N_VQ = 32
 AUDIO_PAD_CODE = 1024
@@ -157,9 +158,10 @@ class OracleModel:
 
     def quantize_w4(self, qrecs: dict):
         """Install W4 records ``{(li, name): (q [N,K] uint8, qsz bits, g)}``;
-        those linears then use the reference dequant (gptq.py:87-97)."""
+        those linears then multiply with the reference's int4 GEMM operand
+        (gptq.py:87-97 rounded to bf16, as _weight_int4pack_mm forms it)."""
         for (li, name), (q, qsz, g) in qrecs.items():
-            self._w_eff[li][name] = ref_effective_weight(q, qsz, g)
+            self._w_eff[li][name] = ref_operand_weight(q, qsz, g)
 
     def linear(self, x_bits: np.ndarray, li: int, name: str) -> np.ndarray:
         w = self._w_eff[li][name]                   # [N, K] fp32

@@ -153,6 +153,22 @@ def ref_effective_weight(q: np.ndarray, qsz_bits: np.ndarray, group_size: int = 
     return w.reshape(n, k).astype(np.float32)
 
 
+def ref_operand_weight(q: np.ndarray, qsz_bits: np.ndarray, group_size: int = 128) -> np.ndarray:
+    """The operand torch's int4 GEMM (``_weight_int4pack_mm``, the reference's
+    W4 linear at fast.py:118 / gptq.py:582) multiplies with: the effective
+    weight of gptq.py:87-97 rounded once to bf16 (bf16 FMA of the exact
+    q - 8 with the bf16 scale and zero).  Returned widened to fp32 [N, K].
+    Pinned against the kernel's own outputs by tests/golden/tinygemm.npz."""
+    n, k = q.shape
+    g = group_size
+    qsz = bf16_to_f32(qsz_bits).astype(np.float64)    # [G, N, 2]
+    scale = qsz[:, :, 0].T                            # [N, G]
+    zero = qsz[:, :, 1].T
+    qf = q.astype(np.float64).reshape(n, k // g, g)
+    exact = (qf - 8.0) * scale[..., None] + zero[..., None]   # exact in fp64
+    return bf16_to_f32(f32_to_bf16(exact.reshape(n, k).astype(np.float32)))
+
+
 # --------------------------------------------------------------------------
 # The W4A16 linear itself
 # --------------------------------------------------------------------------

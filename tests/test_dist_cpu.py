@@ -61,6 +61,6 @@ def test_reference_arm_is_rank0_only(monkeypatch):
         steps, warmup, gpus = 1, 1, 2
 
     called = []
-    monkeypatch.setattr(bench, "CpuStep", lambda: called.append(1))
+    monkeypatch.setattr(bench, "cpu_step_runner", lambda *a: called.append(1))
     assert bench.run_reference_arm(_Args(), ctx) is None
     assert called == []

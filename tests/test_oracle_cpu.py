@@ -212,3 +212,27 @@ def test_inner_scan_thread_split():
     reference scans: [R, 1025] for R = 2..31 sampled channels."""
     assert [osmp.inner_scan_log_threads_x(r, 1025) for r in (2, 4, 5, 8, 9, 16, 17, 31)] == [9, 9, 8, 8, 8, 8, 7, 7]
     assert osmp.inner_scan_log_threads_x(1024, 16) == 4
+
+
+def test_operand_weight_pinned_to_tinygemm():
+    """The reference's W4 linear (torch._weight_int4pack_mm on the reference's
+    own RTN codes, run on a B200 by tests/golden/make_golden_tinygemm.py)
+    multiplies with the effective weight rounded once to bf16: the oracle
+    with ref_operand_weight reproduces its outputs up to the fp32 summation
+    order (almost all bitwise, the rest within one bf16 ulp), while the
+    unrounded fp32 effective weight does not."""
+    path = os.path.join(GOLD, "tinygemm.npz")
+    if not os.path.exists(path):
+        pytest.skip("tinygemm fixture not generated yet")
+    z = np.load(path)
+    n_cases = len([k for k in z.files if k.endswith("_shape")])
+    for ci in range(n_cases):
+        M, K, N, g = (int(v) for v in z[f"c{ci}_shape"])
+        q, qsz, x, y = z[f"c{ci}_q"], z[f"c{ci}_qsz"], z[f"c{ci}_x"], z[f"c{ci}_y"]
+        yo = ow.linear_bf16(x, ow.ref_operand_weight(q, qsz, g).T)
+        ye = ow.linear_bf16(x, ow.ref_effective_weight(q, qsz, g).T)
+        same = (yo == y).mean()
+        ulp = np.abs(bf16_to_f32(y)) * 2.0 ** -7 + 1e-30
+        assert same > 0.98, (ci, same)
+        assert (np.abs(bf16_to_f32(yo) - bf16_to_f32(y)) <= ulp * 1.001).all(), ci
+        assert (ye == y).mean() < same, ci
