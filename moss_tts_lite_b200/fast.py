@@ -28,7 +28,7 @@ from .generate import GenResult
 from .model import (AUDIO_DELAY_SLOT_TOKEN_ID, AUDIO_END_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_PAD_CODE,
                     AUDIO_START_TOKEN_ID, AUDIO_VOCAB, IM_END_TOKEN_ID, LIN_NAMES, N_VQ, PAD_TOKEN_ID,
                     RMS_EPS, HiddenState)
-from .quant import W4Weight
+from .quant import W4Weight, gemm_supported
 
 _INT64_MAX = 9223372036854775807
 _LIN_NAMES = LIN_NAMES
@@ -219,8 +219,7 @@ class _StepEngine:
         m = self.m
         kcs, vcs = caches if caches is not None else (m.k_cache, m.v_cache)
         L = ids.shape[0]
-        if L >= _GEMM_PREFILL_ROWS and all(isinstance(self.lins[0][n], _W4Lin) and self.lins[0][n].w.fmt !=
-                                          _lib.MTL_FMT_TC and self.lins[0][n].w.k_perm is None
+        if L >= _GEMM_PREFILL_ROWS and all(isinstance(self.lins[0][n], _W4Lin) and gemm_supported(self.lins[0][n].w)
                                           for n in ("qkv", "o", "gu", "down")):
             return self._prefill_gemm(ids, kcs, vcs)
         H = m.hidden_size
@@ -256,50 +255,42 @@ class _StepEngine:
         return out
 
     def _prefill_gemm(self, ids: torch.Tensor, kcs, vcs) -> torch.Tensor:
-        """A long prompt, layer by layer over all its rows (fast.py:218-270,
-        where the reference runs each projection as one tinygemm call with
-        M = L): each projection is one bf16 GEMM (cuBLAS through
-        torch.matmul) on the layer's effective weights, dequantised from the
-        W4 tiles just before (``mtl_w4_dequant``); one launch appends every
-        row's normed + rotated K and V to the cache and writes the normed +
-        rotated q heads, and the attention is the reference's own causal
-        ``F.scaled_dot_product_attention`` over the cache (fast.py:237-241).
-        The residual adds and SwiGLU are the reference's bf16 tensor ops."""
+        """A long prompt, layer by layer over all its rows, as the reference
+        prefills (fast.py:218-270, every projection one int4 GEMM with
+        M = L): each projection is one tcgen05 W4 GEMM over all rows on the
+        packed weights (``mtl_w4a16_gemm``; the o and down projections add
+        the residual, gate|up applies SwiGLU in its epilogue); one launch
+        appends every row's normed + rotated K and V to the cache and writes
+        the normed + rotated q heads, and the attention is the reference's
+        own causal ``F.scaled_dot_product_attention`` over the cache
+        (fast.py:237-241)."""
         m = self.m
         L = ids.shape[0]
         H, D = m.hidden_size, m.head_dim
         dev, bf = m.device, torch.bfloat16
         nq = m.n_heads * D
         rep = m.n_heads // m.n_kv_heads
-        if getattr(self, "_g_wbuf", None) is None:
-            big = max(Lw[n].w.N * Lw[n].w.K for Lw in self.lins[:1] for n in ("qkv", "o", "gu", "down"))
-            self._g_wbuf = torch.empty(big, dtype=bf, device=dev)
-
-        def weight(lin):
-            w = lin.w
-            return w.dequant(self._g_wbuf[:w.N * w.K].view(w.N, w.K))
         h = torch.empty(L, H, dtype=bf, device=dev)
         xn = torch.empty(L, H, dtype=bf, device=dev)
         qn = torch.empty(L, m.n_heads, D, dtype=bf, device=dev)
+        qkv = torch.empty(L, self.lins[0]["qkv"].N, dtype=bf, device=dev)
+        act = torch.empty(L, self.lins[0]["gu"].N // 2, dtype=bf, device=dev)
         pos = torch.arange(L, dtype=torch.long, device=dev)
         kernels.embed_sum(ids.contiguous(), m.embed_tokens, self.emb_audio, h)
         for li in range(m.n_layers):
             lyr, Lw = m.layers[li], self.lins[li]
             kernels.rmsnorm(h, lyr["input_layernorm"], xn, RMS_EPS)
-            qkv = torch.matmul(xn, weight(Lw["qkv"]).t())
+            Lw["qkv"].w.gemm(xn, out=qkv)
             kernels.attn_append(qkv, lyr["k_norm"], m.rope_cos, m.rope_sin, kcs[li], vcs[li], pos, m.n_heads,
                                 m.n_kv_heads, streams=L, q_norm_w=lyr["q_norm"], q_out=qn)
             keys = kcs[li][:, :L].repeat_interleave(rep, dim=0).unsqueeze(0)
             vals = vcs[li][:, :L].repeat_interleave(rep, dim=0).unsqueeze(0)
             attn = F.scaled_dot_product_attention(qn.view(1, L, m.n_heads, D).transpose(1, 2), keys, vals,
-                                                  is_causal=True).transpose(1, 2).reshape(L, nq)
-            h = h + torch.matmul(attn, weight(Lw["o"]).t())                 # fast.py:168
+                                                  is_causal=True).transpose(1, 2).reshape(L, nq).contiguous()
+            Lw["o"].w.gemm(attn, residual=h, out=h)                                  # fast.py:168
             kernels.rmsnorm(h, lyr["post_attention_layernorm"], xn, RMS_EPS)
-            gu = torch.matmul(xn, weight(Lw["gu"]).t())
-            fb = Lw["gu"].fuse_block                                         # gate|up interleaved per block
-            gu = gu.view(L, -1, 2, fb)
-            act = (F.silu(gu[:, :, 0]) * gu[:, :, 1]).reshape(L, -1)         # fast.py:170-171
-            h = h + torch.matmul(act, weight(Lw["down"]).t())                # fast.py:170
+            Lw["gu"].w.gemm(xn, out=act, swiglu=True)                                 # fast.py:170-171
+            Lw["down"].w.gemm(act, residual=h, out=h)                                 # fast.py:170
         out = torch.empty(L, H, dtype=bf, device=dev)
         kernels.rmsnorm(h, m.final_norm, out, RMS_EPS)
         return out

@@ -147,6 +147,38 @@ class W4Weight:
         return out.reshape(*lead, nout)
 
 
+def gemm_supported(w: "W4Weight") -> bool:
+    """Whether the tcgen05 prefill GEMM (mtl_w4a16_gemm) serves this weight."""
+    return (w.fmt == _lib.MTL_FMT_REF and w.k_perm is None and w.group_size >= 64 and w.K % 64 == 0
+            and w.N % 128 == 0)
+
+
+def _gemm(self: "W4Weight", x: torch.Tensor, *, out: torch.Tensor | None = None,
+          residual: torch.Tensor | None = None, swiglu: bool = False) -> torch.Tensor:
+    """Many-row W4 GEMM on the tensor cores (the prompt prefill): ``x`` bf16
+    [M, K] -> bf16 [M, N] (or [M, N/2] with swiglu; ``residual`` [M, N] added
+    and rounded as the reference's residual add, may be ``out``)."""
+    if not gemm_supported(self):
+        raise ValueError("mtl_w4a16_gemm needs reference-format tiles, group_size >= 64, K % 64 == 0, N % 128 == 0")
+    x2 = x.reshape(-1, self.K)
+    if x2.dtype != torch.bfloat16 or not x2.is_contiguous():
+        raise ValueError("x must be contiguous bf16 [M, K]")
+    M = x2.shape[0]
+    nout = self.N // 2 if swiglu else self.N
+    epi = _lib.MTL_EPI_SWIGLU if swiglu else (_lib.MTL_EPI_RESIDUAL if residual is not None else _lib.MTL_EPI_STORE)
+    if out is None:
+        out = torch.empty(M, nout, dtype=torch.bfloat16, device=x.device)
+    if M == 0:
+        return out
+    r2 = residual.reshape(M, self.N) if residual is not None else None
+    _lib.call("mtl_w4a16_gemm", x2.data_ptr(), self.K, M, self.K, self.N, self.group_size, self.tiles.data_ptr(), epi,
+              _ptr(r2), self.N, out.data_ptr(), nout, _stream())
+    return out
+
+
+W4Weight.gemm = _gemm
+
+
 class RefW4Linear(torch.nn.Module):
     """The reference's W4 linear (``(packed, qsz)`` call sites of fast.py:118,
     gptq.py:582) built from the codes before tinygemm packing."""

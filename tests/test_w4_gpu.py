@@ -214,9 +214,10 @@ def test_vs_reference_tinygemm():
         y_ref = torch._weight_int4pack_mm(x, packed, g, qsz)
         y = RefW4Linear(q, qsz, g)(x)
         same = (y.view(torch.int16) == y_ref.view(torch.int16)).float().mean().item()
-        ulp = y_ref.float().abs() * 2.0 ** -7 + 1e-30
+        # one bf16 ulp, or the fp32 summation noise where an output cancels to ~0
+        tol = torch.clamp(y_ref.float().abs() * 2.0 ** -7, min=1e-4)
         assert same > 0.99, (M, same)
-        assert bool(((y.float() - y_ref.float()).abs() <= ulp * 1.001).all()), M
+        assert bool(((y.float() - y_ref.float()).abs() <= tol * 1.001).all()), M
         w_eff = ref.effective_weight(q, qsz, g)
         exact = x.float() @ w_eff.t()
         rel_mine = ((y.float() - exact).norm() / exact.norm()).item()
