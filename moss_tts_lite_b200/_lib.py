@@ -55,6 +55,8 @@ SIGNATURES = {
                                           _c_int, _c_void_p]),
     "mtl_w4a16_gemm": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_int, _c_void_p,
                                 _c_int, _c_void_p, _c_int, _c_void_p]),
+    "mtl_attn_prefill": (_c_int, [_c_void_p, _c_void_p, _c_void_p, ctypes.c_longlong, _c_int, _c_int, _c_int,
+                                  _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
     "mtl_embed_sum": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_void_p, _c_int, _c_void_p, _c_void_p]),
     "mtl_attn_scratch_bytes": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_size_p]),
     "mtl_attn_decode": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,

@@ -121,6 +121,25 @@ class BatchedFastMossTTS:
         self.seq[s] = L
         return out
 
+    def prefill_all(self, prompts: list) -> torch.Tensor:
+        """Every stream's prompt (rows [L, 33] each, stream s = prompts[s]) in
+        one pass: with equal lengths of at least 32 rows the projections run
+        as tcgen05 W4 GEMMs over all streams' rows at once (M = streams x L)
+        and one attention launch covers every stream's cache; otherwise
+        stream by stream.  Returns the final-normed hidden [streams * L, H]
+        (or the per-stream results concatenated)."""
+        if len(prompts) != self.B:
+            raise ValueError(f"{len(prompts)} prompts for {self.B} streams")
+        rows = [p.reshape(-1, N_VQ + 1).to(device=self.m.device, dtype=torch.long) for p in prompts]
+        L = int(rows[0].shape[0])
+        eng = self.fast.engine
+        if all(int(r.shape[0]) == L for r in rows) and eng.gemm_prefill_ok(L) and L < self.max_seq:
+            out = eng._prefill_gemm(torch.cat(rows, 0), [self.k_cache[li] for li in range(self.m.n_layers)],
+                                    [self.v_cache[li] for li in range(self.m.n_layers)], streams=self.B)
+            self.seq = [L] * self.B
+            return out
+        return torch.cat([self.prefill(s, r) for s, r in enumerate(rows)], 0)
+
     def start(self, s: int, row: torch.Tensor, pos: int) -> None:
         """Set stream ``s``'s next input row [33] and its cache position."""
         self.ids[s].copy_(row.reshape(-1))

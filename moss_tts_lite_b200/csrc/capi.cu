@@ -42,6 +42,8 @@ int w4_tcb_plan(int K, int N, int g, int num_sms, TcPlan* out);
 cudaError_t w4_tcb_launch(const TcbArgs& a, cudaStream_t stream, int use_pdl);
 cudaError_t w4_tc_pack(const uint8_t* q, const uint16_t* qsz, int K, int N, int g, uint8_t* tiles, cudaStream_t s);
 cudaError_t w4_tc_unpack_codes(const uint8_t* tiles, int K, int N, int g, uint8_t* codes, cudaStream_t s);
+struct PrefillAttnArgs;
+cudaError_t launch_attn_prefill(const PrefillAttnArgs& a, int streams, cudaStream_t s);
 cudaError_t w4_gemm_launch(const uint16_t* x, int ldx, int L, int K, int N, int g, const uint8_t* tiles, int epi,
                            const uint16_t* residual, int ldr, uint16_t* y, int ldy, int num_sms, cudaStream_t s,
                            int use_pdl);
@@ -398,6 +400,39 @@ int mtl_w4a16_gemm(const uint16_t* x, int ldx, int M, int K, int N, int group_si
   cudaError_t e = mtl::w4_gemm_launch(x, ldx, M, K, N, group_size, static_cast<const uint8_t*>(tiles), epilogue,
                                       residual, ldr, y, ldy, num_sms(), stream, use_pdl() ? 1 : 0);
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4a16_gemm");
+}
+
+int mtl_attn_prefill(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                     long long cache_stream_stride, int max_seq, int n_heads, int n_kv, int head_dim,
+                     int rows_per_stream, int streams, int p0, uint16_t* out, mtl_stream_t stream) {
+  if (!q || !k_cache || !v_cache || !out) return fail(MTL_E_INVALID, "mtl_attn_prefill: NULL pointer");
+  if (head_dim != 128) return fail(MTL_E_UNSUPPORTED, "head_dim %d (only 128)", head_dim);
+  if (n_kv <= 0 || n_heads % n_kv) return fail(MTL_E_INVALID, "n_heads=%d n_kv=%d", n_heads, n_kv);
+  const int rep = n_heads / n_kv;
+  if (rep != 1 && rep != 2 && rep != 4 && rep != 8)
+    return fail(MTL_E_UNSUPPORTED, "mtl_attn_prefill: %d query heads per KV head (1/2/4/8 served)", rep);
+  if (rows_per_stream < 1 || streams < 1 || p0 < 0 || p0 + rows_per_stream > max_seq)
+    return fail(MTL_E_INVALID, "rows_per_stream=%d streams=%d p0=%d max_seq=%d", rows_per_stream, streams, p0,
+                max_seq);
+  if (streams > 1 && cache_stream_stride < (long long)n_kv * max_seq * 128)
+    return fail(MTL_E_INVALID, "cache_stream_stride %lld below one stream's cache", cache_stream_stride);
+  if (!aligned(q, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(out, 4))
+    return fail(MTL_E_ALIGN, "mtl_attn_prefill: q / caches 16-byte, out 4-byte aligned");
+  if (streams > 1 && (cache_stream_stride % 8)) return fail(MTL_E_ALIGN, "cache_stream_stride %% 8 != 0");
+  mtl::PrefillAttnArgs a{};
+  a.q = q;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.cache_stream_stride = streams > 1 ? cache_stream_stride : 0;
+  a.max_seq = max_seq;
+  a.nh = n_heads;
+  a.nkv = n_kv;
+  a.rows_per_stream = rows_per_stream;
+  a.p0 = p0;
+  a.scale = 1.0f / sqrtf(128.0f);
+  a.out = out;
+  cudaError_t e = mtl::launch_attn_prefill(a, streams, stream);
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_attn_prefill");
 }
 
 int mtl_embed_sum(const int64_t* ids, int M, const uint16_t* emb_text, int text_vocab, const uint16_t* emb_audio,

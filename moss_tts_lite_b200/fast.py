@@ -21,7 +21,6 @@ import time
 from dataclasses import dataclass, field
 
 import torch
-import torch.nn.functional as F
 
 from . import _lib, fsm, kernels
 from .generate import GenResult
@@ -219,8 +218,7 @@ class _StepEngine:
         m = self.m
         kcs, vcs = caches if caches is not None else (m.k_cache, m.v_cache)
         L = ids.shape[0]
-        if L >= _GEMM_PREFILL_ROWS and all(isinstance(self.lins[0][n], _W4Lin) and gemm_supported(self.lins[0][n].w)
-                                          for n in ("qkv", "o", "gu", "down")):
+        if self.gemm_prefill_ok(L):
             return self._prefill_gemm(ids, kcs, vcs)
         H = m.hidden_size
         C = self._prefill_chunk_rows()
@@ -254,46 +252,61 @@ class _StepEngine:
             kernels.rmsnorm(h, m.final_norm, out[r0:r0 + R], RMS_EPS)
         return out
 
-    def _prefill_gemm(self, ids: torch.Tensor, kcs, vcs) -> torch.Tensor:
-        """A long prompt, layer by layer over all its rows, as the reference
+    def _prefill_gemm(self, ids: torch.Tensor, kcs, vcs, streams: int = 1) -> torch.Tensor:
+        """Long prompts, layer by layer over all their rows, as the reference
         prefills (fast.py:218-270, every projection one int4 GEMM with
         M = L): each projection is one tcgen05 W4 GEMM over all rows on the
         packed weights (``mtl_w4a16_gemm``; the o and down projections add
-        the residual, gate|up applies SwiGLU in its epilogue); one launch
-        appends every row's normed + rotated K and V to the cache and writes
-        the normed + rotated q heads, and the attention is the reference's
-        own causal ``F.scaled_dot_product_attention`` over the cache
-        (fast.py:237-241)."""
+        the residual, gate|up applies SwiGLU in its epilogue); one launch per
+        stream appends its rows' normed + rotated K and V to the cache and
+        writes the normed + rotated q heads, and one causal GQA attention
+        launch (``mtl_attn_prefill``) reads each K/V tile once per head group
+        where the reference expands K/V and runs SDPA (fast.py:237-241).
+
+        ``streams`` > 1: ``ids`` holds that many prompts of equal length one
+        after the other, and ``kcs`` / ``vcs`` [layer] are [streams, n_kv,
+        max_seq, 128] caches; the GEMMs then run over all streams' rows at
+        once (M = streams x L)."""
         m = self.m
-        L = ids.shape[0]
+        L_all = ids.shape[0]
+        L = L_all // streams
         H, D = m.hidden_size, m.head_dim
         dev, bf = m.device, torch.bfloat16
         nq = m.n_heads * D
-        rep = m.n_heads // m.n_kv_heads
-        h = torch.empty(L, H, dtype=bf, device=dev)
-        xn = torch.empty(L, H, dtype=bf, device=dev)
-        qn = torch.empty(L, m.n_heads, D, dtype=bf, device=dev)
-        qkv = torch.empty(L, self.lins[0]["qkv"].N, dtype=bf, device=dev)
-        act = torch.empty(L, self.lins[0]["gu"].N // 2, dtype=bf, device=dev)
+        h = torch.empty(L_all, H, dtype=bf, device=dev)
+        xn = torch.empty(L_all, H, dtype=bf, device=dev)
+        qn = torch.empty(L_all, m.n_heads, D, dtype=bf, device=dev)
+        qkv = torch.empty(L_all, self.lins[0]["qkv"].N, dtype=bf, device=dev)
+        act = torch.empty(L_all, self.lins[0]["gu"].N // 2, dtype=bf, device=dev)
+        attn = torch.empty(L_all, nq, dtype=bf, device=dev)
         pos = torch.arange(L, dtype=torch.long, device=dev)
         kernels.embed_sum(ids.contiguous(), m.embed_tokens, self.emb_audio, h)
         for li in range(m.n_layers):
             lyr, Lw = m.layers[li], self.lins[li]
             kernels.rmsnorm(h, lyr["input_layernorm"], xn, RMS_EPS)
             Lw["qkv"].w.gemm(xn, out=qkv)
-            kernels.attn_append(qkv, lyr["k_norm"], m.rope_cos, m.rope_sin, kcs[li], vcs[li], pos, m.n_heads,
-                                m.n_kv_heads, streams=L, q_norm_w=lyr["q_norm"], q_out=qn)
-            keys = kcs[li][:, :L].repeat_interleave(rep, dim=0).unsqueeze(0)
-            vals = vcs[li][:, :L].repeat_interleave(rep, dim=0).unsqueeze(0)
-            attn = F.scaled_dot_product_attention(qn.view(1, L, m.n_heads, D).transpose(1, 2), keys, vals,
-                                                  is_causal=True).transpose(1, 2).reshape(L, nq).contiguous()
+            if streams == 1:
+                kernels.attn_append(qkv, lyr["k_norm"], m.rope_cos, m.rope_sin, kcs[li], vcs[li], pos, m.n_heads,
+                                    m.n_kv_heads, streams=L, q_norm_w=lyr["q_norm"], q_out=qn)
+            else:
+                for s in range(streams):
+                    r = slice(s * L, (s + 1) * L)
+                    kernels.attn_append(qkv[r], lyr["k_norm"], m.rope_cos, m.rope_sin, kcs[li][s], vcs[li][s], pos,
+                                        m.n_heads, m.n_kv_heads, streams=L, q_norm_w=lyr["q_norm"], q_out=qn[r])
+            kernels.attn_prefill(qn, kcs[li], vcs[li], m.n_heads, m.n_kv_heads, attn, rows_per_stream=L,
+                                 streams=streams, cache_stream_stride=kcs[li][0].numel() if streams > 1 else 0)
             Lw["o"].w.gemm(attn, residual=h, out=h)                                  # fast.py:168
             kernels.rmsnorm(h, lyr["post_attention_layernorm"], xn, RMS_EPS)
             Lw["gu"].w.gemm(xn, out=act, swiglu=True)                                 # fast.py:170-171
             Lw["down"].w.gemm(act, residual=h, out=h)                                 # fast.py:170
-        out = torch.empty(L, H, dtype=bf, device=dev)
+        out = torch.empty(L_all, H, dtype=bf, device=dev)
         kernels.rmsnorm(h, m.final_norm, out, RMS_EPS)
         return out
+
+    def gemm_prefill_ok(self, L: int) -> bool:
+        """Whether a prompt of L rows prefills through the tensor-core GEMM path."""
+        return L >= _GEMM_PREFILL_ROWS and all(isinstance(self.lins[0][n], _W4Lin) and gemm_supported(self.lins[0][n].w)
+                                               for n in ("qkv", "o", "gu", "down"))
 
 
 # --------------------------------------------------------------- FastMossTTS

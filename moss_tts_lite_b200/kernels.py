@@ -70,6 +70,19 @@ def attn_append(qkv, k_norm_w, rope_cos, rope_sin, k_cache_layer, v_cache_layer,
               k_cache_layer.shape[-1], _p(q_out), _s())
 
 
+def attn_prefill(q: torch.Tensor, k_cache_layer: torch.Tensor, v_cache_layer: torch.Tensor, n_heads: int,
+                 n_kv: int, out: torch.Tensor, *, rows_per_stream: int | None = None, streams: int = 1, p0: int = 0,
+                 cache_stream_stride: int = 0) -> torch.Tensor:
+    """Causal GQA attention over prompt rows (mtl_attn_prefill): q bf16
+    [streams * rows, n_heads, 128] (normed + rotated), one layer's caches
+    [n_kv, max_seq, 128] per stream, out bf16 [streams * rows, n_heads * 128]."""
+    rows = rows_per_stream if rows_per_stream is not None else q.shape[0] // streams
+    _lib.call("mtl_attn_prefill", q.data_ptr(), k_cache_layer.data_ptr(), v_cache_layer.data_ptr(),
+              ctypes.c_longlong(cache_stream_stride), k_cache_layer.shape[-2], n_heads, n_kv, q.shape[-1], rows,
+              streams, p0, out.data_ptr(), _s())
+    return out
+
+
 def bf16_linear(x: torch.Tensor, W: torch.Tensor, out: torch.Tensor, *, norm_weight=None, eps: float = 1e-6,
                 x_normed=None, pad_period: int = 0, pad_col: int = 0, residual=None,
                 swiglu: bool = False) -> torch.Tensor:

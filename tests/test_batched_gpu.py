@@ -101,3 +101,24 @@ def test_batched_tensor_core_tiles_agree():
     assert agree >= 0.95, agree
     from moss_tts_lite_b200 import _lib
     assert _lib.device_status() == 0
+
+
+def test_prefill_all_equals_per_stream_prefill():
+    """All streams' prompts prefilled together (tcgen05 GEMMs over M = streams
+    x L rows, one attention launch over every stream's cache) equal the
+    streams prefilled one at a time, bit for bit: hidden states and caches."""
+    dev = require_cuda()
+    from moss_tts_lite_b200.batched import BatchedFastMossTTS
+    fast, m, om = _w4_setup(dev, seed=35, max_seq=160)
+    B, L = 3, 40
+    prompts = [_t(_prompt(L, seed=80 + s), dev) for s in range(B)]
+    together = BatchedFastMossTTS(fast, B, max_seq=128)
+    h_all = together.prefill_all(prompts)
+    apart = BatchedFastMossTTS(fast, B, max_seq=128)
+    h_each = torch.cat([apart.prefill(s, prompts[s]) for s in range(B)], 0)
+    torch.cuda.synchronize()
+    assert torch.equal(h_all.view(torch.int16), h_each.view(torch.int16))
+    assert torch.equal(together.k_cache[:, :, :, :L].view(torch.int16), apart.k_cache[:, :, :, :L].view(torch.int16))
+    assert torch.equal(together.v_cache[:, :, :, :L].view(torch.int16), apart.v_cache[:, :, :, :L].view(torch.int16))
+    from moss_tts_lite_b200 import _lib
+    assert _lib.device_status() == 0

@@ -385,16 +385,18 @@ def test_cfg4_streams_match_reference_batch1(trio):
     B, L, STEPS = 16, 256, 12
     g = torch.Generator().manual_seed(4)
     bt = BatchedFastMossTTS(mine, B, max_seq=L + STEPS + 8)
-    prompts = []
+    prompts, firsts = [], []
     for s in range(B):
         ids = torch.zeros(L, N_VQ + 1, dtype=torch.long)
         ids[:, 0] = torch.randint(0, 151643, (L,), generator=g)
         ids[:, 1:] = torch.randint(0, 1024, (L, N_VQ), generator=g)
         ids[-1, 0] = AUDIO_START_TOKEN_ID
         first = torch.cat([torch.tensor([AUDIO_GEN_SLOT_TOKEN_ID]), torch.randint(0, 1024, (N_VQ,), generator=g)])
-        bt.prefill(s, ids.to(dev))
-        bt.start(s, first.to(dev), L)
         prompts.append(ids)
+        firsts.append(first)
+    bt.prefill_all([p.to(dev) for p in prompts])     # the M = 16 x 256 tensor-core prefill
+    for s in range(B):
+        bt.start(s, firsts[s].to(dev), L)
     bt.capture()
     rows, las, twos = [], [], []
     for _ in range(STEPS):

@@ -125,3 +125,44 @@ def test_gemm_rejects_unserved_shapes():
     rc = _lib.lib.mtl_w4a16_gemm(x.data_ptr(), 256, 8, 256, 128, 32, w.tiles.data_ptr(), 0, None, 0, y.data_ptr(),
                                  128, torch.cuda.current_stream().cuda_stream)
     assert rc == _lib.MTL_E_UNSUPPORTED
+
+
+@pytest.mark.parametrize("L,rep,streams,p0", [(128, 4, 1, 0), (300, 4, 1, 0), (77, 2, 3, 0), (64, 8, 2, 0),
+                                              (40, 4, 1, 150), (1, 1, 1, 0)])
+def test_attn_prefill_vs_oracle(L, rep, streams, p0):
+    """mtl_attn_prefill against the oracle's causal attention (the
+    flash-style rounding points) for every row and head, with partial query
+    blocks, several streams over separate caches and a prompt chunk that
+    starts at position p0 > 0 (rows beyond the chunk hold NaN and are never
+    read)."""
+    dev = require_cuda()
+    from moss_tts_lite_b200 import _lib, kernels
+    rng = np.random.default_rng(L + rep + streams + p0)
+    nkv, D, max_seq = 2, 128, 512
+    nh = nkv * rep
+    q = f32_to_bf16(rng.standard_normal((streams * L, nh, D)).astype(np.float32))
+    kc = f32_to_bf16(rng.standard_normal((streams, nkv, max_seq, D)).astype(np.float32))
+    vc = f32_to_bf16((rng.standard_normal((streams, nkv, max_seq, D)) * 1.5).astype(np.float32))
+    kc[:, :, p0 + L:] = 0x7FC0
+    vc[:, :, p0 + L:] = 0x7FC0
+    out = torch.empty(streams * L, nh * D, dtype=torch.bfloat16, device=dev)
+    kernels.attn_prefill(_t(q, dev, torch.bfloat16), _t(kc, dev, torch.bfloat16), _t(vc, dev, torch.bfloat16),
+                         nh, nkv, out, rows_per_stream=L, streams=streams, p0=p0,
+                         cache_stream_stride=nkv * max_seq * D)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    got = bf16_to_f32(_bits(out)).reshape(streams, L, nh, D)
+    qf = bf16_to_f32(q).astype(np.float64).reshape(streams, L, nh, D)
+    kf, vf = bf16_to_f32(kc).astype(np.float64), bf16_to_f32(vc).astype(np.float64)
+    scale = 1.0 / np.sqrt(D)
+    worst = 0.0
+    for s in range(streams):
+        for h in range(nh):
+            kv = h // rep
+            keys, vals = kf[s, kv, :p0 + L], vf[s, kv, :p0 + L]
+            want = ost.attend(qf[s, :, h], keys, vals, scale, causal=True)
+            d = np.abs(got[s, :, h] - want)
+            assert np.isfinite(got[s, :, h]).all()
+            # bf16 output rounding (2^-8 relative) plus fp32 summation order
+            assert (d <= 1e-2 + 8e-3 * np.abs(want)).all(), (s, h, float(d.max()))
+            worst = max(worst, float(d.max()))
