@@ -784,6 +784,35 @@ def run_reference_arm(args, ctx):
     print(json.dumps(line), flush=True)
 
 
+def profile_gemv_ref(launches: int = 6):
+    """Small case for ncu: the reference-format W4 linear of the decode step
+    (RTN codes + bf16 (scale, zero) of a seeded N(0, 0.02) weight, 4096 ->
+    12288, g128, batch 1, the configuration-0 shape) on cuda:0, `launches`
+    launches over 4 weight copies (107 MB, > L2)."""
+    import torch
+    from moss_tts_lite_b200 import _lib, kernels
+    from moss_tts_lite_b200.quant import W4Weight
+    dev = torch.device("cuda", 0)
+    K, N, g = 4096, 12288, 128
+    gen = torch.Generator(device=dev).manual_seed(0)
+    ws = []
+    for _ in range(4):
+        w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        q, qsz = kernels.rtn_quantize(w, g)
+        ws.append(W4Weight.from_ref(q, qsz, g))
+        del w, q, qsz
+    x = torch.randn(1, K, generator=gen, device=dev).to(torch.bfloat16)
+    out = torch.empty(1, N, dtype=torch.bfloat16, device=dev)
+    for i in range(launches):
+        ws[i % 4].linear(x, out=out)
+    torch.cuda.synchronize()
+    st = _lib.device_status()
+    print(json.dumps({"profile": "w4_gemv reference format 4096 -> 12288", "launches": launches,
+                      "bytes_per_launch": ws[0].tiles.numel() + 2 * K + 2 * N, "device_status": st}))
+    if st != 0:
+        raise SystemExit(1)
+
+
 def profile_gemv(launches: int = 6):
     """Small case for ncu: config 0 (AutoGPTQ W4 linear 4096 -> 12288, g128,
     seeded synthetic tensors) on cuda:0, `launches` launches over 4 weight
@@ -867,6 +896,36 @@ def profile_cfg4(steps: int = 2):
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_pop()
     print(json.dumps({"profile": "cfg4 batched step", "steps": steps}))
+
+
+def profile_prefill(rows: int):
+    """A prompt of `rows` rows (seeded random ids, last row AUDIO_START)
+    prefilled through FastMossTTS.prefill on the configuration-2 model: two
+    untimed calls, then one inside the NVTX range `mtl_timed` (the ncu
+    launch-list case), timed with CUDA events."""
+    import torch
+    from moss_tts_lite_b200.model import AUDIO_START_TOKEN_ID, N_VQ
+    dev = torch.device("cuda", 0)
+    fast = build_fast(dev, seed=CFG["seed"], max_seq=max(rows + 8, 256))
+    g = torch.Generator().manual_seed(3)
+    ids = torch.zeros(1, rows, N_VQ + 1, dtype=torch.long)
+    ids[0, :, 0] = torch.randint(0, 151643, (rows,), generator=g)
+    ids[0, :, 1:] = torch.randint(0, 1024, (rows, N_VQ), generator=g)
+    ids[0, -1, 0] = AUDIO_START_TOKEN_ID
+    ids = ids.to(dev)
+    for _ in range(2):
+        fast.prefill(ids)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("mtl_timed")
+    e0.record()
+    fast.prefill(ids)
+    e1.record()
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    from moss_tts_lite_b200 import _lib
+    print(json.dumps({"profile": f"prefill {rows} rows", "ms": e0.elapsed_time(e1),
+                      "device_status": _lib.device_status()}))
 
 
 def profile_attn(timed: bool = True, launches: int = 4, lengths=(136, 1024, 4096, 8191)):
@@ -980,11 +1039,13 @@ def main():
     ap.add_argument("--no-cfg3", action="store_true", help="skip the long-context sampled configuration-3 run")
     ap.add_argument("--no-cfg4", action="store_true", help="skip the 16-stream batched configuration-4 run")
     ap.add_argument("--profile-gemv", action="store_true", help="small config-0 GEMV case for ncu")
+    ap.add_argument("--profile-gemv-ref", action="store_true", help="reference-format 4096->12288 GEMV (ncu case)")
     ap.add_argument("--profile-attn", action="store_true", help="decode attention alone (config 2 heads)")
     ap.add_argument("--profile-attn-launches", action="store_true", help="4 plain attention launches (ncu case)")
     ap.add_argument("--attn-len", type=int, default=136, help="cache length of the plain attention launches")
     ap.add_argument("--profile-heads", action="store_true", help="text-head bf16 GEMV alone (ncu case)")
     ap.add_argument("--profile-cfg4", action="store_true", help="2 batched configuration-4 steps in an NVTX range")
+    ap.add_argument("--profile-prefill", type=int, default=0, help="prefill of this many prompt rows (ncu case)")
     args = ap.parse_args()
     if args.profile_heads:
         profile_heads()
@@ -992,8 +1053,14 @@ def main():
     if args.profile_cfg4:
         profile_cfg4()
         return
+    if args.profile_prefill:
+        profile_prefill(args.profile_prefill)
+        return
     if args.profile_gemv:
         profile_gemv()
+        return
+    if args.profile_gemv_ref:
+        profile_gemv_ref()
         return
     if args.profile_attn or args.profile_attn_launches:
         lengths = (args.attn_len,) + tuple(L for L in (136, 1024, 4096, 8191) if L != args.attn_len)
