@@ -784,6 +784,68 @@ def run_reference_arm(args, ctx):
     print(json.dumps(line), flush=True)
 
 
+def profile_gemv_shapes():
+    """Device time per W4 GEMV launch of each projection of the decode step
+    (q|k|v, o, gate|up, down): 36 launches of one projection over the 36
+    layers' weights in one CUDA graph (weights streaming from HBM), and the
+    fit t = fixed + bytes / rate over the four shapes."""
+    import numpy as np
+    import torch
+    dev = torch.device("cuda", 0)
+    fast = build_fast(dev, seed=CFG["seed"], max_seq=256)
+    eng, m = fast.engine, fast.m
+    res = {}
+    for name, res_epi in (("qkv", 0), ("o", 1), ("gu", 0), ("down", 1)):
+        def body():
+            for li in range(m.n_layers):
+                lyr, L = m.layers[li], eng.lins[li]
+                if name == "qkv":
+                    L["qkv"](eng.h, eng.qkv, norm_weight=lyr["input_layernorm"])
+                elif name == "o":
+                    L["o"](eng.attn, eng.h, residual=eng.h)
+                elif name == "gu":
+                    L["gu"](eng.h, eng.act, norm_weight=lyr["post_attention_layernorm"], swiglu=True)
+                else:
+                    L["down"](eng.act, eng.h, residual=eng.h)
+        t = _graph_time(body, reps=10) / m.n_layers
+        w = eng.lins[0][name].w
+        nout = w.N // 2 if name == "gu" else w.N
+        nbytes = w.tiles.numel() + 2 * w.K + 2 * nout + (2 * w.N if res_epi else 0)
+        res[name] = {"us": t * 1e6, "bytes": nbytes, "gbs": nbytes / t / 1e9}
+    x = np.array([v["bytes"] for v in res.values()], np.float64)
+    y = np.array([v["us"] for v in res.values()], np.float64)
+    b, a = np.polyfit(x, y, 1)
+    print(json.dumps({"profile": "w4 gemv per projection (36 chained launches each)", "per_shape": res,
+                      "fit_fixed_us": a, "fit_rate_tbs": 1e-6 / b if b > 0 else None}))
+
+
+def profile_chain():
+    """Device time of the persistent W4 chain (mtl_w4_chain) per launch: the
+    four-phase o -> gate|up -> down -> q|k|v chain over the 36 layers'
+    weights in one graph, and one-phase chains of each projection (weights
+    streaming from HBM), beside the one-launch-per-linear GEMV."""
+    import torch
+    from moss_tts_lite_b200 import kernels
+    from moss_tts_lite_b200.model import RMS_EPS
+    dev = torch.device("cuda", 0)
+    fast = build_fast(dev, seed=CFG["seed"], max_seq=256)
+    eng, m = fast.engine, fast.m
+    if eng.strips is None:
+        raise SystemExit("the chain is not enabled for this model")
+    bar, g, n = eng.chain_bar, eng.chain_g, m.n_layers
+    out = {}
+
+    def chains(names):
+        def body():
+            for li in range(n):
+                kernels.w4_chain([eng._phase(li, nm) for nm in names], g, bar[li], RMS_EPS)
+        return body
+    out["o,gu,down,qkv"] = _graph_time(chains(("o", "gu", "down", "qkv")), reps=10) / n * 1e6
+    for nm in ("qkv", "o", "gu", "down"):
+        out[nm] = _graph_time(chains((nm,)), reps=10) / n * 1e6
+    print(json.dumps({"profile": "w4 chain us per launch (36 launches over the layers' weights)", "us": out}))
+
+
 def profile_gemv_ref(launches: int = 6):
     """Small case for ncu: the reference-format W4 linear of the decode step
     (RTN codes + bf16 (scale, zero) of a seeded N(0, 0.02) weight, 4096 ->
@@ -1040,6 +1102,8 @@ def main():
     ap.add_argument("--no-cfg4", action="store_true", help="skip the 16-stream batched configuration-4 run")
     ap.add_argument("--profile-gemv", action="store_true", help="small config-0 GEMV case for ncu")
     ap.add_argument("--profile-gemv-ref", action="store_true", help="reference-format 4096->12288 GEMV (ncu case)")
+    ap.add_argument("--profile-gemv-shapes", action="store_true", help="per-projection GEMV times and fixed-cost fit")
+    ap.add_argument("--profile-chain", action="store_true", help="persistent W4 chain times per launch")
     ap.add_argument("--profile-attn", action="store_true", help="decode attention alone (config 2 heads)")
     ap.add_argument("--profile-attn-launches", action="store_true", help="4 plain attention launches (ncu case)")
     ap.add_argument("--attn-len", type=int, default=136, help="cache length of the plain attention launches")
@@ -1061,6 +1125,12 @@ def main():
         return
     if args.profile_gemv_ref:
         profile_gemv_ref()
+        return
+    if args.profile_gemv_shapes:
+        profile_gemv_shapes()
+        return
+    if args.profile_chain:
+        profile_chain()
         return
     if args.profile_attn or args.profile_attn_launches:
         lengths = (args.attn_len,) + tuple(L for L in (136, 1024, 4096, 8191) if L != args.attn_len)

@@ -150,6 +150,40 @@ int mtl_w4a16_linear_noalloc(const uint16_t* x, int ldx, int M, int K, int N, in
                              float norm_eps, int epilogue, const uint16_t* residual, uint16_t* y, int ldy,
                              mtl_stream_t stream);
 
+/* ---- persistent W4 chain (batch-1 decode) ------------------------------
+ * Strip layout: the [N, K] int4 weight in tiles of 16 output rows x one
+ * group (8 g + 64 bytes each, strip-major), the layout mtl_w4_chain reads.
+ * Same codes and (scale, zero) as mtl_w4_pack_ref (w = bf16((q-8)*scale +
+ * zero)); a gate|up pair for the SwiGLU epilogue is interleaved in blocks
+ * of 8 rows (rows 0-7 of a strip gate, 8-15 up, of the same 8 outputs).
+ * group_size 64/128/256, K % group_size == 0, N % 16 == 0. */
+int mtl_w4_strip_bytes(int K, int N, int group_size, size_t* bytes);
+int mtl_w4_pack_strip(const uint8_t* q, const uint16_t* qsz, int K, int N, int group_size, void* tiles,
+                      mtl_stream_t stream);
+
+typedef struct {
+  const void* tiles;         /* strip-layout weight, K x N, 16-byte aligned */
+  const uint16_t* x;         /* bf16 [K] input row, 16-byte aligned         */
+  const uint16_t* norm_w;    /* nullable: RMSNorm of x first (bf16 [K])     */
+  const uint16_t* residual;  /* MTL_EPI_RESIDUAL: bf16 [N], may alias y     */
+  uint16_t* y;               /* bf16 [N] ([N/2] with MTL_EPI_SWIGLU)        */
+  int K, N, epilogue;
+} mtl_chain_phase;
+
+/* Up to 4 dependent batch-1 W4 linears in one launch, each phase reading
+ * the previous phases' outputs: the sequence o -> gate|up -> down -> next
+ * q|k|v that the reference's decode step runs as separate
+ * torch._weight_int4pack_mm calls (moss_tts_lite/fast.py:165-171 with
+ * FastMossTTS._linear at fast.py:107-121), RMSNorm (model.py:34-40) and
+ * residual / SwiGLU epilogues as mtl_w4a16_linear applies them.  One CTA
+ * per SM; phases are separated by a grid barrier on `barrier`, a device
+ * uint32 that must be 0 before the launch and is 0 again after it (give
+ * each launch that may overlap another its own word).  Results are
+ * bitwise reproducible; they equal mtl_w4a16_linear's up to the fp32
+ * summation order.  K <= 16384 per phase. */
+int mtl_w4_chain(const mtl_chain_phase* phases, int nphases, int group_size, float norm_eps, uint32_t* barrier,
+                 mtl_stream_t stream);
+
 /* y = epilogue(x . W^T) for a prompt of M rows on the 5th-generation tensor
  * cores (tcgen05 GEMM, the prefill path).  Replaces
  * torch._weight_int4pack_mm(x, packed, g, qsz) at M = prompt length as

@@ -35,6 +35,14 @@ _c_size_t = ctypes.c_size_t
 _c_size_p = ctypes.POINTER(ctypes.c_size_t)
 _c_u32_p = ctypes.POINTER(ctypes.c_uint32)
 
+
+
+class ChainPhase(ctypes.Structure):
+    """mtl_chain_phase (include/mtl_b200.h)."""
+    _fields_ = [("tiles", _c_void_p), ("x", _c_void_p), ("norm_w", _c_void_p), ("residual", _c_void_p),
+                ("y", _c_void_p), ("K", _c_int), ("N", _c_int), ("epilogue", _c_int)]
+
+
 # name -> (restype, argtypes); every exported symbol of include/mtl_b200.h.
 SIGNATURES = {
     "mtl_last_error": (ctypes.c_char_p, []),
@@ -55,6 +63,9 @@ SIGNATURES = {
                                           _c_int, _c_void_p]),
     "mtl_w4a16_gemm": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_int, _c_void_p,
                                 _c_int, _c_void_p, _c_int, _c_void_p]),
+    "mtl_w4_strip_bytes": (_c_int, [_c_int, _c_int, _c_int, _c_size_p]),
+    "mtl_w4_pack_strip": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
+    "mtl_w4_chain": (_c_int, [ctypes.POINTER(ChainPhase), _c_int, _c_int, _c_float, _c_void_p, _c_void_p]),
     "mtl_attn_prefill": (_c_int, [_c_void_p, _c_void_p, _c_void_p, ctypes.c_longlong, _c_int, _c_int, _c_int,
                                   _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
     "mtl_embed_sum": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_void_p, _c_int, _c_void_p, _c_void_p]),
@@ -136,6 +147,13 @@ def w4_plan(M: int, K: int, N: int, g: int, fmt: int) -> tuple[int, int]:
     sb = ctypes.c_size_t(0)
     call("mtl_w4_plan", M, K, N, g, fmt, ctypes.byref(tb), ctypes.byref(sb))
     return int(tb.value), int(sb.value)
+
+
+def strip_bytes(K: int, N: int, g: int) -> int:
+    """Bytes of a strip-layout W4 weight (mtl_w4_pack_strip)."""
+    out = ctypes.c_size_t(0)
+    call("mtl_w4_strip_bytes", K, N, g, ctypes.byref(out))
+    return int(out.value)
 
 
 def attn_scratch_bytes(streams: int, n_heads: int, n_kv: int, splits: int) -> int:

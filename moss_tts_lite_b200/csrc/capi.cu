@@ -4,6 +4,7 @@
 #include "../../include/mtl_b200.h"
 #include "common.cuh"
 #include "w4_gemv.cuh"
+#include "w4_chain.cuh"
 
 #include <cstdarg>
 #include <cstdio>
@@ -400,6 +401,88 @@ int mtl_w4a16_gemm(const uint16_t* x, int ldx, int M, int K, int N, int group_si
   cudaError_t e = mtl::w4_gemm_launch(x, ldx, M, K, N, group_size, static_cast<const uint8_t*>(tiles), epilogue,
                                       residual, ldr, y, ldy, num_sms(), stream, use_pdl() ? 1 : 0);
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4a16_gemm");
+}
+
+int mtl_w4_strip_bytes(int K, int N, int group_size, size_t* bytes) {
+  if (!bytes) return fail(MTL_E_INVALID, "mtl_w4_strip_bytes: NULL output");
+  if (group_size != 64 && group_size != 128 && group_size != 256)
+    return fail(MTL_E_UNSUPPORTED, "strip layout: group_size %d (64/128/256 served)", group_size);
+  if (K <= 0 || N <= 0 || K % group_size || N % 16)
+    return fail(MTL_E_INVALID, "strip layout: K=%d (multiple of %d), N=%d (multiple of 16)", K, group_size, N);
+  *bytes = (size_t)(N / 16) * (K / group_size) * mtl::strip_tile_bytes(group_size);
+  return MTL_OK;
+}
+
+int mtl_w4_pack_strip(const uint8_t* q, const uint16_t* qsz, int K, int N, int group_size, void* tiles,
+                      mtl_stream_t stream) {
+  size_t nb = 0;
+  if (int r = mtl_w4_strip_bytes(K, N, group_size, &nb)) return r;
+  if (!q || !qsz || !tiles) return fail(MTL_E_INVALID, "mtl_w4_pack_strip: NULL pointer");
+  if (!aligned(tiles, 16) || !aligned(qsz, 2)) return fail(MTL_E_ALIGN, "tiles 16-byte, qsz 2-byte aligned");
+  cudaError_t e = mtl::w4_pack_strip(q, qsz, K, N, group_size, static_cast<uint8_t*>(tiles), stream);
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4_pack_strip");
+}
+
+int mtl_w4_chain(const mtl_chain_phase* phases, int nphases, int group_size, float norm_eps, uint32_t* barrier,
+                 mtl_stream_t stream) {
+  if (!phases || nphases < 1 || nphases > mtl::kChainMaxPhases)
+    return fail(MTL_E_INVALID, "mtl_w4_chain: %d phases (1..%d)", nphases, mtl::kChainMaxPhases);
+  if (group_size != 64 && group_size != 128 && group_size != 256)
+    return fail(MTL_E_UNSUPPORTED, "mtl_w4_chain: group_size %d (64/128/256 served)", group_size);
+  if (!barrier || !aligned(barrier, 4)) return fail(MTL_E_INVALID, "mtl_w4_chain: barrier word NULL or misaligned");
+  if (!(norm_eps > 0.f)) return fail(MTL_E_INVALID, "mtl_w4_chain: norm_eps must be > 0");
+  mtl::ChainArgs a{};
+  int Ks[mtl::kChainMaxPhases], Ns[mtl::kChainMaxPhases];
+  for (int i = 0; i < nphases; ++i) {
+    const mtl_chain_phase& P = phases[i];
+    if (!P.tiles || !P.x || !P.y) return fail(MTL_E_INVALID, "mtl_w4_chain: phase %d: NULL tiles / x / y", i);
+    if (P.K <= 0 || P.N <= 0 || P.K % group_size || P.N % 16 || P.K > mtl::kChainMaxK)
+      return fail(MTL_E_INVALID, "mtl_w4_chain: phase %d: K=%d (multiple of %d, <= %d), N=%d (multiple of 16)", i,
+                  P.K, group_size, mtl::kChainMaxK, P.N);
+    if (P.epilogue != MTL_EPI_STORE && P.epilogue != MTL_EPI_RESIDUAL && P.epilogue != MTL_EPI_SWIGLU)
+      return fail(MTL_E_INVALID, "mtl_w4_chain: phase %d: unknown epilogue %d", i, P.epilogue);
+    if (P.epilogue == MTL_EPI_RESIDUAL && !P.residual)
+      return fail(MTL_E_INVALID, "mtl_w4_chain: phase %d: residual epilogue needs residual", i);
+    if (!aligned(P.tiles, 16) || !aligned(P.x, 16) || (P.norm_w && !aligned(P.norm_w, 16)) || !aligned(P.y, 2) ||
+        (P.residual && !aligned(P.residual, 2)))
+      return fail(MTL_E_ALIGN, "mtl_w4_chain: phase %d: tiles / x / norm_w 16-byte, y / residual 2-byte aligned", i);
+    a.ph[i].tiles = static_cast<const uint8_t*>(P.tiles);
+    a.ph[i].x = P.x;
+    a.ph[i].norm_w = P.norm_w;
+    a.ph[i].residual = P.residual;
+    a.ph[i].y = P.y;
+    a.ph[i].K = P.K;
+    a.ph[i].N = P.N;
+    a.ph[i].epi = P.epilogue;
+    Ks[i] = P.K;
+    Ns[i] = P.N;
+  }
+  a.nphases = nphases;
+  a.eps = norm_eps;
+  a.barrier = barrier;
+  mtl::ChainPlan plan;
+  {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, int, int, int, int, int, int, int, int, int>, mtl::ChainPlan> cache;
+    int kk[4] = {0, 0, 0, 0}, nn[4] = {0, 0, 0, 0};
+    for (int i = 0; i < nphases; ++i) {
+      kk[i] = Ks[i];
+      nn[i] = Ns[i];
+    }
+    const int sms = num_sms();
+    auto key = std::make_tuple(nphases, group_size, sms, kk[0], kk[1], kk[2], kk[3], nn[0], nn[1], nn[2], nn[3]);
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      plan = it->second;
+    } else {
+      if (mtl::w4_chain_plan(Ks, Ns, nphases, group_size, sms, &plan) != 0)
+        return fail(MTL_E_UNSUPPORTED, "mtl_w4_chain: no plan fits these phases");
+      cache[key] = plan;
+    }
+  }
+  cudaError_t e = mtl::w4_chain_launch(a, group_size, plan, stream, use_pdl() ? 1 : 0);
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4_chain");
 }
 
 int mtl_attn_prefill(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,

@@ -6,6 +6,7 @@
 #include "step_kernels.cu"
 #include "attn_decode.cu"
 #include "w4_gemm.cu"
+#include "w4_chain.cu"
 #include "attn_prefill.cu"
 #include "sampling.cu"
 #include "capi.cu"

@@ -1,0 +1,74 @@
+// Persistent W4A16 GEMV chain (batch-1 decode): strip layout, phase
+// descriptors, planning and launch interface.
+//
+// Strip layout (MTL_FMT_STRIP): the [N, K] int4 matrix is cut into tiles of
+// 16 output rows (a "strip") x one quantisation group of K (g columns).
+// Tile (u, k) - rows [16u, 16u + 16), group k - sits at (u * K/g + k) *
+// (8 g + 64) bytes, so a strip's groups are contiguous:
+//
+//   words  : [g/64][32 lanes][4] uint32  (8 g bytes)
+//   params : [8][2] uint32 = bf16 scale | bf16 zero << 16; word (r, h) is
+//            row r + 8h, so a lane's two rows (gr, gr + 8) are adjacent
+//
+// Word (h, lane, l) holds the eight codes lane (gr = lane/4, t = lane%4)
+// feeds as the A fragment of one m16n8k16 MMA at k16-step ks = 4h + l:
+// rows r0 = gr, r1 = gr + 8 of the strip, k = 16 ks + {2t, 2t+1, 2t+8,
+// 2t+9}; slot s (bits 4s..4s+3) holds
+//   s0 = W[r0][2t]    s4 = W[r0][2t+1]     -> A register a0
+//   s1 = W[r1][2t]    s5 = W[r1][2t+1]     -> a1
+//   s2 = W[r0][2t+8]  s6 = W[r0][2t+9]     -> a2
+//   s3 = W[r1][2t+8]  s7 = W[r1][2t+9]     -> a3
+// (the slot order of the 64-column register-MMA tiles, with the four words
+// of a uint4 being four k16-steps of one strip instead of four 16-row
+// subtiles).  A gate|up pair for the SwiGLU epilogue is interleaved in
+// blocks of 8 rows: rows 0-7 of strip u are gate rows 8u..8u+7, rows 8-15
+// the up rows of the same outputs, so the MMA lane that holds a gate sum
+// also holds its up sum.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace mtl {
+
+constexpr int kChainMaxPhases = 4;
+constexpr int kChainWarps = 16;  // consumer warps per CTA (+1 producer warp)
+constexpr int kChainMaxK = kChainWarps * 32 * 32;  // x staged from registers: one 32-block per thread
+
+__host__ __device__ inline int strip_tile_bytes(int g) { return 8 * g + 64; }
+
+struct ChainPhase {
+  const uint8_t* tiles;      // strip layout, K x N
+  const uint16_t* x;         // bf16 [K] input row
+  const uint16_t* norm_w;    // nullable: RMSNorm of x before the linear (bf16 [K])
+  const uint16_t* residual;  // kEpiResidual: bf16 [N] (may alias y)
+  uint16_t* y;               // bf16 [N] (or [N/2] with SwiGLU)
+  int K, N, epi;
+};
+
+struct ChainArgs {
+  ChainPhase ph[kChainMaxPhases];
+  int nphases;
+  float eps;
+  unsigned* barrier;  // grid counter: 0 before the launch, reset to 0 by it
+  int stages, kmax, umax;
+};
+
+struct ChainPlan {
+  int G;       // CTAs (one per SM)
+  int stages;  // ring stages of kChainWarps tiles
+  int kmax;    // largest K of the phases (x staging)
+  int umax;    // most strips one CTA owns in any phase
+  size_t smem;
+};
+
+// Plan for phases with the given (K, N) and group size g (64/128/256).
+// Returns 0, or -1 (shape not served) / -2 (does not fit).
+int w4_chain_plan(const int* K, const int* N, int nphases, int g, int num_sms, ChainPlan* out);
+
+cudaError_t w4_chain_launch(const ChainArgs& a, int g, const ChainPlan& p, cudaStream_t stream, int use_pdl);
+
+cudaError_t w4_pack_strip(const uint8_t* q, const uint16_t* qsz, int K, int N, int g, uint8_t* tiles,
+                          cudaStream_t s);
+
+}  // namespace mtl

@@ -17,6 +17,7 @@ buffers, plus ``generate_fast``.  What changes is the step itself:
 """
 from __future__ import annotations
 
+import os
 import time
 from dataclasses import dataclass, field
 
@@ -27,7 +28,7 @@ from .generate import GenResult
 from .model import (AUDIO_DELAY_SLOT_TOKEN_ID, AUDIO_END_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_PAD_CODE,
                     AUDIO_START_TOKEN_ID, AUDIO_VOCAB, IM_END_TOKEN_ID, LIN_NAMES, N_VQ, PAD_TOKEN_ID,
                     RMS_EPS, HiddenState)
-from .quant import W4Weight, gemm_supported
+from .quant import StripWeight, W4Weight, gemm_supported
 
 _INT64_MAX = 9223372036854775807
 _LIN_NAMES = LIN_NAMES
@@ -153,10 +154,74 @@ class _StepEngine:
         # True while a step graph is captured: every replay follows the steps
         # that wrote pos and the cache rows before it
         self.kv_stable = False
+        self.strips: list | None = None
+
+    def chain_capable(self) -> bool:
+        """Whether every layer's four fused linears are reference-format W4
+        weights of one group size that the persistent chain kernel serves."""
+        gs = set()
+        for L in self.lins:
+            for n in ("qkv", "o", "gu", "down"):
+                lin = L[n]
+                if not isinstance(lin, _W4Lin) or lin.w.fmt != _lib.MTL_FMT_REF or lin.w.k_perm is not None:
+                    return False
+                if not StripWeight.supported(lin.w.K, lin.w.N, lin.w.group_size):
+                    return False
+                gs.add(lin.w.group_size)
+        return len(gs) == 1
+
+    def enable_chain(self) -> bool:
+        """Strip-layout copies of the layers' W4 weights (the prefill keeps
+        the register-MMA tiles) and one barrier word per chain launch; the
+        backbone then runs each layer's o -> gate|up -> down -> next q|k|v
+        as one persistent launch (mtl_w4_chain) between the attention
+        launches.  Returns False (nothing changed) when not capable."""
+        if self.strips is not None:
+            return True
+        if not self.chain_capable():
+            return False
+        self.strips = [{"qkv": L["qkv"].w.to_strip(), "o": L["o"].w.to_strip(),
+                        "gu": L["gu"].w.to_strip(swiglu_block=L["gu"].fuse_block), "down": L["down"].w.to_strip()}
+                       for L in self.lins]
+        self.chain_g = self.lins[0]["qkv"].w.group_size
+        # one word per launch, 128 bytes apart
+        self.chain_bar = torch.zeros(self.m.n_layers + 1, 32, dtype=torch.int32, device=self.m.device)
+        return True
+
+    def _phase(self, li: int, name: str) -> dict:
+        m, S = self.m, self.strips[li]
+        lyr = m.layers[li]
+        h = self.h.view(-1)
+        if name == "qkv":
+            return {"w": S["qkv"], "x": h, "y": self.qkv.view(-1), "norm_w": lyr["input_layernorm"]}
+        if name == "o":
+            return {"w": S["o"], "x": self.attn.view(-1), "y": h, "residual": h}
+        if name == "gu":
+            return {"w": S["gu"], "x": h, "y": self.act.view(-1), "norm_w": lyr["post_attention_layernorm"],
+                    "swiglu": True}
+        return {"w": S["down"], "x": self.act.view(-1), "y": h, "residual": h}
+
+    def _attn(self, li: int) -> None:
+        m = self.m
+        lyr = m.layers[li]
+        kernels.attn_decode(self.qkv, lyr["q_norm"], lyr["k_norm"], m.rope_cos, m.rope_sin,
+                            m.k_cache[li], m.v_cache[li], self.pos_dev, m.n_heads, m.n_kv_heads,
+                            self.splits, self.attn, self.attn_scratch, kv_stable=self.kv_stable)
 
     def backbone(self) -> None:
         m = self.m
         kernels.embed_sum(self.ids_row.view(1, N_VQ + 1), m.embed_tokens, self.emb_audio, self.h)
+        if self.strips is not None:
+            n, g, bar = m.n_layers, self.chain_g, self.chain_bar
+            kernels.w4_chain([self._phase(0, "qkv")], g, bar[0], RMS_EPS)
+            for li in range(n):
+                self._attn(li)
+                names = ("o", "gu", "down", "qkv") if li + 1 < n else ("o", "gu", "down")
+                phases = [self._phase(li, nm) for nm in names[:3]]
+                if li + 1 < n:
+                    phases.append(self._phase(li + 1, "qkv"))
+                kernels.w4_chain(phases, g, bar[li + 1], RMS_EPS)
+            return
         for li in range(m.n_layers):
             lyr, L = m.layers[li], self.lins[li]
             L["qkv"](self.h, self.qkv, norm_weight=lyr["input_layernorm"])
@@ -314,7 +379,8 @@ class FastMossTTS:
     """CUDA-graph decoder around a MossTTSModel (weights / cache are shared)."""
 
     def __init__(self, model, enable_gqa: bool = True, gqa_max_len: int = 640,
-                 quant: str | None = None, inner_k_tiles: int = 8, w4_group_size: int = 128):
+                 quant: str | None = None, inner_k_tiles: int = 8, w4_group_size: int = 128,
+                 chain: bool | None = None):
         self.m = model
         dev = model.device
         if dev.type != "cuda":
@@ -347,6 +413,11 @@ class FastMossTTS:
         else:
             self._lins = bf16_linears(model)
         self.engine = _StepEngine(model, self._lins, buffers=self)
+        # persistent chain launches for the W4 decode step (MTL_CHAIN=0 or
+        # chain=False keeps one launch per linear)
+        if chain is None:
+            chain = os.environ.get("MTL_CHAIN", "1") != "0"
+        self.chain = bool(chain) and self.engine.enable_chain()
         self.graphs: list | None = None
         self.capture_stream = torch.cuda.Stream(device=dev)
 

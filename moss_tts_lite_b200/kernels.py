@@ -186,3 +186,22 @@ def rtn_quantize(w: torch.Tensor, group_size: int = 128) -> tuple[torch.Tensor, 
     qsz = torch.empty(K // group_size, N, 2, dtype=torch.bfloat16, device=w.device)
     _lib.call("mtl_w4_rtn_quantize", w.data_ptr(), N, K, group_size, q.data_ptr(), qsz.data_ptr(), _s())
     return q, qsz
+
+
+def w4_chain(phases: list, group_size: int, barrier: torch.Tensor, eps: float = 1e-6) -> None:
+    """Dependent batch-1 W4 linears in one persistent launch (mtl_w4_chain).
+    ``phases``: up to 4 dicts {"w": StripWeight, "x": bf16 [K], "y": bf16
+    out, "norm_w": bf16 [K] or None, "residual": bf16 [N] or None,
+    "swiglu": bool}; phase i may read what phases < i wrote.  ``barrier``:
+    a zeroed int32 device word (zero again after the launch)."""
+    arr = (_lib.ChainPhase * len(phases))()
+    for i, ph in enumerate(phases):
+        w = ph["w"]
+        epi = _lib.MTL_EPI_STORE
+        if ph.get("swiglu"):
+            epi = _lib.MTL_EPI_SWIGLU
+        elif ph.get("residual") is not None:
+            epi = _lib.MTL_EPI_RESIDUAL
+        arr[i] = _lib.ChainPhase(w.tiles.data_ptr(), ph["x"].data_ptr(), _p(ph.get("norm_w")), _p(ph.get("residual")),
+                                 ph["y"].data_ptr(), w.K, w.N, epi)
+    _lib.call("mtl_w4_chain", arr, len(phases), group_size, ctypes.c_float(eps), barrier.data_ptr(), _s())

@@ -105,6 +105,22 @@ class W4Weight:
             qsz = z.permute(0, 2, 1, 3).reshape(qsz.shape[0], self.N, 2)
         return W4Weight.from_ref(q.contiguous(), qsz.contiguous(), self.group_size, fmt=_lib.MTL_FMT_TC)
 
+    def to_strip(self, swiglu_block: int = 0) -> "StripWeight":
+        """The same reference-format codes and (scale, zero) in the strip
+        layout of the persistent chain kernel (mtl_w4_pack_strip).
+        ``swiglu_block``: the weight is a gate|up pair interleaved in blocks
+        of that many rows; the strips interleave it in blocks of 8."""
+        if self.fmt != _lib.MTL_FMT_REF or self.k_perm is not None:
+            raise ValueError("to_strip needs reference-format tiles without a k permutation")
+        q, qsz = self.unpack_codes(), self.ref_params()
+        if swiglu_block:
+            b, KT = swiglu_block, qsz.shape[0]
+            gu = q.view(-1, 2, b, self.K).permute(1, 0, 2, 3).reshape(2, -1, self.K)          # [gate | up][I][K]
+            q = torch.stack([gu[0].reshape(-1, 8, self.K), gu[1].reshape(-1, 8, self.K)], 1).reshape(self.N, self.K)
+            z = qsz.view(KT, -1, 2, b, 2).permute(0, 2, 1, 3, 4).reshape(KT, 2, -1, 2)          # [KT][gate | up][I][2]
+            qsz = torch.stack([z[:, 0].reshape(KT, -1, 8, 2), z[:, 1].reshape(KT, -1, 8, 2)], 2).reshape(KT, self.N, 2)
+        return StripWeight.from_ref(q.contiguous(), qsz.contiguous(), self.group_size)
+
     def dequant(self, out: torch.Tensor | None = None) -> torch.Tensor:
         """Effective weights bf16 [N, K] in packed column order (k_perm order
         for act-order AutoGPTQ weights), as the operand of a many-row GEMM."""
@@ -145,6 +161,30 @@ class W4Weight:
                   _ptr(norm_weight), ctypes.c_float(norm_eps), epi, _ptr(residual), out.data_ptr(),
                   nout, self.scratch.data_ptr(), self.scratch.numel(), _stream())
         return out.reshape(*lead, nout)
+
+
+class StripWeight:
+    """A W4 weight in the strip layout (16 output rows x one group per tile)
+    read by the persistent chain kernel (mtl_w4_chain)."""
+
+    def __init__(self, tiles: torch.Tensor, K: int, N: int, group_size: int):
+        self.tiles, self.K, self.N, self.group_size = tiles, int(K), int(N), int(group_size)
+
+    @staticmethod
+    def supported(K: int, N: int, group_size: int) -> bool:
+        return group_size in (64, 128, 256) and K % group_size == 0 and N % 16 == 0 and K <= 16384
+
+    @classmethod
+    def from_ref(cls, q: torch.Tensor, qsz: torch.Tensor, group_size: int) -> "StripWeight":
+        """Codes uint8 [N, K] + qsz bf16 [K/g, N, 2] on a CUDA device."""
+        N, K = q.shape
+        if tuple(qsz.shape) != (K // group_size, N, 2):
+            raise ValueError(f"qsz shape {tuple(qsz.shape)} != {(K // group_size, N, 2)}")
+        q = q.to(torch.uint8).contiguous()
+        qsz = qsz.to(torch.bfloat16).contiguous()
+        tiles = torch.empty(_lib.strip_bytes(K, N, group_size), dtype=torch.uint8, device=q.device)
+        _lib.call("mtl_w4_pack_strip", q.data_ptr(), qsz.data_ptr(), K, N, group_size, tiles.data_ptr(), _stream())
+        return cls(tiles, K, N, group_size)
 
 
 def gemm_supported(w: "W4Weight") -> bool:
