@@ -846,6 +846,49 @@ def profile_chain():
     print(json.dumps({"profile": "w4 chain us per launch (36 launches over the layers' weights)", "us": out}))
 
 
+def profile_chain_small(layers: int = 2, launches: int = 6):
+    """A small ncu case for the persistent W4 chain: `layers` layers of
+    configuration-2-shaped strip weights (random codes, ~205 MB, > L2 with
+    two layers), `launches` four-phase chain launches cycling over them."""
+    import torch
+    from moss_tts_lite_b200 import kernels
+    from moss_tts_lite_b200.quant import StripWeight
+    dev = torch.device("cuda", 0)
+    H, I, NQ, g = CFG["hidden"], CFG["inter"], CFG["n_heads"] * 128 + 2 * CFG["n_kv"] * 128, 128
+    gen = torch.Generator(device=dev).manual_seed(0)
+
+    def strip(K, N):
+        q = torch.randint(0, 16, (N, K), device=dev, dtype=torch.uint8, generator=gen)
+        qsz = torch.empty(K // g, N, 2, device=dev, dtype=torch.bfloat16)
+        qsz[..., 0] = 0.01
+        qsz[..., 1] = -0.005
+        return StripWeight.from_ref(q, qsz, g)
+    L = [{"o": strip(H, H), "gu": strip(H, 2 * I), "down": strip(I, H), "qkv": strip(H, NQ)} for _ in range(layers)]
+    bf = torch.bfloat16
+    h = torch.randn(H, device=dev, generator=gen).to(bf)
+    attn = torch.randn(H, device=dev, generator=gen).to(bf)
+    act = torch.empty(I, device=dev, dtype=bf)
+    qkv = torch.empty(NQ, device=dev, dtype=bf)
+    nw = torch.ones(H, device=dev, dtype=bf)
+    def phases(w):
+        return [{"w": w["o"], "x": attn, "y": h, "residual": h},
+                {"w": w["gu"], "x": h, "y": act, "norm_w": nw, "swiglu": True},
+                {"w": w["down"], "x": act, "y": h, "residual": h},
+                {"w": w["qkv"], "x": h, "y": qkv, "norm_w": nw}]
+    bar = torch.zeros(launches, 32, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(launches):
+        if i == launches // 2:
+            e0.record()
+        kernels.w4_chain(phases(L[i % layers]), g, bar[i], 1e-6)
+    e1.record()
+    torch.cuda.synchronize()
+    n = launches - launches // 2
+    print(json.dumps({"profile": "w4 chain small case", "layers": layers, "launches": launches,
+                      "us_per_launch_eager": e0.elapsed_time(e1) * 1e3 / n}))
+
+
 def profile_gemv_ref(launches: int = 6):
     """Small case for ncu: the reference-format W4 linear of the decode step
     (RTN codes + bf16 (scale, zero) of a seeded N(0, 0.02) weight, 4096 ->
@@ -1104,6 +1147,7 @@ def main():
     ap.add_argument("--profile-gemv-ref", action="store_true", help="reference-format 4096->12288 GEMV (ncu case)")
     ap.add_argument("--profile-gemv-shapes", action="store_true", help="per-projection GEMV times and fixed-cost fit")
     ap.add_argument("--profile-chain", action="store_true", help="persistent W4 chain times per launch")
+    ap.add_argument("--profile-chain-small", action="store_true", help="2-layer W4 chain case (ncu)")
     ap.add_argument("--profile-attn", action="store_true", help="decode attention alone (config 2 heads)")
     ap.add_argument("--profile-attn-launches", action="store_true", help="4 plain attention launches (ncu case)")
     ap.add_argument("--attn-len", type=int, default=136, help="cache length of the plain attention launches")
@@ -1131,6 +1175,9 @@ def main():
         return
     if args.profile_chain:
         profile_chain()
+        return
+    if args.profile_chain_small:
+        profile_chain_small()
         return
     if args.profile_attn or args.profile_attn_launches:
         lengths = (args.attn_len,) + tuple(L for L in (136, 1024, 4096, 8191) if L != args.attn_len)

@@ -178,7 +178,9 @@ typedef struct {
  * residual / SwiGLU epilogues as mtl_w4a16_linear applies them.  One CTA
  * per SM; phases are separated by a grid barrier on `barrier`, a device
  * uint32 that must be 0 before the launch and is 0 again after it (give
- * each launch that may overlap another its own word).  Results are
+ * each launch that may overlap another its own word).  A phase's y must
+ * not overlap its own x (other phases' inputs and outputs may alias, as
+ * the decode step's h does).  Results are
  * bitwise reproducible; they equal mtl_w4a16_linear's up to the fp32
  * summation order.  K <= 16384 per phase. */
 int mtl_w4_chain(const mtl_chain_phase* phases, int nphases, int group_size, float norm_eps, uint32_t* barrier,

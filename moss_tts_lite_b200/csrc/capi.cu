@@ -446,6 +446,11 @@ int mtl_w4_chain(const mtl_chain_phase* phases, int nphases, int group_size, flo
     if (!aligned(P.tiles, 16) || !aligned(P.x, 16) || (P.norm_w && !aligned(P.norm_w, 16)) || !aligned(P.y, 2) ||
         (P.residual && !aligned(P.residual, 2)))
       return fail(MTL_E_ALIGN, "mtl_w4_chain: phase %d: tiles / x / norm_w 16-byte, y / residual 2-byte aligned", i);
+    // every CTA reads all of x while others write their strips of y
+    const uintptr_t yb = reinterpret_cast<uintptr_t>(P.y), xb = reinterpret_cast<uintptr_t>(P.x);
+    const size_t ybytes = (size_t)(P.epilogue == MTL_EPI_SWIGLU ? P.N / 2 : P.N) * 2;
+    if (yb < xb + (size_t)P.K * 2 && xb < yb + ybytes)
+      return fail(MTL_E_INVALID, "mtl_w4_chain: phase %d: y overlaps its own x", i);
     a.ph[i].tiles = static_cast<const uint8_t*>(P.tiles);
     a.ph[i].x = P.x;
     a.ph[i].norm_w = P.norm_w;

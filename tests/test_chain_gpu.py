@@ -71,8 +71,9 @@ def test_epilogues_norm_residual_swiglu_vs_oracle():
     h = f32_to_bf16((rng.standard_normal((1, K)) * 3).astype(np.float32))
     nw = f32_to_bf16((1 + 0.1 * rng.standard_normal(K)).astype(np.float32))
     ht = _t(h, dev, torch.bfloat16).view(-1).clone()
+    xt = ht.clone()              # a phase's y must not overlap its own x
     nwt = _t(nw, dev, torch.bfloat16)
-    _run([{"w": _strip(q, qsz, g, dev), "x": ht, "y": ht, "norm_w": nwt, "residual": ht}], g, dev)
+    _run([{"w": _strip(q, qsz, g, dev), "x": xt, "y": ht, "norm_w": nwt, "residual": ht}], g, dev)
     ref = f32_to_bf16(bf16_to_f32(h) + bf16_to_f32(ow.linear_bf16(ost.rms_norm(h, nw), Wnk.T)))
     d = np.abs(bf16_to_f32(_bits(ht)) - bf16_to_f32(ref.reshape(-1)))
     assert d.max() <= 2e-2 + 1e-2 * np.abs(bf16_to_f32(ref)).max()
@@ -193,6 +194,8 @@ def test_chain_rejects_bad_arguments():
     bad = StripWeight(w.tiles, 1024, 72, 128)                                   # N % 16 != 0
     with pytest.raises(_lib.MtlError):
         kernels.w4_chain([{"w": bad, "x": x, "y": y}], 128, bar[0])
+    with pytest.raises(_lib.MtlError):                                          # y overlaps its own x
+        kernels.w4_chain([{"w": w, "x": x, "y": x[:64]}], 128, bar[0])
     torch.cuda.synchronize()
     assert int(bar[0]) == 0 and _lib.device_status() == 0
 
