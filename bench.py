@@ -15,12 +15,14 @@ weak and the value is the whole-job steps/s.
 * ``e2e``    - the same metric through the public API ``generate_fast``
   (greedy): per step the graph replay, device-side decisions, a device->host
   read of the 33 tokens, the host FSM and a host->device copy of the next row.
-* ``roofline`` - the dominant kernel (W4 GEMV): one graph of the 144 W4
-  GEMV launches of a step (same weights, same launch order) timed with CUDA
-  events; achieved = algorithmic bytes / average launch time.
-* ``cpu_baseline`` / ``--impl reference`` - the numpy oracle (the CPU
-  restatement of the reference decoder) timed on the host cores on a bounded
-  sample of the same step, scaled to the full model.
+* ``roofline`` - the dominant kernel: the persistent W4 chain (37 launches
+  per step: o -> gate|up -> down -> next q|k|v per layer; the 144
+  one-linear GEMV launches with MTL_CHAIN=0), in one graph with the same
+  weights and launch order, timed with CUDA events; achieved = algorithmic
+  bytes / average launch time.
+* ``cpu_baseline`` / ``--impl reference`` - the reference's own decoder
+  (MossTTSModel) on the host cores (the numpy oracle when the reference
+  package is absent), on a bounded sample of the same step.
 """
 from __future__ import annotations
 
@@ -49,10 +51,10 @@ def _peaks():
         return 6650.0, "fallback"
 
 
-def _ncu_traffic():
-    """Per-launch DRAM bytes of the W4 GEMV from the committed ncu summary."""
+def _ncu_traffic(name: str = "w4_gemv_traffic.json"):
+    """DRAM traffic / algorithmic bytes of the W4 kernel from its committed ncu summary."""
     try:
-        with open(os.path.join(ROOT, "profiles", "w4_gemv_traffic.json")) as f:
+        with open(os.path.join(ROOT, "profiles", name)) as f:
             return json.load(f)
     except Exception:
         return None
@@ -214,12 +216,37 @@ def time_decode_loop(fast, steps: int, warmup: int, dist_ctx):
 
 
 def time_w4_gemvs(fast, reps: int = 5):
-    """Roofline of the dominant kernel: the 144 W4 GEMV launches of one step
-    in one graph (production order, same buffers and weights)."""
+    """Roofline of the dominant kernel, timed as the step runs it: with the
+    persistent chain (the default), its 37 launches of one step (q|k|v of
+    layer 0, then o -> gate|up -> down -> next q|k|v per layer) in one graph;
+    else the 144 W4 GEMV launches.  Production order, buffers and weights;
+    algorithmic bytes = packed weights + x / y / residual rows."""
     import torch
+    from moss_tts_lite_b200 import kernels
+    from moss_tts_lite_b200.model import RMS_EPS
     eng = fast.engine
     m = fast.m
     launches, alg = 0, 0
+    if eng.strips is not None:
+        def phase_bytes(ph):
+            w = ph["w"]
+            nout = w.N // 2 if ph.get("swiglu") else w.N
+            return w.tiles.numel() + 2 * w.K + 2 * nout + (2 * w.N if ph.get("residual") is not None else 0)
+
+        def body():
+            nonlocal launches, alg
+            launches, alg = 0, 0
+            seq = [[eng._phase(0, "qkv")]]
+            for li in range(m.n_layers):
+                ph = [eng._phase(li, nm) for nm in ("o", "gu", "down")]
+                if li + 1 < m.n_layers:
+                    ph.append(eng._phase(li + 1, "qkv"))
+                seq.append(ph)
+            for i, ph in enumerate(seq):
+                kernels.w4_chain(ph, eng.chain_g, eng.chain_bar[i], RMS_EPS)
+                alg += sum(phase_bytes(p) for p in ph)
+                launches += 1
+        return _graph_launch_time(body, reps, lambda: (alg, launches))
 
     def body():
         nonlocal launches, alg
@@ -236,6 +263,13 @@ def time_w4_gemvs(fast, reps: int = 5):
                 alg += w.tiles.numel() + 2 * w.K + 2 * nout + (2 * w.N if res else 0)
                 launches += 1
 
+    return _graph_launch_time(body, reps, lambda: (alg, launches))
+
+
+def _graph_launch_time(body, reps, totals):
+    """(bytes per launch, seconds per launch, launches) of `body` replayed as
+    one CUDA graph; `totals()` gives (algorithmic bytes, launches) of one body."""
+    import torch
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
@@ -253,9 +287,9 @@ def time_w4_gemvs(fast, reps: int = 5):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
-    per_launch_s = ms * 1e-3 / launches
-    per_launch_bytes = alg / launches
-    return per_launch_bytes, per_launch_s, launches
+    alg, launches = totals()
+    del g
+    return alg / launches, ms * 1e-3 / launches, launches
 
 
 def time_e2e(fast, prompt, steps: int, warmup: int):
@@ -1218,7 +1252,8 @@ def main():
     e2e_val = ctx.world * (-e2e_all) if e2e else None
     peak, peak_kind = _peaks()
     achieved = bytes_per_launch / s_per_launch / 1e9
-    traffic = _ncu_traffic()
+    chained = fast.engine.strips is not None
+    traffic = _ncu_traffic("w4_chain_traffic.json" if chained else "w4_gemv_traffic.json")
     single = ctx.world == 1
     cfg01 = None
     if ctx.rank == 0 and not args.no_cfg01:
@@ -1265,13 +1300,16 @@ def main():
                     "note": "next input row built on the device from the read-back decisions (no per-step h2d)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         # ncu DRAM bytes of the config-0 capture, scaled by its
+                         # ncu DRAM bytes of the committed capture, scaled by its
                          # traffic/algorithmic ratio to the average step launch
                          "traffic": (bytes_per_launch * traffic["traffic_over_algorithmic"]
                                      if traffic else None),
-                         "kernel": "w4_gemv_kernel (144 launches per step: q|k|v, o, gate|up, down x 36)",
+                         "kernel": ("w4_chain_kernel (37 launches per step: q|k|v of layer 0, then o -> gate|up "
+                                    "-> down -> next q|k|v per layer)" if chained else
+                                    "w4_gemv_kernel (144 launches per step: q|k|v, o, gate|up, down x 36)"),
                          "bytes_per_launch": bytes_per_launch, "us_per_launch": s_per_launch * 1e6},
-            "gpu_launches": steps * (1 + 5 * CFG["n_layers"] + 2 + 1),
+            "gpu_launches": steps * ((2 + 2 * CFG["n_layers"]) if chained else (1 + 5 * CFG["n_layers"])
+                                     + 2 + 1),
             "clocks": clocks,
         }
         if ref_gpu is not None:
