@@ -880,6 +880,37 @@ def profile_chain():
     print(json.dumps({"profile": "w4 chain us per launch (36 launches over the layers' weights)", "us": out}))
 
 
+def profile_chain_rows(streams: int = 16):
+    """Device time per launch of the batched persistent chain (mtl_w4_chain_rows,
+    `streams` rows) over the 36 layers' strip weights, four-phase and
+    one-phase, beside the batched attention launch at cache 256."""
+    import torch
+    from moss_tts_lite_b200 import kernels
+    from moss_tts_lite_b200.batched import BatchedFastMossTTS
+    from moss_tts_lite_b200.model import RMS_EPS
+    dev = torch.device("cuda", 0)
+    fast = build_fast(dev, seed=CFG["seed"], max_seq=512)
+    bt = BatchedFastMossTTS(fast, streams, max_seq=512, chain=True)
+    m, g, n = fast.m, fast.engine.chain_g, fast.m.n_layers
+    bt.pos.fill_(256)
+    out = {}
+
+    def chains(names):
+        def body():
+            for li in range(n):
+                kernels.w4_chain_rows([bt._phase(li, nm) for nm in names], g, bt.chain_bar[li], RMS_EPS)
+        return body
+    out["o,gu,down,qkv"] = _graph_time(chains(("o", "gu", "down", "qkv")), reps=5) / n * 1e6
+    for nm in ("qkv", "o", "gu", "down"):
+        out[nm] = _graph_time(chains((nm,)), reps=5) / n * 1e6
+
+    def attn():
+        for li in range(n):
+            bt._attn(li)
+    out["attn (cache 256)"] = _graph_time(attn, reps=5) / n * 1e6
+    print(json.dumps({"profile": f"batched chain us per launch, {streams} rows", "us": out}))
+
+
 def profile_chain_small(layers: int = 2, launches: int = 6):
     """A small ncu case for the persistent W4 chain: `layers` layers of
     configuration-2-shaped strip weights (random codes, ~205 MB, > L2 with
@@ -1067,7 +1098,7 @@ def profile_prefill(rows: int):
                       "device_status": _lib.device_status()}))
 
 
-def profile_attn(timed: bool = True, launches: int = 4, lengths=(136, 1024, 4096, 8191)):
+def profile_attn(timed: bool = True, launches: int = 4, lengths=(136, 1024, 4096, 8191), splits: int = 16):
     """Decode attention of configuration 2 alone (32 query / 8 KV heads x 128,
     KV cache [8, 8192, 128] for one layer, seeded synthetic values): per cache
     length, the device time of 50 launches chained in a CUDA graph (if
@@ -1079,7 +1110,6 @@ def profile_attn(timed: bool = True, launches: int = 4, lengths=(136, 1024, 4096
     dev = torch.device("cuda", 0)
     g = torch.Generator(device="cpu").manual_seed(0)
     nh, nkv, hd, max_seq = CFG["n_heads"], CFG["n_kv"], CFG["head_dim"], MAX_SEQ
-    splits = 16
 
     def r(*shape, s=1.0):
         return (torch.randn(*shape, generator=g) * s).to(torch.bfloat16).to(dev)
@@ -1119,8 +1149,8 @@ def profile_attn(timed: bool = True, launches: int = 4, lengths=(136, 1024, 4096
         launch()
     torch.cuda.synchronize()
     st = _lib.device_status()
-    print(json.dumps({"profile": "attn_decode cfg2", "us_per_launch_in_graph": res, "launches": launches,
-                      "device_status": st}))
+    print(json.dumps({"profile": "attn_decode cfg2", "splits": splits, "us_per_launch_in_graph": res,
+                      "launches": launches, "device_status": st}))
     if st != 0:
         raise SystemExit(1)
 
@@ -1182,9 +1212,11 @@ def main():
     ap.add_argument("--profile-gemv-shapes", action="store_true", help="per-projection GEMV times and fixed-cost fit")
     ap.add_argument("--profile-chain", action="store_true", help="persistent W4 chain times per launch")
     ap.add_argument("--profile-chain-small", action="store_true", help="2-layer W4 chain case (ncu)")
+    ap.add_argument("--profile-chain-rows", type=int, default=0, help="batched chain times for this many rows")
     ap.add_argument("--profile-attn", action="store_true", help="decode attention alone (config 2 heads)")
     ap.add_argument("--profile-attn-launches", action="store_true", help="4 plain attention launches (ncu case)")
     ap.add_argument("--attn-len", type=int, default=136, help="cache length of the plain attention launches")
+    ap.add_argument("--attn-splits", type=int, default=16, help="KV splits per head of --profile-attn")
     ap.add_argument("--profile-heads", action="store_true", help="text-head bf16 GEMV alone (ncu case)")
     ap.add_argument("--profile-cfg4", action="store_true", help="2 batched configuration-4 steps in an NVTX range")
     ap.add_argument("--profile-prefill", type=int, default=0, help="prefill of this many prompt rows (ncu case)")
@@ -1213,9 +1245,12 @@ def main():
     if args.profile_chain_small:
         profile_chain_small()
         return
+    if args.profile_chain_rows:
+        profile_chain_rows(args.profile_chain_rows)
+        return
     if args.profile_attn or args.profile_attn_launches:
         lengths = (args.attn_len,) + tuple(L for L in (136, 1024, 4096, 8191) if L != args.attn_len)
-        profile_attn(timed=args.profile_attn, lengths=lengths)
+        profile_attn(timed=args.profile_attn, lengths=lengths, splits=args.attn_splits)
         return
     ctx = _Dist()
     if ctx.world > 1 and args.gpus != ctx.world:

@@ -186,6 +186,27 @@ typedef struct {
 int mtl_w4_chain(const mtl_chain_phase* phases, int nphases, int group_size, float norm_eps, uint32_t* barrier,
                  mtl_stream_t stream);
 
+typedef struct {
+  const void* tiles;         /* strip-layout weight, K x N, 16-byte aligned      */
+  const uint16_t* x;         /* bf16 [M, ldx], 16-byte aligned, ldx % 8 == 0     */
+  const uint16_t* norm_w;    /* nullable: RMSNorm of each row first (K <= 4096)  */
+  const uint16_t* residual;  /* MTL_EPI_RESIDUAL: bf16 [M, ldr], may alias y     */
+  uint16_t* y;               /* bf16 [M, ldy] ([M, N/2 columns] with SwiGLU)     */
+  int ldx, ldr, ldy;
+  int K, N, epilogue;
+} mtl_chain_phase_rows;
+
+/* mtl_w4_chain for M = 2..16 activation rows (the streams of a batched
+ * decode step: the reference runs each stream's linears separately,
+ * moss_tts_lite/fast.py:165-171).  The rows share one pass over the strip
+ * weights as the N dimension of the MMAs; x is staged 4096 columns at a
+ * time.  Each output is the fp32 MMA sums of the CTA's warps added as
+ * 64-bit fixed-point integers (value x 2^32): bitwise reproducible, exact
+ * in the additions, for outputs below 2^31 in magnitude.  Same phase rules
+ * and barrier word as mtl_w4_chain. */
+int mtl_w4_chain_rows(const mtl_chain_phase_rows* phases, int nphases, int M, int group_size, float norm_eps,
+                      uint32_t* barrier, mtl_stream_t stream);
+
 /* y = epilogue(x . W^T) for a prompt of M rows on the 5th-generation tensor
  * cores (tcgen05 GEMM, the prefill path).  Replaces
  * torch._weight_int4pack_mm(x, packed, g, qsz) at M = prompt length as

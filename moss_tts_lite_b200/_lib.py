@@ -43,6 +43,13 @@ class ChainPhase(ctypes.Structure):
                 ("y", _c_void_p), ("K", _c_int), ("N", _c_int), ("epilogue", _c_int)]
 
 
+class ChainPhaseRows(ctypes.Structure):
+    """mtl_chain_phase_rows (include/mtl_b200.h)."""
+    _fields_ = [("tiles", _c_void_p), ("x", _c_void_p), ("norm_w", _c_void_p), ("residual", _c_void_p),
+                ("y", _c_void_p), ("ldx", _c_int), ("ldr", _c_int), ("ldy", _c_int), ("K", _c_int), ("N", _c_int),
+                ("epilogue", _c_int)]
+
+
 # name -> (restype, argtypes); every exported symbol of include/mtl_b200.h.
 SIGNATURES = {
     "mtl_last_error": (ctypes.c_char_p, []),
@@ -66,6 +73,8 @@ SIGNATURES = {
     "mtl_w4_strip_bytes": (_c_int, [_c_int, _c_int, _c_int, _c_size_p]),
     "mtl_w4_pack_strip": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
     "mtl_w4_chain": (_c_int, [ctypes.POINTER(ChainPhase), _c_int, _c_int, _c_float, _c_void_p, _c_void_p]),
+    "mtl_w4_chain_rows": (_c_int, [ctypes.POINTER(ChainPhaseRows), _c_int, _c_int, _c_int, _c_float, _c_void_p,
+                                   _c_void_p]),
     "mtl_attn_prefill": (_c_int, [_c_void_p, _c_void_p, _c_void_p, ctypes.c_longlong, _c_int, _c_int, _c_int,
                                   _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
     "mtl_embed_sum": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_void_p, _c_int, _c_void_p, _c_void_p]),

@@ -8,7 +8,10 @@ other.  Here one decode step advances all B streams:
   ``tc=True`` (the default from 2 streams) in tensor-core tiles, the B rows
   being the N dimension of the tcgen05 MMAs (up to 16 rows per launch);
   with ``tc=False`` in the register-MMA tiles of the batch-1 engine
-  (launches of up to 8 rows, the mma.sync N dimension);
+  (launches of up to 8 rows, the mma.sync N dimension); with ``chain=True``
+  (up to 16 streams, the batch-1 engine running the persistent chain) each
+  layer's o -> gate|up -> down -> next q|k|v is one persistent launch over
+  the batch-1 engine's strip weights (``mtl_w4_chain_rows``);
 * attention runs the B streams in one launch, each over its own KV cache
   (``mtl_attn_decode`` with ``streams = B`` and a per-stream cache stride);
 * the final norm, the two-way text head and the 32 audio heads run on the
@@ -17,7 +20,8 @@ other.  Here one decode step advances all B streams:
   device, so a captured step graph replays with no host round trip.
 
 Each stream's prompt is prefilled into its own cache slice with the
-prefill of the batch-1 engine.  With ``tc=False`` stream s's results equal a
+prefill of the batch-1 engine.  With ``tc=False, chain=False`` (and a batch-1
+engine without the chain) stream s's results equal a
 batch-1 decode of the same stream bit for bit (same kernels, same split-K
 plan) while the caches hold up to 256 positions (one attention split per
 head either way; past that the batched step splits each head's cache into
@@ -38,7 +42,8 @@ _HEAD_ROWS = 4  # rows per bf16 head launch (mtl_bf16_linear)
 class BatchedFastMossTTS:
     """``streams`` decode streams over the weights of a FastMossTTS (shared)."""
 
-    def __init__(self, fast, streams: int, max_seq: int | None = None, tc: bool | None = None):
+    def __init__(self, fast, streams: int, max_seq: int | None = None, tc: bool | None = None,
+                 chain: bool | None = None):
         m = fast.m
         if streams < 1:
             raise ValueError("streams must be >= 1")
@@ -52,11 +57,22 @@ class BatchedFastMossTTS:
         H, D = m.hidden_size, m.head_dim
         eng = fast.engine
         self.lins = eng.lins
+        # per-linear launches (tensor-core tiles by default from 2 streams,
+        # register-MMA tiles with tc=False), or with chain=True the
+        # persistent chain over the batch-1 engine's strip weights
+        if chain is None:
+            chain = False
+        self.chain = bool(chain) and eng.strips is not None and streams <= 16
+        if chain and not self.chain:
+            raise ValueError("the chain needs the batch-1 engine's strip weights (FastMossTTS(chain=True)) and "
+                             "at most 16 streams")
         if tc is None:
-            tc = streams >= 2
-        self.tc = bool(tc) and self._tc_capable(eng.lins)
+            tc = streams >= 2 and not self.chain
+        self.tc = bool(tc) and not self.chain and self._tc_capable(eng.lins)
         if self.tc:
             self.lins = self._tc_lins(eng.lins)
+        if self.chain:
+            self.chain_bar = torch.zeros(m.n_layers + 1, 32, dtype=torch.int32, device=m.device)
         self.emb_audio = eng.emb_audio
         self.head_audio2d = eng.head_audio2d
         B = streams
@@ -146,10 +162,41 @@ class BatchedFastMossTTS:
         self.pos[s].fill_(pos)
 
     # ------------------------------------------------------------------- step
+    def _phase(self, li: int, name: str) -> dict:
+        lyr, S = self.m.layers[li], self.fast.engine.strips[li]
+        if name == "qkv":
+            return {"w": S["qkv"], "x": self.h, "y": self.qkv, "norm_w": lyr["input_layernorm"]}
+        if name == "o":
+            return {"w": S["o"], "x": self.attn, "y": self.h, "residual": self.h}
+        if name == "gu":
+            return {"w": S["gu"], "x": self.h, "y": self.act, "norm_w": lyr["post_attention_layernorm"],
+                    "swiglu": True}
+        return {"w": S["down"], "x": self.act, "y": self.h, "residual": self.h}
+
+    def _attn(self, li: int) -> None:
+        m, B = self.m, self.B
+        lyr = m.layers[li]
+        stride = m.n_kv_heads * self.max_seq * m.head_dim
+        kernels.attn_decode(self.qkv, lyr["q_norm"], lyr["k_norm"], m.rope_cos, m.rope_sin,
+                            self.k_cache[li], self.v_cache[li], self.pos, m.n_heads, m.n_kv_heads,
+                            self.splits, self.attn, self.attn_scratch, streams=B, cache_stream_stride=stride,
+                            kv_stable=self.kv_stable)
+
     def _step(self) -> None:
         m, B = self.m, self.B
         kernels.embed_sum(self.ids, m.embed_tokens, self.emb_audio, self.h)
         stride = m.n_kv_heads * self.max_seq * m.head_dim
+        if self.chain:
+            g, bar, n = self.fast.engine.chain_g, self.chain_bar, m.n_layers
+            kernels.w4_chain_rows([self._phase(0, "qkv")], g, bar[0], RMS_EPS)
+            for li in range(n):
+                self._attn(li)
+                phases = [self._phase(li, nm) for nm in ("o", "gu", "down")]
+                if li + 1 < n:
+                    phases.append(self._phase(li + 1, "qkv"))
+                kernels.w4_chain_rows(phases, g, bar[li + 1], RMS_EPS)
+            self._heads()
+            return
         for li in range(m.n_layers):
             lyr, L = m.layers[li], self.lins[li]
             L["qkv"](self.h, self.qkv, norm_weight=lyr["input_layernorm"])
@@ -160,6 +207,10 @@ class BatchedFastMossTTS:
             L["o"](self.attn, self.h, residual=self.h)
             L["gu"](self.h, self.act, norm_weight=lyr["post_attention_layernorm"], swiglu=True)
             L["down"](self.act, self.h, residual=self.h)
+        self._heads()
+
+    def _heads(self) -> None:
+        m, B = self.m, self.B
         la2 = self.la.view(B, N_VQ * AUDIO_VOCAB)
         for r0 in range(0, B, _HEAD_ROWS):
             r1 = min(B, r0 + _HEAD_ROWS)

@@ -490,6 +490,65 @@ int mtl_w4_chain(const mtl_chain_phase* phases, int nphases, int group_size, flo
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4_chain");
 }
 
+int mtl_w4_chain_rows(const mtl_chain_phase_rows* phases, int nphases, int M, int group_size, float norm_eps,
+                      uint32_t* barrier, mtl_stream_t stream) {
+  if (!phases || nphases < 1 || nphases > mtl::kChainMaxPhases)
+    return fail(MTL_E_INVALID, "mtl_w4_chain_rows: %d phases (1..%d)", nphases, mtl::kChainMaxPhases);
+  if (M < 1 || M > 16) return fail(MTL_E_INVALID, "mtl_w4_chain_rows: M=%d (1..16)", M);
+  if (group_size != 64 && group_size != 128 && group_size != 256)
+    return fail(MTL_E_UNSUPPORTED, "mtl_w4_chain_rows: group_size %d (64/128/256 served)", group_size);
+  if (!barrier || !aligned(barrier, 4)) return fail(MTL_E_INVALID, "mtl_w4_chain_rows: barrier word NULL or misaligned");
+  if (!(norm_eps > 0.f)) return fail(MTL_E_INVALID, "mtl_w4_chain_rows: norm_eps must be > 0");
+  mtl::ChainBArgs a{};
+  int Ks[mtl::kChainMaxPhases], Ns[mtl::kChainMaxPhases], norm[mtl::kChainMaxPhases];
+  for (int i = 0; i < nphases; ++i) {
+    const mtl_chain_phase_rows& P = phases[i];
+    if (!P.tiles || !P.x || !P.y) return fail(MTL_E_INVALID, "mtl_w4_chain_rows: phase %d: NULL tiles / x / y", i);
+    if (P.K <= 0 || P.N <= 0 || P.K % group_size || P.N % 16)
+      return fail(MTL_E_INVALID, "mtl_w4_chain_rows: phase %d: K=%d (multiple of %d), N=%d (multiple of 16)", i,
+                  P.K, group_size, P.N);
+    if (P.norm_w && P.K > 4096)
+      return fail(MTL_E_UNSUPPORTED, "mtl_w4_chain_rows: phase %d: RMSNorm with K=%d > 4096", i, P.K);
+    if (P.epilogue != MTL_EPI_STORE && P.epilogue != MTL_EPI_RESIDUAL && P.epilogue != MTL_EPI_SWIGLU)
+      return fail(MTL_E_INVALID, "mtl_w4_chain_rows: phase %d: unknown epilogue %d", i, P.epilogue);
+    const int nout = P.epilogue == MTL_EPI_SWIGLU ? P.N / 2 : P.N;
+    if (P.ldx < P.K || P.ldx % 8 || P.ldy < nout || (P.epilogue == MTL_EPI_RESIDUAL && (!P.residual || P.ldr < P.N)))
+      return fail(MTL_E_INVALID, "mtl_w4_chain_rows: phase %d: ldx=%d ldy=%d ldr=%d", i, P.ldx, P.ldy, P.ldr);
+    if (!aligned(P.tiles, 16) || !aligned(P.x, 16) || (P.norm_w && !aligned(P.norm_w, 16)) || !aligned(P.y, 2) ||
+        (P.residual && !aligned(P.residual, 2)))
+      return fail(MTL_E_ALIGN, "mtl_w4_chain_rows: phase %d: tiles / x / norm_w 16-byte, y / residual 2-byte", i);
+    // every CTA reads all of x while others write their strips of y
+    const uintptr_t yb = reinterpret_cast<uintptr_t>(P.y), xb = reinterpret_cast<uintptr_t>(P.x);
+    const size_t xbytes = ((size_t)(M - 1) * P.ldx + P.K) * 2, ybytes = ((size_t)(M - 1) * P.ldy + nout) * 2;
+    if (yb < xb + xbytes && xb < yb + ybytes)
+      return fail(MTL_E_INVALID, "mtl_w4_chain_rows: phase %d: y overlaps its own x", i);
+    mtl::ChainBPhase& Q = a.ph[i];
+    Q.tiles = static_cast<const uint8_t*>(P.tiles);
+    Q.x = P.x;
+    Q.norm_w = P.norm_w;
+    Q.residual = P.residual;
+    Q.y = P.y;
+    Q.ldx = P.ldx;
+    Q.ldr = P.ldr;
+    Q.ldy = P.ldy;
+    Q.K = P.K;
+    Q.N = P.N;
+    Q.epi = P.epilogue;
+    Ks[i] = P.K;
+    Ns[i] = P.N;
+    norm[i] = P.norm_w != nullptr;
+  }
+  a.nphases = nphases;
+  a.M = M;
+  a.eps = norm_eps;
+  a.barrier = barrier;
+  mtl::ChainPlan plan;
+  if (mtl::w4_chainb_plan(Ks, Ns, norm, nphases, M, group_size, num_sms(), &plan) != 0)
+    return fail(MTL_E_UNSUPPORTED, "mtl_w4_chain_rows: no plan fits these phases");
+  cudaError_t e = mtl::w4_chainb_launch(a, group_size, plan, stream, use_pdl() ? 1 : 0);
+  return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4_chain_rows");
+}
+
 int mtl_attn_prefill(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                      long long cache_stream_stride, int max_seq, int n_heads, int n_kv, int head_dim,
                      int rows_per_stream, int streams, int p0, uint16_t* out, mtl_stream_t stream) {

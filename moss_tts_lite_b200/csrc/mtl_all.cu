@@ -7,6 +7,7 @@
 #include "attn_decode.cu"
 #include "w4_gemm.cu"
 #include "w4_chain.cu"
+#include "w4_chainb.cu"
 #include "attn_prefill.cu"
 #include "sampling.cu"
 #include "capi.cu"

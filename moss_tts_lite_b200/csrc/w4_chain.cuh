@@ -68,6 +68,29 @@ int w4_chain_plan(const int* K, const int* N, int nphases, int g, int num_sms, C
 
 cudaError_t w4_chain_launch(const ChainArgs& a, int g, const ChainPlan& p, cudaStream_t stream, int use_pdl);
 
+// Batched chain (w4_chainb.cu): M = 2..16 activation rows per phase.
+struct ChainBPhase {
+  const uint8_t* tiles;      // strip layout, K x N
+  const uint16_t* x;         // bf16 [M, ldx]
+  const uint16_t* norm_w;    // nullable: RMSNorm of each row first (K <= 4096)
+  const uint16_t* residual;  // kEpiResidual: bf16 [M, ldr] (may alias y)
+  uint16_t* y;               // bf16 [M, ldy]
+  int ldx, ldr, ldy;
+  int K, N, epi;
+};
+
+struct ChainBArgs {
+  ChainBPhase ph[kChainMaxPhases];
+  int nphases, M;
+  float eps;
+  unsigned* barrier;  // grid counter: 0 before the launch, reset to 0 by it
+  int stages, kslice, umax;
+};
+
+int w4_chainb_plan(const int* K, const int* N, const int* norm, int nphases, int M, int g, int num_sms,
+                   ChainPlan* out);
+cudaError_t w4_chainb_launch(const ChainBArgs& a, int g, const ChainPlan& p, cudaStream_t stream, int use_pdl);
+
 cudaError_t w4_pack_strip(const uint8_t* q, const uint16_t* qsz, int K, int N, int g, uint8_t* tiles,
                           cudaStream_t s);
 

@@ -1,0 +1,474 @@
+// Persistent W4A16 GEMV chain for the batched multi-stream decode step
+// (2..16 activation rows: the streams of BatchedFastMossTTS), sm_100a.
+//
+// The batch-1 chain (w4_chain.cu) with the rows of the batch as the N
+// dimension of the m16n8k16 MMAs (one or two 8-row n-tiles): the same strip
+// weights, the same one-CTA-per-SM grid with a grid barrier between phases
+// (o -> gate|up -> down -> next q|k|v, as the reference's decode step calls
+// torch._weight_int4pack_mm once per stream, moss_tts_lite/fast.py:165-171),
+// the same bf16 operand bf16((q - 8) s + z).  What changes:
+//
+//  * x is staged per K-slice of up to 4096 columns (16 rows x 4096 bf16 do
+//    not leave room for more): the rows land by bulk copies, are normalised
+//    and permuted into MMA-B order in place; the CTA walks its pieces slice
+//    by slice, strip by strip within a slice, and re-stages x between
+//    slices (RMSNorm phases have K <= 4096, one slice);
+//  * each warp's fp32 MMA sums of a strip are added into the CTA's strip
+//    accumulators as 64-bit fixed-point integers (value x 2^32) with shared
+//    memory atomics: integer addition is exact and order-free, so results
+//    are bitwise reproducible without a per-warp partial buffer (which would
+//    need 16 KB per strip at 16 rows).  Outputs must stay below 2^31 in
+//    magnitude (float -> integer conversion saturates; NaN becomes 0);
+//  * the epilogue (store / residual / SwiGLU) runs per batch row.
+#include "w4_chain.cuh"
+
+namespace mtl {
+
+namespace {
+
+constexpr int kCbSlice = 4096;                    // max x columns staged at once
+constexpr int kCbPieces = kChainWarps;            // pieces per ring stage: one per consumer warp
+constexpr float kCbFix = 4294967296.0f;           // 2^32
+constexpr int kCbMiscWords = 64;                  // [0] bail, [8, 8 + kCW) warp sums of squares
+
+struct CbLayout {
+  size_t bar, ring, xs, acc, misc, total;
+};
+
+// x row stride in bytes: a slice of bf16 plus 64 bytes, so that the 8 rows
+// one MMA fragment load touches fall in different banks
+__host__ __device__ inline int cb_xstride(int kslice) { return kslice * 2 + 64; }
+
+__host__ __device__ inline CbLayout cb_layout(int stages, int tile_bytes, int kslice, int rows, int umax) {
+  CbLayout L;
+  size_t o = 0;
+  L.bar = o;
+  o += round_up((size_t)(2 * stages + 1) * 8, 128);
+  L.ring = o;
+  o += (size_t)stages * kCbPieces * tile_bytes;
+  o = round_up(o, 128);
+  L.xs = o;
+  o += (size_t)rows * cb_xstride(kslice);
+  o = round_up(o, 16);
+  L.acc = o;
+  o += (size_t)umax * 16 * rows * 8;
+  L.misc = o;
+  o += kCbMiscWords * 4;
+  L.total = round_up(o, 128);
+  return L;
+}
+
+// Pieces of a phase in the CTA's order: slice sl, strip u in [u0, u1),
+// groups of the slice; a "run" is one (slice, strip) pair, contiguous in
+// memory (strip-major tiles).
+struct CbRun {
+  int KT, gps, nsl, nu;  // groups, groups per slice, slices, strips
+};
+
+template <int GS, int NT>
+__global__ void __launch_bounds__((kChainWarps + 1) * 32, 1) w4_chainb_kernel(const ChainBArgs a) {
+  extern __shared__ __align__(128) uint8_t cb_sm[];
+  constexpr int kCW = kChainWarps;
+  constexpr int kCThr = kCW * 32;
+  constexpr int TB = 8 * GS + 64;
+  constexpr uint32_t kStageBytes = (uint32_t)kCbPieces * TB;
+  constexpr int MR = 8 * NT;  // staged rows (batch rows padded to the n-tiles)
+  const int S = a.stages, M = a.M, KSL = a.kslice;
+  const int XS = cb_xstride(KSL);
+  const CbLayout L = cb_layout(S, TB, KSL, MR, a.umax);
+  uint64_t* full = reinterpret_cast<uint64_t*>(cb_sm + L.bar);
+  uint64_t* empty = full + S;
+  uint64_t* xbar = empty + S;  // x rows of a slice landed
+  uint8_t* ring = cb_sm + L.ring;
+  uint8_t* xs = cb_sm + L.xs;
+  unsigned long long* acc_s = reinterpret_cast<unsigned long long*>(cb_sm + L.acc);
+  float* misc = reinterpret_cast<float*>(cb_sm + L.misc);
+  int* imisc = reinterpret_cast<int*>(misc);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x, G = gridDim.x;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kCW);
+    }
+    mbar_init(xbar, 1);
+    fence_mbar_init();
+    imisc[0] = 0;
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  auto runs = [&](const ChainBPhase& P, int& u0, int& u1) {
+    CbRun r;
+    r.KT = P.K / GS;
+    r.gps = KSL / GS;
+    r.nsl = (r.KT + r.gps - 1) / r.gps;
+    strip_range(P.N / 16, c, G, u0, u1);
+    r.nu = u1 - u0;
+    return r;
+  };
+
+  if (warp == kCW) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int st = 0;
+      bool ok = true;
+      for (int ph = 0; ph < a.nphases && ok; ++ph) {
+        const ChainBPhase& P = a.ph[ph];
+        int u0, u1;
+        const CbRun r = runs(P, u0, u1);
+        for (int sl = 0; sl < r.nsl && ok; ++sl) {
+          const int g0 = sl * r.gps, g1 = min(r.KT, g0 + r.gps);
+          for (int u = u0; u < u1 && ok; ++u) {
+            const uint8_t* src = P.tiles + ((size_t)u * r.KT + g0) * TB;
+            for (int s0 = 0; s0 < g1 - g0; s0 += kCbPieces) {
+              const int slot = st % S;
+              if (st >= S && !mbar_wait(&empty[slot], ((st / S) - 1) & 1)) {
+                ok = false;
+                break;
+              }
+              const uint32_t bytes = (uint32_t)min(kCbPieces, g1 - g0 - s0) * TB;
+              mbar_arrive_expect_tx(&full[slot], bytes);
+              bulk_g2s(ring + (size_t)slot * kStageBytes, src + (size_t)s0 * TB, bytes, &full[slot]);
+              ++st;
+            }
+          }
+        }
+      }
+      const uint64_t deadline = globaltimer_ns() + kWaitNs;
+      for (int s = 0; s < S && s < st; ++s) {
+        const int last = s + ((st - 1 - s) / S) * S;
+        if (!mbar_wait_until(&full[s], (last / S) & 1, deadline)) {
+          flag_error(kDevCopyDrainTimeout);
+          break;
+        }
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int tid = threadIdx.x;
+  const int gr = lane >> 2, tq = lane & 3;
+  int slot = 0;
+  uint32_t par = 0;
+  uint32_t xpar = 0;  // phase parity of xbar
+  int arrived = 0;
+  bool bail = false;
+  // staging roles: thread t stages rows t / tpr (tpr threads per row), its
+  // 32-column blocks t % tpr, t % tpr + tpr, ... of the slice
+  constexpr int kTpr = kCThr / MR;
+  const int srow = tid / kTpr, scol = tid % kTpr;
+  const int swarps = kTpr / 32;  // warps per staged row (1 or 2)
+
+  for (int ph = 0; ph < a.nphases && !bail; ++ph) {
+    const ChainBPhase& P = a.ph[ph];
+    int u0, u1;
+    const CbRun r = runs(P, u0, u1);
+    for (int i = tid; i < r.nu * 16 * MR; i += kCThr) acc_s[i] = 0ull;
+
+    if (ph == 0) {
+      pdl_wait();
+    } else {
+      if (tid == 0 && !grid_wait(a.barrier, (unsigned)G * ph)) {
+        flag_error(kDevWaitTimeout);
+        imisc[0] = 1;
+      }
+      chain_sync();
+      if (imisc[0]) {
+        bail = true;
+        break;
+      }
+    }
+
+    float acc[NT][4], acc2[NT][4];
+    int cur = -1;  // local strip of the registers' sums
+    auto flush = [&]() {
+      if (cur >= 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int row = gr + ((e & 2) ? 8 : 0), m = 8 * nt + 2 * tq + (e & 1);
+            if (m < M) {
+              const long long q = __float2ll_rn((acc[nt][e] + acc2[nt][e]) * kCbFix);
+              atomicAdd(acc_s + ((size_t)cur * 16 + row) * MR + m, (unsigned long long)q);
+            }
+          }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[nt][e] = acc2[nt][e] = 0.f;
+    };
+
+    for (int sl = 0; sl < r.nsl && !bail; ++sl) {
+      const int g0 = sl * r.gps, g1 = min(r.KT, g0 + r.gps);
+      const int kc = (g1 - g0) * GS;  // columns of this slice
+      // ---- stage x[:, slice] (RMSNorm phases have a single slice): the M
+      //      rows land in shared memory by bulk copies (one round trip), are
+      //      normalised there and permuted in place into MMA-B order
+      if (sl > 0) chain_sync();  // every warp is done with the previous slice
+      const int nblk = kc / 32;
+      if (tid == 0) {
+        // generic-proxy accesses of xs (the previous slice) and the phase
+        // inputs written through the grid barrier before the async copies
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        mbar_arrive_expect_tx(xbar, (uint32_t)(M * kc * 2));
+        for (int mm = 0; mm < M; ++mm)
+          bulk_g2s(xs + (size_t)mm * XS, P.x + (size_t)mm * P.ldx + g0 * GS, (uint32_t)(kc * 2), xbar);
+      }
+      if (!mbar_wait(xbar, xpar)) imisc[0] = 1;
+      xpar ^= 1u;
+      uint8_t* xrow = xs + (size_t)srow * XS;
+      float rinv = 1.f;
+      if (P.norm_w) {
+        float ss = 0.f;
+        if (srow < M) {
+          for (int b = scol; b < nblk; b += kTpr) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint4 v = reinterpret_cast<const uint4*>(xrow + 64 * b)[e];
+              const uint32_t u4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float lo = __uint_as_float(u4[q] << 16), hi = __uint_as_float(u4[q] & 0xFFFF0000u);
+                ss = fmaf(lo, lo, ss);
+                ss = fmaf(hi, hi, ss);
+              }
+            }
+          }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) misc[8 + warp] = ss;
+        chain_sync();
+        float t = 0.f;
+        for (int w = 0; w < swarps; ++w) t += misc[8 + srow * swarps + w];
+        rinv = rsqrtf(t / (float)P.K + a.eps);
+      }
+      for (int b = scol; b < nblk; b += kTpr) {
+        uint32_t u[16];
+        uint4* blk = reinterpret_cast<uint4*>(xrow + 64 * b);
+        if (srow < M) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint4 v = blk[e];
+            u[4 * e] = v.x;
+            u[4 * e + 1] = v.y;
+            u[4 * e + 2] = v.z;
+            u[4 * e + 3] = v.w;
+          }
+          if (P.norm_w) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint4 nv = __ldg(reinterpret_cast<const uint4*>(P.norm_w + g0 * GS + 32 * b) + e);
+              const uint32_t w4[4] = {nv.x, nv.y, nv.z, nv.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const uint32_t x2 = u[4 * e + q];
+                // model.py:34-40: bf16(h * rsqrt(var + eps)), then bf16(weight * that)
+                const float v0 = round_bf16(__uint_as_float(w4[q] << 16) * round_bf16(__uint_as_float(x2 << 16) * rinv));
+                const float v1 = round_bf16(__uint_as_float(w4[q] & 0xFFFF0000u) *
+                                            round_bf16(__uint_as_float(x2 & 0xFFFF0000u) * rinv));
+                u[4 * e + q] = (__float_as_uint(v0) >> 16) | (__float_as_uint(v1) & 0xFFFF0000u);
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 16; ++q) u[q] = 0u;  // padding rows of the n-tile
+        }
+        // MMA-B order, two k16-steps per 16-byte lane load (as w4_chain.cu);
+        // this thread alone owns the block, so the permutation is in place
+#pragma unroll
+        for (int t = 0; t < 4; ++t) blk[t] = make_uint4(u[t], u[t + 4], u[t + 8], u[t + 12]);
+      }
+      chain_sync();
+      if (imisc[0]) {
+        bail = true;
+        break;
+      }
+
+      // ---- this slice's pieces: strip by strip, one piece per warp per stage
+      for (int ul = 0; ul < r.nu; ++ul) {
+        for (int s0 = 0; s0 < g1 - g0; s0 += kCbPieces) {
+          const bool landed = mbar_wait(&full[slot], par);
+          if (__any_sync(0xffffffffu, !landed)) {
+            bail = true;
+            break;
+          }
+          const int k = g0 + s0 + warp;  // this warp's group
+          if (k < g1) {
+            if (ul != cur) {
+              flush();
+              cur = ul;
+            }
+            const uint8_t* tile = ring + (size_t)slot * kStageBytes + (size_t)warp * TB;
+            const uint2 pw = *reinterpret_cast<const uint2*>(tile + 8 * GS + 8 * gr);
+            const uint32_t sc0 = __byte_perm(pw.x, 0u, 0x1010), zr0 = __byte_perm(pw.x, 0u, 0x3232);
+            const uint32_t sc1 = __byte_perm(pw.y, 0u, 0x1010), zr1 = __byte_perm(pw.y, 0u, 0x3232);
+            const uint4* wt = reinterpret_cast<const uint4*>(tile);
+            const size_t xo = (size_t)(k - g0) * GS * 2 + 16 * tq;
+#pragma unroll
+            for (int h = 0; h < GS / 64; ++h) {
+              const uint4 wv = wt[h * 32 + lane];
+              const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
+              uint32_t bx[NT][8];
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) {
+                const uint8_t* xb = xs + (size_t)(gr + 8 * nt) * XS + xo + 128 * h;
+                const uint4 xa = *reinterpret_cast<const uint4*>(xb);
+                const uint4 xc = *reinterpret_cast<const uint4*>(xb + 64);
+                bx[nt][0] = xa.x;
+                bx[nt][1] = xa.y;
+                bx[nt][2] = xa.z;
+                bx[nt][3] = xa.w;
+                bx[nt][4] = xc.x;
+                bx[nt][5] = xc.y;
+                bx[nt][6] = xc.z;
+                bx[nt][7] = xc.w;
+              }
+#pragma unroll
+              for (int l = 0; l < 4; ++l) {
+                const uint32_t w = wr[l];
+                const uint32_t a0 = w4_ref_pair(lop3_and_or(w, 0x000F000Fu, 0x43004300u), sc0, zr0);
+                const uint32_t a1 = w4_ref_pair(lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u), sc1, zr1);
+                const uint32_t a2 = w4_ref_pair(lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u), sc0, zr0);
+                const uint32_t a3 = w4_ref_pair(lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u), sc1, zr1);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                  if (l & 1)
+                    mma_bf16(acc2[nt], a0, a1, a2, a3, bx[nt][2 * l], bx[nt][2 * l + 1]);
+                  else
+                    mma_bf16(acc[nt], a0, a1, a2, a3, bx[nt][2 * l], bx[nt][2 * l + 1]);
+                }
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[slot]);
+          if (++slot == S) {
+            slot = 0;
+            par ^= 1u;
+          }
+        }
+        if (bail) break;
+      }
+      flush();  // the slice's last strip (x is re-staged before the next slice)
+      cur = -1;
+      if (bail) imisc[0] = 1;
+    }
+    chain_sync();
+    if (imisc[0]) {
+      bail = true;
+      break;
+    }
+
+    // ------------------------------------------ epilogue per batch row
+    const double inv = 1.0 / 4294967296.0;
+    if (P.epi == kEpiSwiGLU) {
+      for (int t = tid; t < r.nu * 8 * M; t += kCThr) {
+        const int m = t % M, rr = t / M, ul = rr >> 3, row = rr & 7;
+        const long long qg = (long long)acc_s[((size_t)ul * 16 + row) * MR + m];
+        const long long qu = (long long)acc_s[((size_t)ul * 16 + row + 8) * MR + m];
+        // fast.py:170-171: bf16(silu(gate)) * up, each op rounded to bf16
+        const float gt = round_bf16((float)((double)qg * inv)), up = round_bf16((float)((double)qu * inv));
+        const float sg = round_bf16(gt / (1.0f + expf(-gt)));
+        P.y[(size_t)m * P.ldy + 8 * (u0 + ul) + row] = f32_to_bf16_bits(sg * up);
+      }
+    } else {
+      for (int t = tid; t < r.nu * 16 * M; t += kCThr) {
+        const int m = t % M, rr = t / M, ul = rr >> 4, row = rr & 15;
+        float v = (float)((double)(long long)acc_s[((size_t)ul * 16 + row) * MR + m] * inv);
+        const int n = 16 * (u0 + ul) + row;
+        if (P.epi == kEpiResidual) {
+          // fast.py:168 / :170: residual + bf16(linear(...)), rounded to bf16
+          v = bf16_bits_to_f32(__ldcg(P.residual + (size_t)m * P.ldr + n)) + round_bf16(v);
+        }
+        P.y[(size_t)m * P.ldy + n] = f32_to_bf16_bits(v);
+      }
+    }
+    chain_sync();
+    if (ph + 1 < a.nphases && tid == 0) {
+      asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.barrier), "r"(1u) : "memory");
+      ++arrived;
+    }
+  }
+
+  if (tid == 0) {
+    if (bail) flag_error(kDevWaitTimeout);
+    const unsigned rem = (unsigned)(a.nphases - arrived);
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(a.barrier), "r"(rem) : "memory");
+    if (old + rem == (unsigned)G * (unsigned)a.nphases) atomicExch(a.barrier, 0u);
+  }
+}
+
+}  // namespace
+
+int w4_chainb_plan(const int* K, const int* N, const int* norm, int nphases, int M, int g, int num_sms,
+                   ChainPlan* out) {
+  if (nphases < 1 || nphases > kChainMaxPhases || M < 1 || M > 16 || (g != 64 && g != 128 && g != 256) ||
+      num_sms < 1)
+    return -1;
+  ChainPlan p{};
+  p.G = num_sms;
+  p.kmax = 0;
+  p.umax = 1;
+  for (int i = 0; i < nphases; ++i) {
+    if (K[i] <= 0 || N[i] <= 0 || K[i] % g || N[i] % 16) return -1;
+    if (norm[i] && K[i] > kCbSlice) return -1;  // RMSNorm statistics need the row in one slice
+    p.kmax = std::max(p.kmax, std::min(K[i], kCbSlice));
+    p.umax = std::max(p.umax, (N[i] / 16 + p.G - 1) / p.G);
+  }
+  const int rows = M > 8 ? 16 : 8;
+  const int tb = strip_tile_bytes(g);
+  p.stages = 0;
+  for (int s = 12; s >= 2; --s) {
+    if (cb_layout(s, tb, p.kmax, rows, p.umax).total <= 227 * 1024) {
+      p.stages = s;
+      break;
+    }
+  }
+  if (p.stages == 0) return -2;
+  p.smem = cb_layout(p.stages, tb, p.kmax, rows, p.umax).total;
+  *out = p;
+  return 0;
+}
+
+cudaError_t w4_chainb_launch(const ChainBArgs& args, int g, const ChainPlan& p, cudaStream_t stream, int use_pdl) {
+  ChainBArgs a = args;
+  a.stages = p.stages;
+  a.kslice = p.kmax;
+  a.umax = p.umax;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.G);
+  cfg.blockDim = dim3((kChainWarps + 1) * 32);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = use_pdl ? 1 : 0;
+  const int two = a.M > 8 ? 1 : 0;
+  const int gi = (g == 64 ? 0 : (g == 128 ? 1 : 2)) * 2 + two;
+  using K_t = void (*)(const ChainBArgs);
+  static const K_t kerns[6] = {w4_chainb_kernel<64, 1>,  w4_chainb_kernel<64, 2>,  w4_chainb_kernel<128, 1>,
+                               w4_chainb_kernel<128, 2>, w4_chainb_kernel<256, 1>, w4_chainb_kernel<256, 2>};
+  static bool done[6] = {false, false, false, false, false, false};
+  if (!done[gi]) {
+    cudaError_t e = cudaFuncSetAttribute(kerns[gi], cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    int occ = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kerns[gi], (kChainWarps + 1) * 32, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    if (occ < 1) return cudaErrorInvalidConfiguration;
+    done[gi] = true;
+  }
+  return cudaLaunchKernelEx(&cfg, kerns[gi], a);
+}
+
+}  // namespace mtl

@@ -205,3 +205,24 @@ def w4_chain(phases: list, group_size: int, barrier: torch.Tensor, eps: float = 
         arr[i] = _lib.ChainPhase(w.tiles.data_ptr(), ph["x"].data_ptr(), _p(ph.get("norm_w")), _p(ph.get("residual")),
                                  ph["y"].data_ptr(), w.K, w.N, epi)
     _lib.call("mtl_w4_chain", arr, len(phases), group_size, ctypes.c_float(eps), barrier.data_ptr(), _s())
+
+
+def w4_chain_rows(phases: list, group_size: int, barrier: torch.Tensor, eps: float = 1e-6) -> None:
+    """w4_chain for M = 2..16 activation rows (mtl_w4_chain_rows): each
+    phase's "x", "y" (and "residual") are [M, ...] row-major bf16 tensors
+    with unit column stride."""
+    arr = (_lib.ChainPhaseRows * len(phases))()
+    M = int(phases[0]["x"].shape[0])
+    for i, ph in enumerate(phases):
+        w, x, y = ph["w"], ph["x"], ph["y"]
+        res = ph.get("residual")
+        epi = _lib.MTL_EPI_STORE
+        if ph.get("swiglu"):
+            epi = _lib.MTL_EPI_SWIGLU
+        elif res is not None:
+            epi = _lib.MTL_EPI_RESIDUAL
+        if int(x.shape[0]) != M or int(y.shape[0]) != M:
+            raise ValueError("every phase has the same number of rows")
+        arr[i] = _lib.ChainPhaseRows(w.tiles.data_ptr(), x.data_ptr(), _p(ph.get("norm_w")), _p(res), y.data_ptr(),
+                                     x.stride(0), 0 if res is None else res.stride(0), y.stride(0), w.K, w.N, epi)
+    _lib.call("mtl_w4_chain_rows", arr, len(phases), M, group_size, ctypes.c_float(eps), barrier.data_ptr(), _s())

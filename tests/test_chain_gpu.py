@@ -243,3 +243,103 @@ def test_engine_chain_matches_per_linear_launches():
         assert np.abs(la[fin] - lb[fin]).max() < 0.1
     from moss_tts_lite_b200 import _lib
     assert _lib.device_status() == 0
+
+
+def _run_rows(phases, g):
+    from moss_tts_lite_b200 import _lib, kernels
+    bar = torch.zeros(32, dtype=torch.int32, device=phases[0]["x"].device)
+    kernels.w4_chain_rows(phases, g, bar[0])
+    torch.cuda.synchronize()
+    assert int(bar[0]) == 0, "barrier word not re-armed"
+    assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("M,K,N,g", [(2, 4096, 6144, 128), (9, 12288, 4096, 128), (16, 4096, 1536, 128),
+                                     (16, 1024, 4112, 64), (5, 2048, 320, 256)])
+def test_rows_single_phase_vs_oracle(M, K, N, g):
+    """mtl_w4_chain_rows: every row against the product with the reference's
+    operand (K = 12288 runs three x slices)."""
+    dev = require_cuda()
+    q, qsz, Wnk = _ref_case(K, N, g, seed=K + N + M)
+    rng = np.random.default_rng(M)
+    x = f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    xt = _t(x, dev, torch.bfloat16)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    _run_rows([{"w": _strip(q, qsz, g, dev), "x": xt, "y": y}], g)
+    _check(_bits(y), ow.linear_f64(x, Wnk.T))
+
+
+def test_rows_four_phases_phase_by_phase_and_replay():
+    """o -> gate|up -> down -> q|k|v for 16 rows at the benchmark
+    configuration's shapes, each phase against the oracle on the chain's own
+    input to it, then in place as the batched step runs it (same bits) and
+    as a replayed graph (same bits)."""
+    dev = require_cuda()
+    H, I, NQKV, g, M = 4096, 12288, 6144, 128, 16
+    L = _layer(H, I, NQKV, g, seed=70, dev=dev)
+    rng = np.random.default_rng(19)
+    h0 = f32_to_bf16((rng.standard_normal((M, H)) * 2).astype(np.float32))
+    attn = f32_to_bf16(rng.standard_normal((M, H)).astype(np.float32))
+    n1 = f32_to_bf16((1 + 0.1 * rng.standard_normal(H)).astype(np.float32))
+    n2 = f32_to_bf16((1 + 0.1 * rng.standard_normal(H)).astype(np.float32))
+    T = lambda a: _t(a, dev, torch.bfloat16)
+    h0t, at, n1t, n2t = T(h0), T(attn), T(n1), T(n2)
+    h1 = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+    act = torch.empty(M, I, dtype=torch.bfloat16, device=dev)
+    h2 = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+    qkv = torch.empty(M, NQKV, dtype=torch.bfloat16, device=dev)
+    _run_rows([{"w": L["o"][0], "x": at, "y": h1, "residual": h0t},
+               {"w": L["gu"][0], "x": h1, "y": act, "norm_w": n1t, "swiglu": True},
+               {"w": L["down"][0], "x": act, "y": h2, "residual": h1},
+               {"w": L["qkv"][0], "x": h2, "y": qkv, "norm_w": n2t}], g)
+    h1b, actb, h2b, qkvb = _bits(h1), _bits(act), _bits(h2), _bits(qkv)
+    ref1 = ost.add_bf16(h0, ow.linear_bf16(attn, L["o"][1].T))
+    ref2 = ost.silu_mul(ow.linear_bf16(ost.rms_norm(h1b, n1), L["gu"][1].T),
+                        ow.linear_bf16(ost.rms_norm(h1b, n1), L["gu"][2].T))
+    ref3 = ost.add_bf16(h1b, ow.linear_bf16(actb, L["down"][1].T))
+    ref4 = ow.linear_bf16(ost.rms_norm(h2b, n2), L["qkv"][1].T)
+    for name, got, ref in (("o", h1b, ref1), ("gu", actb, ref2), ("down", h2b, ref3), ("qkv", qkvb, ref4)):
+        d = np.abs(bf16_to_f32(got) - bf16_to_f32(ref))
+        assert d.max() <= 2e-2 + 1e-2 * np.abs(bf16_to_f32(ref)).max(), (name, d.max())
+        assert (d == 0).mean() > 0.9, (name, (d == 0).mean())
+    h = h0t.clone()
+    act2, qkv2 = torch.empty_like(act), torch.empty_like(qkv)
+    inplace = [{"w": L["o"][0], "x": at, "y": h, "residual": h},
+               {"w": L["gu"][0], "x": h, "y": act2, "norm_w": n1t, "swiglu": True},
+               {"w": L["down"][0], "x": act2, "y": h, "residual": h},
+               {"w": L["qkv"][0], "x": h, "y": qkv2, "norm_w": n2t}]
+    _run_rows(inplace, g)
+    assert np.array_equal(_bits(h), h2b) and np.array_equal(_bits(qkv2), qkvb)
+    from moss_tts_lite_b200 import _lib, kernels
+    bar = torch.zeros(32, dtype=torch.int32, device=dev)
+    gph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.graph(gph, stream=s):
+        kernels.w4_chain_rows(inplace, g, bar[0])
+    for _ in range(2):
+        h.copy_(h0t)
+        gph.replay()
+        torch.cuda.synchronize()
+        assert int(bar[0]) == 0
+        assert np.array_equal(_bits(h), h2b) and np.array_equal(_bits(qkv2), qkvb)
+    assert _lib.device_status() == 0
+
+
+def test_rows_reject_bad_arguments():
+    dev = require_cuda()
+    from moss_tts_lite_b200 import _lib, kernels
+    q, qsz, _ = _ref_case(8192, 64, 128, seed=5)
+    w = _strip(q, qsz, 128, dev)
+    x = torch.zeros(4, 8192, dtype=torch.bfloat16, device=dev)
+    y = torch.zeros(4, 64, dtype=torch.bfloat16, device=dev)
+    nw = torch.ones(8192, dtype=torch.bfloat16, device=dev)
+    bar = torch.zeros(32, dtype=torch.int32, device=dev)
+    with pytest.raises(_lib.MtlError):          # RMSNorm needs K <= 4096 (one x slice)
+        kernels.w4_chain_rows([{"w": w, "x": x, "y": y, "norm_w": nw}], 128, bar[0])
+    x17 = torch.zeros(17, 8192, dtype=torch.bfloat16, device=dev)
+    y17 = torch.zeros(17, 64, dtype=torch.bfloat16, device=dev)
+    with pytest.raises(_lib.MtlError):          # more than 16 rows
+        kernels.w4_chain_rows([{"w": w, "x": x17, "y": y17}], 128, bar[0])
+    torch.cuda.synchronize()
+    assert int(bar[0]) == 0 and _lib.device_status() == 0

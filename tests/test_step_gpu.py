@@ -301,12 +301,12 @@ def test_bf16_model_step_vs_oracle():
     assert np.mean(agree) > 0.97, agree
 
 
-def _w4_setup(dev, seed=13, max_seq=256):
+def _w4_setup(dev, seed=13, max_seq=256, chain=None):
     from moss_tts_lite_b200.fast import FastMossTTS
     from moss_tts_lite_b200.model import MossTTSModel
     w = _weights(seed=seed)
     m = MossTTSModel(_torch_weights(w, dev), device=dev, max_seq_len=max_seq)
-    fast = FastMossTTS(m, quant="w4", w4_group_size=128)
+    fast = FastMossTTS(m, quant="w4", w4_group_size=128, chain=chain)
     om = _oracle_model(w, max_seq)
     recs = {}
     names = {"q": "self_attn.q_proj", "k": "self_attn.k_proj", "v": "self_attn.v_proj", "o": "self_attn.o_proj",
