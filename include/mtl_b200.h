@@ -290,7 +290,11 @@ int mtl_attn_append(const uint16_t* qkv, const uint16_t* q_norm_w, const uint16_
  * residual of MTL_EPI_RESIDUAL has row stride ldy and may alias y.  When
  * pad_period > 0 (store epilogue), output column n with
  * n % pad_period == pad_col is set to -inf (AUDIO_PAD_CODE, model.py:292).
- * M <= 4, K <= 8192, K % 8 == 0. */
+ * K <= 8192, K % 8 == 0; M <= 4 with any epilogue (CUDA-core kernel, one
+ * warp per output row; each row equals a one-row call bit for bit), or
+ * 5 <= M <= 16 with the store epilogue and K % 32 == 0 (tensor-core kernel:
+ * m16n8k16 MMAs, W rows as A, the M rows as N; the batched decode step's
+ * heads). */
 int mtl_bf16_linear(const uint16_t* x, int M, int K, int N, const uint16_t* W, const uint16_t* norm_w, float eps,
                     uint16_t* x_normed, int pad_period, int pad_col, int epilogue, const uint16_t* residual,
                     uint16_t* y, int ldy, mtl_stream_t stream);

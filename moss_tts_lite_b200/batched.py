@@ -36,7 +36,8 @@ import torch
 from . import _lib, kernels
 from .model import AUDIO_DELAY_SLOT_TOKEN_ID, AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_PAD_CODE, AUDIO_VOCAB, N_VQ, RMS_EPS
 
-_HEAD_ROWS = 4  # rows per bf16 head launch (mtl_bf16_linear)
+_HEAD_ROWS = 4  # rows per bf16 head launch where they must equal one-row launches bit for bit
+_HEAD_ROWS_TC = 16  # rows per launch otherwise (mtl_bf16_linear: 5..16 rows on the tensor-core kernel)
 
 
 class BatchedFastMossTTS:
@@ -212,8 +213,9 @@ class BatchedFastMossTTS:
     def _heads(self) -> None:
         m, B = self.m, self.B
         la2 = self.la.view(B, N_VQ * AUDIO_VOCAB)
-        for r0 in range(0, B, _HEAD_ROWS):
-            r1 = min(B, r0 + _HEAD_ROWS)
+        rows = _HEAD_ROWS_TC if (self.tc or self.chain) else _HEAD_ROWS
+        for r0 in range(0, B, rows):
+            r1 = min(B, r0 + rows)
             kernels.bf16_linear(self.h[r0:r1], m.head_2way, self.two[r0:r1], norm_weight=m.final_norm, eps=RMS_EPS,
                                 x_normed=self.h_final[r0:r1])
             kernels.bf16_linear(self.h[r0:r1], self.head_audio2d, la2[r0:r1], norm_weight=m.final_norm, eps=RMS_EPS,

@@ -20,6 +20,8 @@ cudaError_t launch_embed_sum(const int64_t* ids, int M, const uint16_t* emb_text
 cudaError_t launch_attn_decode(const AttnArgs& a, int streams, cudaStream_t s, int use_pdl);
 cudaError_t launch_attn_append(const AttnArgs& a, int streams, cudaStream_t s, int use_pdl);
 cudaError_t launch_bf16_gemv(const Bf16GemvArgs& a, int num_sms, cudaStream_t s, int use_pdl);
+cudaError_t launch_bf16_rows(const Bf16GemvArgs& a, int num_sms, cudaStream_t s, int use_pdl);
+size_t bf16_rows_smem(int M, int K);
 cudaError_t launch_argmax_rows(const uint16_t* x, int rows, int cols, int ld, int64_t* out, cudaStream_t s,
                                int use_pdl);
 cudaError_t launch_rtn_quantize(const uint16_t* w, int N, int K, int g, uint8_t* q, uint16_t* qsz, cudaStream_t s);
@@ -682,8 +684,14 @@ int mtl_bf16_linear(const uint16_t* x, int M, int K, int N, const uint16_t* W, c
   if (epilogue == 1 && !residual) return fail(MTL_E_INVALID, "mtl_bf16_linear: residual epilogue needs residual");
   if (epilogue == 2 && (N % 2)) return fail(MTL_E_INVALID, "mtl_bf16_linear: SwiGLU needs an even N");
   const int nout = epilogue == 2 ? N / 2 : N;
-  if (M < 1 || M > mtl::kGemvMaxM || K <= 0 || K > mtl::kGemvMaxK || K % 8 || N <= 0 || ldy < nout)
-    return fail(MTL_E_INVALID, "mtl_bf16_linear: M=%d K=%d N=%d ldy=%d (M<=4, K<=8192, K%%8==0)", M, K, N, ldy);
+  // 5..16 rows with the store epilogue: the tensor-core kernel (up to 4 rows
+  // the CUDA-core kernel, whose rows equal one-row calls bit for bit)
+  const bool rows = M > mtl::kGemvMaxM && M <= 16 && epilogue == 0 && K % 32 == 0 && K <= mtl::kGemvMaxK &&
+                    mtl::bf16_rows_smem(M, K) <= 227 * 1024;
+  if (M < 1 || (M > mtl::kGemvMaxM && !rows) || K <= 0 || K > mtl::kGemvMaxK || K % 8 || N <= 0 || ldy < nout)
+    return fail(MTL_E_INVALID,
+                "mtl_bf16_linear: M=%d K=%d N=%d ldy=%d (M<=4, or M<=16 with the store epilogue and K%%32==0; "
+                "K<=8192, K%%8==0)", M, K, N, ldy);
   if (pad_period < 0 || (pad_period > 0 && (pad_col < 0 || pad_col >= pad_period)))
     return fail(MTL_E_INVALID, "mtl_bf16_linear: pad_period=%d pad_col=%d", pad_period, pad_col);
   if (!aligned(W, 16)) return fail(MTL_E_ALIGN, "mtl_bf16_linear: W must be 16-byte aligned");
@@ -702,7 +710,8 @@ int mtl_bf16_linear(const uint16_t* x, int M, int K, int N, const uint16_t* W, c
   a.residual = residual;
   a.y = y;
   a.ldy = ldy;
-  cudaError_t e = mtl::launch_bf16_gemv(a, num_sms(), stream, use_pdl());
+  cudaError_t e = rows ? mtl::launch_bf16_rows(a, num_sms(), stream, use_pdl())
+                       : mtl::launch_bf16_gemv(a, num_sms(), stream, use_pdl());
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_bf16_linear");
 }
 

@@ -267,6 +267,40 @@ def test_bf16_linear_pad_and_epilogues():
     assert ow.close_enough(_bits(y)[:, mask], ref[:, mask])[0]
 
 
+@pytest.mark.parametrize("M,N", [(16, 32800), (9, 4112), (5, 2), (3, 2050)])
+def test_bf16_rows_tensor_core_heads(M, N):
+    """The bf16 head kernels for several rows (5..16: the tensor-core kernel
+    of the batched heads; 3: the CUDA-core kernel): final
+    RMSNorm fused, pad column -inf, normed rows returned; against a torch fp32
+    reference on the oracle's normed rows, and the normed rows bit-exact to
+    the oracle's RMSNorm."""
+    dev = require_cuda()
+    from moss_tts_lite_b200 import kernels
+    rng = np.random.default_rng(M + N)
+    K = 4096
+    W = f32_to_bf16((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+    h = f32_to_bf16((rng.standard_normal((M, K)) * 3).astype(np.float32))
+    nw = f32_to_bf16((1 + 0.1 * rng.standard_normal(K)).astype(np.float32))
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    xn = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+    pad = 1025 if N % 1025 == 0 else 0
+    kernels.bf16_linear(_t(h, dev, torch.bfloat16), _t(W, dev, torch.bfloat16), y, norm_weight=_t(nw, dev, torch.bfloat16),
+                        x_normed=xn, pad_period=pad, pad_col=1024)
+    torch.cuda.synchronize()
+    xo = ost.rms_norm(h, nw)
+    assert np.array_equal(_bits(xn), xo)
+    ref = torch.from_numpy(bf16_to_f32(xo)).float() @ torch.from_numpy(bf16_to_f32(W)).float().T
+    yy = bf16_to_f32(_bits(y))
+    mask = np.ones(N, bool)
+    if pad:
+        mask[1024::1025] = False
+        assert np.isneginf(yy[:, ~mask]).all()
+    d = np.abs(yy[:, mask] - ref.numpy()[:, mask])
+    assert (d <= 2e-2 + 1e-2 * np.abs(ref.numpy()[:, mask])).all(), d.max()
+    from moss_tts_lite_b200 import _lib
+    assert _lib.device_status() == 0
+
+
 # ------------------------------------------------------------- whole model
 def _oracle_model(w, max_seq):
     return ost.OracleModel(w, max_seq_len=max_seq)
