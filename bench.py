@@ -343,7 +343,7 @@ def time_cfg3(fast, prompt_len: int = 4096, steps: int = 1024, seed: int = 3):
             "roofline_ms_per_step_at_mean_cache": (3883599872 + 147456 * (prompt_len + n / 2)) / (_peaks()[0] * 1e6)}
 
 
-def time_cfg4(fast, streams: int = 16, prompt_len: int = 256, steps: int = 2048, seed: int = 4, chain: bool = False):
+def time_cfg4(fast, streams: int = 16, prompt_len: int = 256, steps: int = 2048, seed: int = 4, tc: bool = False):
     """Configuration 4: ``streams`` independent utterances per GPU, each a
     seeded random ``prompt_len``-row prompt (last row AUDIO_START) prefilled
     into its own KV cache, then ``steps`` batched greedy audio-phase decode
@@ -354,7 +354,7 @@ def time_cfg4(fast, streams: int = 16, prompt_len: int = 256, steps: int = 2048,
     from moss_tts_lite_b200.model import AUDIO_GEN_SLOT_TOKEN_ID, AUDIO_START_TOKEN_ID, N_VQ
     g = torch.Generator().manual_seed(seed)
     dev = fast.m.device
-    bt = BatchedFastMossTTS(fast, streams, max_seq=prompt_len + steps + 8, chain=chain)
+    bt = BatchedFastMossTTS(fast, streams, max_seq=prompt_len + steps + 8, tc=True if tc else None)
     prompts, firsts = [], []
     for s in range(streams):
         ids = torch.zeros(prompt_len, N_VQ + 1, dtype=torch.long)
@@ -1210,7 +1210,7 @@ def main():
     ap.add_argument("--no-cfg01", action="store_true", help="skip the configuration-0/1 linear measurements")
     ap.add_argument("--no-cfg3", action="store_true", help="skip the long-context sampled configuration-3 run")
     ap.add_argument("--no-cfg4", action="store_true", help="skip the 16-stream batched configuration-4 run")
-    ap.add_argument("--cfg4-chain", action="store_true", help="configuration 4 on the batched persistent chain")
+    ap.add_argument("--cfg4-tc", action="store_true", help="configuration 4 on tcgen05 tiles, one launch per linear")
     ap.add_argument("--profile-gemv", action="store_true", help="small config-0 GEMV case for ncu")
     ap.add_argument("--profile-gemv-ref", action="store_true", help="reference-format 4096->12288 GEMV (ncu case)")
     ap.add_argument("--profile-gemv-shapes", action="store_true", help="per-projection GEMV times and fixed-cost fit")
@@ -1304,7 +1304,7 @@ def main():
         cfg3["e2e_steps_per_s_all_gpus"] = ctx.world * (-cfg3_e2e)
     cfg4 = None
     if not args.no_cfg4:
-        cfg4 = time_cfg4(fast, chain=args.cfg4_chain)
+        cfg4 = time_cfg4(fast, tc=args.cfg4_tc)
         cfg4_ms = ctx.max(cfg4["device_ms_per_step"])
         cfg4["frames_per_s_all_gpus"] = ctx.world * cfg4["streams"] * 1e3 / cfg4_ms
         cfg4["n_gpus"] = ctx.world

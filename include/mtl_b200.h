@@ -200,10 +200,9 @@ typedef struct {
  * decode step: the reference runs each stream's linears separately,
  * moss_tts_lite/fast.py:165-171).  The rows share one pass over the strip
  * weights as the N dimension of the MMAs; x is staged 4096 columns at a
- * time.  Each output is the fp32 MMA sums of the CTA's warps added as
- * 64-bit fixed-point integers (value x 2^32): bitwise reproducible, exact
- * in the additions, for outputs below 2^31 in magnitude.  Same phase rules
- * and barrier word as mtl_w4_chain. */
+ * time.  Each output is the fp32 MMA sums of the CTA's 16 warps added in
+ * warp order (bitwise reproducible).  Same phase rules and barrier word as
+ * mtl_w4_chain. */
 int mtl_w4_chain_rows(const mtl_chain_phase_rows* phases, int nphases, int M, int group_size, float norm_eps,
                       uint32_t* barrier, mtl_stream_t stream);
 

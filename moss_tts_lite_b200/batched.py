@@ -4,14 +4,14 @@ The reference decodes one utterance at a time (batch 1, moss_tts_lite/
 fast.py:272-325); its throughput configuration runs streams one after the
 other.  Here one decode step advances all B streams:
 
-* every W4 projection reads its weights once for the B rows: with
-  ``tc=True`` (the default from 2 streams) in tensor-core tiles, the B rows
-  being the N dimension of the tcgen05 MMAs (up to 16 rows per launch);
-  with ``tc=False`` in the register-MMA tiles of the batch-1 engine
-  (launches of up to 8 rows, the mma.sync N dimension); with ``chain=True``
+* every W4 projection reads its weights once for the B rows.  By default
   (up to 16 streams, the batch-1 engine running the persistent chain) each
   layer's o -> gate|up -> down -> next q|k|v is one persistent launch over
-  the batch-1 engine's strip weights (``mtl_w4_chain_rows``);
+  the batch-1 engine's strip weights, the B rows as the N dimension of the
+  MMAs (``mtl_w4_chain_rows``); with ``tc=True`` one launch per linear in
+  tensor-core tiles (tcgen05, B rows as N, up to 16 rows per launch); with
+  ``tc=False, chain=False`` one launch per linear in the register-MMA tiles
+  of the batch-1 engine (launches of up to 8 rows, the mma.sync N dimension);
 * attention runs the B streams in one launch, each over its own KV cache
   (``mtl_attn_decode`` with ``streams = B`` and a per-stream cache stride);
 * the final norm, the two-way text head and the 32 audio heads run on the
@@ -58,11 +58,11 @@ class BatchedFastMossTTS:
         H, D = m.hidden_size, m.head_dim
         eng = fast.engine
         self.lins = eng.lins
-        # per-linear launches (tensor-core tiles by default from 2 streams,
-        # register-MMA tiles with tc=False), or with chain=True the
-        # persistent chain over the batch-1 engine's strip weights
+        # the persistent chain over the batch-1 engine's strip weights (the
+        # default when they exist, up to 16 streams, tc not asked for), else
+        # per-linear launches: tensor-core tiles or register-MMA tiles
         if chain is None:
-            chain = False
+            chain = not tc and eng.strips is not None and streams <= 16
         self.chain = bool(chain) and eng.strips is not None and streams <= 16
         if chain and not self.chain:
             raise ValueError("the chain needs the batch-1 engine's strip weights (FastMossTTS(chain=True)) and "

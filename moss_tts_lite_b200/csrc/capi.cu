@@ -502,7 +502,7 @@ int mtl_w4_chain_rows(const mtl_chain_phase_rows* phases, int nphases, int M, in
   if (!barrier || !aligned(barrier, 4)) return fail(MTL_E_INVALID, "mtl_w4_chain_rows: barrier word NULL or misaligned");
   if (!(norm_eps > 0.f)) return fail(MTL_E_INVALID, "mtl_w4_chain_rows: norm_eps must be > 0");
   mtl::ChainBArgs a{};
-  int Ks[mtl::kChainMaxPhases], Ns[mtl::kChainMaxPhases], norm[mtl::kChainMaxPhases];
+  int Ks[mtl::kChainMaxPhases], Ns[mtl::kChainMaxPhases], norm[mtl::kChainMaxPhases], epis[mtl::kChainMaxPhases];
   for (int i = 0; i < nphases; ++i) {
     const mtl_chain_phase_rows& P = phases[i];
     if (!P.tiles || !P.x || !P.y) return fail(MTL_E_INVALID, "mtl_w4_chain_rows: phase %d: NULL tiles / x / y", i);
@@ -539,13 +539,14 @@ int mtl_w4_chain_rows(const mtl_chain_phase_rows* phases, int nphases, int M, in
     Ks[i] = P.K;
     Ns[i] = P.N;
     norm[i] = P.norm_w != nullptr;
+    epis[i] = P.epilogue;
   }
   a.nphases = nphases;
   a.M = M;
   a.eps = norm_eps;
   a.barrier = barrier;
   mtl::ChainPlan plan;
-  if (mtl::w4_chainb_plan(Ks, Ns, norm, nphases, M, group_size, num_sms(), &plan) != 0)
+  if (mtl::w4_chainb_plan(Ks, Ns, norm, epis, nphases, M, group_size, num_sms(), &plan) != 0)
     return fail(MTL_E_UNSUPPORTED, "mtl_w4_chain_rows: no plan fits these phases");
   cudaError_t e = mtl::w4_chainb_launch(a, group_size, plan, stream, use_pdl() ? 1 : 0);
   return e == cudaSuccess ? MTL_OK : cuda_fail(e, "mtl_w4_chain_rows");

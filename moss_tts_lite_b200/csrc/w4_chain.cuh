@@ -59,6 +59,7 @@ struct ChainPlan {
   int stages;  // ring stages of kChainWarps tiles
   int kmax;    // largest K of the phases (x staging)
   int umax;    // most strips one CTA owns in any phase
+  int uaux;    // batched chain: most strips of a phase with a residual or several x slices
   size_t smem;
 };
 
@@ -84,11 +85,11 @@ struct ChainBArgs {
   int nphases, M;
   float eps;
   unsigned* barrier;  // grid counter: 0 before the launch, reset to 0 by it
-  int stages, kslice, umax;
+  int stages, kslice, uaux;
 };
 
-int w4_chainb_plan(const int* K, const int* N, const int* norm, int nphases, int M, int g, int num_sms,
-                   ChainPlan* out);
+int w4_chainb_plan(const int* K, const int* N, const int* norm, const int* epi, int nphases, int M, int g,
+                   int num_sms, ChainPlan* out);
 cudaError_t w4_chainb_launch(const ChainBArgs& a, int g, const ChainPlan& p, cudaStream_t stream, int use_pdl);
 
 cudaError_t w4_pack_strip(const uint8_t* q, const uint16_t* qsz, int K, int N, int g, uint8_t* tiles,

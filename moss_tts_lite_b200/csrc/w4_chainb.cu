@@ -13,13 +13,14 @@
 //    and permuted into MMA-B order in place; the CTA walks its pieces slice
 //    by slice, strip by strip within a slice, and re-stages x between
 //    slices (RMSNorm phases have K <= 4096, one slice);
-//  * each warp's fp32 MMA sums of a strip are added into the CTA's strip
-//    accumulators as 64-bit fixed-point integers (value x 2^32) with shared
-//    memory atomics: integer addition is exact and order-free, so results
-//    are bitwise reproducible without a per-warp partial buffer (which would
-//    need 16 KB per strip at 16 rows).  Outputs must stay below 2^31 in
-//    magnitude (float -> integer conversion saturates; NaN becomes 0);
-//  * the epilogue (store / residual / SwiGLU) runs per batch row.
+//  * after each strip every consumer warp writes its fp32 MMA sums (16 rows
+//    x the batch rows) to one of two shared-memory partial buffers and
+//    arrives on the buffer's mbarrier; a reducer warp sums the 16 partials
+//    in warp order - the results are bitwise reproducible - frees the
+//    buffer and applies the epilogue (store / residual / SwiGLU, per batch
+//    row) while the consumers go on with the next strip.  Phases with
+//    several x slices add each slice's sums into fp32 strip accumulators, in
+//    slice order.
 #include "w4_chain.cuh"
 
 namespace mtl {
@@ -28,30 +29,33 @@ namespace {
 
 constexpr int kCbSlice = 4096;                    // max x columns staged at once
 constexpr int kCbPieces = kChainWarps;            // pieces per ring stage: one per consumer warp
-constexpr float kCbFix = 4294967296.0f;           // 2^32
-constexpr int kCbMiscWords = 64;                  // [0] bail, [8, 8 + kCW) warp sums of squares
+constexpr int kCbMiscWords = 64;                  // [0] bail, [1] reducer phases, [8, 8 + kCW) warp sums of squares
 
 struct CbLayout {
-  size_t bar, ring, xs, acc, misc, total;
+  size_t bar, ring, xs, pbuf, acc, res, misc, total;
 };
 
 // x row stride in bytes: a slice of bf16 plus 64 bytes, so that the 8 rows
 // one MMA fragment load touches fall in different banks
 __host__ __device__ inline int cb_xstride(int kslice) { return kslice * 2 + 64; }
 
-__host__ __device__ inline CbLayout cb_layout(int stages, int tile_bytes, int kslice, int rows, int umax) {
+__host__ __device__ inline CbLayout cb_layout(int stages, int tile_bytes, int kslice, int rows, int uaux) {
   CbLayout L;
   size_t o = 0;
   L.bar = o;
-  o += round_up((size_t)(2 * stages + 1) * 8, 128);
+  o += round_up((size_t)(2 * stages + 5) * 8, 128);
   L.ring = o;
   o += (size_t)stages * kCbPieces * tile_bytes;
   o = round_up(o, 128);
   L.xs = o;
   o += (size_t)rows * cb_xstride(kslice);
   o = round_up(o, 16);
-  L.acc = o;
-  o += (size_t)umax * 16 * rows * 8;
+  L.pbuf = o;  // [2][warps][32 lanes][rows / 2] fp32 strip partials
+  o += (size_t)2 * kChainWarps * 32 * (rows / 2) * 4;
+  L.acc = o;   // [uaux][16][rows] fp32 slice sums
+  o += (size_t)uaux * 16 * rows * 4;
+  L.res = o;   // [uaux][16][rows] bf16 residual of the CTA's strips
+  o += round_up((size_t)uaux * 16 * rows * 2, 16);
   L.misc = o;
   o += kCbMiscWords * 4;
   L.total = round_up(o, 128);
@@ -66,7 +70,7 @@ struct CbRun {
 };
 
 template <int GS, int NT>
-__global__ void __launch_bounds__((kChainWarps + 1) * 32, 1) w4_chainb_kernel(const ChainBArgs a) {
+__global__ void __launch_bounds__((kChainWarps + 2) * 32, 1) w4_chainb_kernel(const ChainBArgs a) {
   extern __shared__ __align__(128) uint8_t cb_sm[];
   constexpr int kCW = kChainWarps;
   constexpr int kCThr = kCW * 32;
@@ -75,13 +79,17 @@ __global__ void __launch_bounds__((kChainWarps + 1) * 32, 1) w4_chainb_kernel(co
   constexpr int MR = 8 * NT;  // staged rows (batch rows padded to the n-tiles)
   const int S = a.stages, M = a.M, KSL = a.kslice;
   const int XS = cb_xstride(KSL);
-  const CbLayout L = cb_layout(S, TB, KSL, MR, a.umax);
+  const CbLayout L = cb_layout(S, TB, KSL, MR, a.uaux);
   uint64_t* full = reinterpret_cast<uint64_t*>(cb_sm + L.bar);
   uint64_t* empty = full + S;
   uint64_t* xbar = empty + S;  // x rows of a slice landed
+  uint64_t* sfull = xbar + 1;  // [2] every consumer warp's partial of a strip written
+  uint64_t* sfree = sfull + 2; // [2] the reducer is done with a partial buffer
   uint8_t* ring = cb_sm + L.ring;
   uint8_t* xs = cb_sm + L.xs;
-  unsigned long long* acc_s = reinterpret_cast<unsigned long long*>(cb_sm + L.acc);
+  float* pbuf = reinterpret_cast<float*>(cb_sm + L.pbuf);
+  float* acc_s = reinterpret_cast<float*>(cb_sm + L.acc);
+  uint16_t* res_s = reinterpret_cast<uint16_t*>(cb_sm + L.res);
   float* misc = reinterpret_cast<float*>(cb_sm + L.misc);
   int* imisc = reinterpret_cast<int*>(misc);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -93,8 +101,14 @@ __global__ void __launch_bounds__((kChainWarps + 1) * 32, 1) w4_chainb_kernel(co
       mbar_init(&empty[s], kCW);
     }
     mbar_init(xbar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sfull[b], kCW);
+      mbar_init(&sfree[b], 1);
+    }
     fence_mbar_init();
     imisc[0] = 0;
+    imisc[1] = 0;  // phases the reducer has finished (a counter: a CTA with no strips in a phase
+                   // finishes it at once, so a parity wait could not tell two phases apart)
   }
   __syncthreads();
   pdl_launch_dependents();
@@ -148,6 +162,85 @@ __global__ void __launch_bounds__((kChainWarps + 1) * 32, 1) w4_chainb_kernel(co
     return;
   }
 
+  if (warp == kCW + 1) {
+    // -------------------------------------------------------------- reducer
+    // For each strip, in the consumers' order: wait until all 16 warps have
+    // written their partials, sum them in warp order (each lane: rows gr /
+    // gr + 8 of the strip, batch rows 8 nt + 2 tq (+1)), add slices in slice
+    // order, apply the epilogue after the last slice, free the buffer.
+    const int gr = lane >> 2, tq = lane & 3;
+    int sq = 0;
+    bool ok = true;
+    for (int ph = 0; ph < a.nphases && ok; ++ph) {
+      const ChainBPhase& P = a.ph[ph];
+      int u0, u1;
+      const CbRun r = runs(P, u0, u1);
+      for (int sl = 0; sl < r.nsl && ok; ++sl) {
+        for (int ul = 0; ul < r.nu; ++ul, ++sq) {
+          const int bsel = sq & 1;
+          const bool landed = mbar_wait(&sfull[bsel], (sq >> 1) & 1);
+          if (__any_sync(0xffffffffu, !landed)) {
+            ok = false;
+            break;
+          }
+          float v[4 * NT];
+#pragma unroll
+          for (int i = 0; i < 4 * NT; ++i) v[i] = 0.f;
+          for (int w = 0; w < kCW; ++w) {
+            const float* src = pbuf + (((size_t)bsel * kCW + w) * 32 + lane) * (4 * NT);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const float4 p4 = *reinterpret_cast<const float4*>(src + 4 * nt);
+              v[4 * nt] += p4.x;
+              v[4 * nt + 1] += p4.y;
+              v[4 * nt + 2] += p4.z;
+              v[4 * nt + 3] += p4.w;
+            }
+          }
+          __syncwarp();  // every lane's reads of the buffer before it is freed
+          if (lane == 0) mbar_arrive(&sfree[bsel]);
+          if (r.nsl > 1) {  // slices add up in slice order
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int row = gr + ((e & 2) ? 8 : 0), m = 8 * nt + 2 * tq + (e & 1);
+                float& cell = acc_s[((size_t)ul * 16 + row) * MR + m];
+                cell += v[4 * nt + e];
+                v[4 * nt + e] = cell;
+              }
+          }
+          if (sl != r.nsl - 1) continue;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int row = gr + ((e & 2) ? 8 : 0), m = 8 * nt + 2 * tq + (e & 1);
+              if (m >= M) continue;
+              if (P.epi == kEpiSwiGLU) {
+                if (e & 2) continue;  // the up row (gr + 8) is paired with gate row gr in this lane
+                // fast.py:170-171: bf16(silu(gate)) * up, each op rounded to bf16
+                const float gt = round_bf16(v[4 * nt + e]), up = round_bf16(v[4 * nt + e + 2]);
+                const float sg = round_bf16(gt / (1.0f + expf(-gt)));
+                P.y[(size_t)m * P.ldy + 8 * (u0 + ul) + gr] = f32_to_bf16_bits(sg * up);
+              } else {
+                float o = v[4 * nt + e];
+                if (P.epi == kEpiResidual)  // fast.py:168 / :170: residual + bf16(linear(...)), rounded to bf16
+                  o = bf16_bits_to_f32(res_s[((size_t)ul * 16 + row) * MR + m]) + round_bf16(o);
+                P.y[(size_t)m * P.ldy + 16 * (u0 + ul) + row] = f32_to_bf16_bits(o);
+              }
+            }
+        }
+      }
+      __syncwarp();
+      if (ok && lane == 0) {
+        __threadfence_block();  // this phase's outputs before the count
+        *reinterpret_cast<volatile int*>(imisc + 1) = ph + 1;
+      }
+    }
+    return;
+  }
+
   // -------------------------------------------------------------- consumers
   const int tid = threadIdx.x;
   const int gr = lane >> 2, tq = lane & 3;
@@ -155,6 +248,8 @@ __global__ void __launch_bounds__((kChainWarps + 1) * 32, 1) w4_chainb_kernel(co
   uint32_t par = 0;
   uint32_t xpar = 0;  // phase parity of xbar
   int arrived = 0;
+  int sq = 0;  // strips flushed in this launch (partial buffer sq & 1)
+  static_assert(kChainWarps == 16, "partial buffers hold 16 warps");
   bool bail = false;
   // staging roles: thread t stages rows t / tpr (tpr threads per row), its
   // 32-column blocks t % tpr, t % tpr + tpr, ... of the slice
@@ -166,7 +261,8 @@ __global__ void __launch_bounds__((kChainWarps + 1) * 32, 1) w4_chainb_kernel(co
     const ChainBPhase& P = a.ph[ph];
     int u0, u1;
     const CbRun r = runs(P, u0, u1);
-    for (int i = tid; i < r.nu * 16 * MR; i += kCThr) acc_s[i] = 0ull;
+    if (r.nsl > 1)  // slice sums (such phases own at most uaux strips)
+      for (int i = tid; i < r.nu * 16 * MR; i += kCThr) acc_s[i] = 0.f;
 
     if (ph == 0) {
       pdl_wait();
@@ -181,26 +277,39 @@ __global__ void __launch_bounds__((kChainWarps + 1) * 32, 1) w4_chainb_kernel(co
         break;
       }
     }
+    // the residual of this CTA's strips (written before this phase), read
+    // by the reducing warps; ordered by the staging barrier below
+    if (P.epi == kEpiResidual) {
+      for (int i = tid; i < r.nu * 16 * M; i += kCThr) {
+        const int ul = i / (16 * M), rem = i - ul * 16 * M, row = rem / M, m = rem - row * M;
+        res_s[((size_t)ul * 16 + row) * MR + m] = __ldcg(P.residual + (size_t)m * P.ldr + 16 * (u0 + ul) + row);
+      }
+    }
 
     float acc[NT][4], acc2[NT][4];
-    int cur = -1;  // local strip of the registers' sums
-    auto flush = [&]() {
-      if (cur >= 0) {
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int row = gr + ((e & 2) ? 8 : 0), m = 8 * nt + 2 * tq + (e & 1);
-            if (m < M) {
-              const long long q = __float2ll_rn((acc[nt][e] + acc2[nt][e]) * kCbFix);
-              atomicAdd(acc_s + ((size_t)cur * 16 + row) * MR + m, (unsigned long long)q);
-            }
-          }
+      for (int e = 0; e < 4; ++e) acc[nt][e] = acc2[nt][e] = 0.f;
+    // this warp's sums of a strip into partial buffer sq & 1 (once the
+    // reducer warp is done with the strip two back that used it)
+    auto flush = [&](int sq) {
+      const int bsel = sq & 1;
+      if (sq >= 2) {
+        const bool freed = mbar_wait(&sfree[bsel], ((sq >> 1) - 1) & 1);
+        if (__any_sync(0xffffffffu, !freed)) imisc[0] = 1;
       }
+      float* dst = pbuf + (((size_t)bsel * kCW + warp) * 32 + lane) * (4 * NT);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        *reinterpret_cast<float4*>(dst + 4 * nt) = make_float4(acc[nt][0] + acc2[nt][0], acc[nt][1] + acc2[nt][1],
+                                                               acc[nt][2] + acc2[nt][2], acc[nt][3] + acc2[nt][3]);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[nt][e] = acc2[nt][e] = 0.f;
+      __syncwarp();  // the warp's partial stores before lane 0's release
+      if (lane == 0) mbar_arrive(&sfull[bsel]);
     };
 
     for (int sl = 0; sl < r.nsl && !bail; ++sl) {
@@ -301,10 +410,6 @@ __global__ void __launch_bounds__((kChainWarps + 1) * 32, 1) w4_chainb_kernel(co
           }
           const int k = g0 + s0 + warp;  // this warp's group
           if (k < g1) {
-            if (ul != cur) {
-              flush();
-              cur = ul;
-            }
             const uint8_t* tile = ring + (size_t)slot * kStageBytes + (size_t)warp * TB;
             const uint2 pw = *reinterpret_cast<const uint2*>(tile + 8 * GS + 8 * gr);
             const uint32_t sc0 = __byte_perm(pw.x, 0u, 0x1010), zr0 = __byte_perm(pw.x, 0u, 0x3232);
@@ -355,42 +460,30 @@ __global__ void __launch_bounds__((kChainWarps + 1) * 32, 1) w4_chainb_kernel(co
           }
         }
         if (bail) break;
+        flush(sq++);  // every warp, pieces or not
       }
-      flush();  // the slice's last strip (x is re-staged before the next slice)
-      cur = -1;
       if (bail) imisc[0] = 1;
+    }
+    // the reducer warp has written every strip of the phase (and is done
+    // with acc_s / res_s before the next phase refills them)
+    if (tid == 0) {
+      const volatile int* done = imisc + 1;
+      if (*done < ph + 1) {
+        const uint64_t deadline = globaltimer_ns() + kWaitNs;
+        for (uint32_t i = 1; *done < ph + 1; ++i)
+          if ((i & 63) == 0 && globaltimer_ns() > deadline) {
+            flag_error(kDevWaitTimeout);
+            imisc[0] = 1;
+            break;
+          }
+      }
+      __threadfence_block();
     }
     chain_sync();
     if (imisc[0]) {
       bail = true;
       break;
     }
-
-    // ------------------------------------------ epilogue per batch row
-    const double inv = 1.0 / 4294967296.0;
-    if (P.epi == kEpiSwiGLU) {
-      for (int t = tid; t < r.nu * 8 * M; t += kCThr) {
-        const int m = t % M, rr = t / M, ul = rr >> 3, row = rr & 7;
-        const long long qg = (long long)acc_s[((size_t)ul * 16 + row) * MR + m];
-        const long long qu = (long long)acc_s[((size_t)ul * 16 + row + 8) * MR + m];
-        // fast.py:170-171: bf16(silu(gate)) * up, each op rounded to bf16
-        const float gt = round_bf16((float)((double)qg * inv)), up = round_bf16((float)((double)qu * inv));
-        const float sg = round_bf16(gt / (1.0f + expf(-gt)));
-        P.y[(size_t)m * P.ldy + 8 * (u0 + ul) + row] = f32_to_bf16_bits(sg * up);
-      }
-    } else {
-      for (int t = tid; t < r.nu * 16 * M; t += kCThr) {
-        const int m = t % M, rr = t / M, ul = rr >> 4, row = rr & 15;
-        float v = (float)((double)(long long)acc_s[((size_t)ul * 16 + row) * MR + m] * inv);
-        const int n = 16 * (u0 + ul) + row;
-        if (P.epi == kEpiResidual) {
-          // fast.py:168 / :170: residual + bf16(linear(...)), rounded to bf16
-          v = bf16_bits_to_f32(__ldcg(P.residual + (size_t)m * P.ldr + n)) + round_bf16(v);
-        }
-        P.y[(size_t)m * P.ldy + n] = f32_to_bf16_bits(v);
-      }
-    }
-    chain_sync();
     if (ph + 1 < a.nphases && tid == 0) {
       asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.barrier), "r"(1u) : "memory");
       ++arrived;
@@ -408,8 +501,8 @@ __global__ void __launch_bounds__((kChainWarps + 1) * 32, 1) w4_chainb_kernel(co
 
 }  // namespace
 
-int w4_chainb_plan(const int* K, const int* N, const int* norm, int nphases, int M, int g, int num_sms,
-                   ChainPlan* out) {
+int w4_chainb_plan(const int* K, const int* N, const int* norm, const int* epi, int nphases, int M, int g,
+                   int num_sms, ChainPlan* out) {
   if (nphases < 1 || nphases > kChainMaxPhases || M < 1 || M > 16 || (g != 64 && g != 128 && g != 256) ||
       num_sms < 1)
     return -1;
@@ -417,23 +510,28 @@ int w4_chainb_plan(const int* K, const int* N, const int* norm, int nphases, int
   p.G = num_sms;
   p.kmax = 0;
   p.umax = 1;
+  p.uaux = 1;
   for (int i = 0; i < nphases; ++i) {
     if (K[i] <= 0 || N[i] <= 0 || K[i] % g || N[i] % 16) return -1;
     if (norm[i] && K[i] > kCbSlice) return -1;  // RMSNorm statistics need the row in one slice
     p.kmax = std::max(p.kmax, std::min(K[i], kCbSlice));
-    p.umax = std::max(p.umax, (N[i] / 16 + p.G - 1) / p.G);
+  }
+  for (int i = 0; i < nphases; ++i) {
+    const int u = (N[i] / 16 + p.G - 1) / p.G;
+    p.umax = std::max(p.umax, u);
+    if (epi[i] == kEpiResidual || K[i] > p.kmax) p.uaux = std::max(p.uaux, u);
   }
   const int rows = M > 8 ? 16 : 8;
   const int tb = strip_tile_bytes(g);
   p.stages = 0;
   for (int s = 12; s >= 2; --s) {
-    if (cb_layout(s, tb, p.kmax, rows, p.umax).total <= 227 * 1024) {
+    if (cb_layout(s, tb, p.kmax, rows, p.uaux).total <= 227 * 1024) {
       p.stages = s;
       break;
     }
   }
   if (p.stages == 0) return -2;
-  p.smem = cb_layout(p.stages, tb, p.kmax, rows, p.umax).total;
+  p.smem = cb_layout(p.stages, tb, p.kmax, rows, p.uaux).total;
   *out = p;
   return 0;
 }
@@ -442,10 +540,10 @@ cudaError_t w4_chainb_launch(const ChainBArgs& args, int g, const ChainPlan& p, 
   ChainBArgs a = args;
   a.stages = p.stages;
   a.kslice = p.kmax;
-  a.umax = p.umax;
+  a.uaux = p.uaux;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.G);
-  cfg.blockDim = dim3((kChainWarps + 1) * 32);
+  cfg.blockDim = dim3((kChainWarps + 2) * 32);  // + producer + reducer
   cfg.dynamicSmemBytes = p.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -463,7 +561,7 @@ cudaError_t w4_chainb_launch(const ChainBArgs& args, int g, const ChainPlan& p, 
     cudaError_t e = cudaFuncSetAttribute(kerns[gi], cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
     int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kerns[gi], (kChainWarps + 1) * 32, 227 * 1024);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kerns[gi], (kChainWarps + 2) * 32, 227 * 1024);
     if (e != cudaSuccess) return e;
     if (occ < 1) return cudaErrorInvalidConfiguration;
     done[gi] = true;

@@ -5,8 +5,8 @@ what a batch-1 decode of that stream gives with the same kernels (one launch
 per linear): the W4 rows, attention streams and head rows are computed
 independently, so logits, final hidden states and the greedily fed next rows
 are compared bit for bit, over several steps, eager and as a replayed CUDA
-graph.  The tensor-core tiles (the default) and the batched persistent chain
-sum in other fp32 / fixed-point orders and are compared within bf16 noise."""
+graph.  The tensor-core tiles and the batched persistent chain (the default)
+sum in other fp32 orders and are compared within bf16 noise."""
 import numpy as np
 import pytest
 import torch
@@ -128,11 +128,11 @@ def test_prefill_all_equals_per_stream_prefill():
 
 @pytest.mark.parametrize("B", [3, 12])
 def test_batched_chain_agrees_with_batch1_chain(B):
-    """The batched persistent chain (mtl_w4_chain_rows, chain=True) against
+    """The batched persistent chain (mtl_w4_chain_rows, the default) against
     batch-1 decodes of each stream with the batch-1 chain: per stream and
     step the logits and hidden states agree within bf16 noise and >= 95% of
     the greedy audio codes coincide; the batched step's graph replay equals
-    its eager pass bit for bit (fixed-point sums are order-free)."""
+    its eager pass bit for bit (warp partials summed in fixed order)."""
     dev = require_cuda()
     from moss_tts_lite_b200.batched import BatchedFastMossTTS
     fast, m, om = _w4_setup(dev, seed=37, max_seq=128)
