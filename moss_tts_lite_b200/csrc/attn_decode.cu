@@ -30,7 +30,7 @@ constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = 4;
 constexpr int kAttnMaxRep = 8;
 constexpr int kAttnTile = 64;                              // positions per tile, 16 per warp
-constexpr int kAttnStages = 4;
+constexpr int kAttnStages = 4;   // ring stages up to 16 splits; 3 (two CTAs per SM) above
 // Positions per split: at least kAttnMinChunk, and a cache of up to
 // kAttnSoloMax positions goes to one CTA per KV head with no split merge
 // (measured on B200 over cache lengths 140..4200: lowest step time).
@@ -38,7 +38,7 @@ constexpr int kAttnMinChunk = 128;
 constexpr int kAttnSoloMax = 256;
 constexpr int kAttnBoxBytes = kAttnTile * 128;             // 64 rows x 64 dims x bf16
 constexpr int kAttnStageBytes = 4 * kAttnBoxBytes;         // K dims 0-63, K 64-127, V 0-63, V 64-127
-constexpr int kAttnDynSmem = kAttnStages * kAttnStageBytes + 1024;  // + alignment slack (swizzle atoms)
+__host__ __device__ constexpr int attn_dyn_smem(int stages) { return stages * kAttnStageBytes + 1024; }  // + swizzle alignment
 constexpr unsigned kAttnKvStable = 1u;  // rows [0, pos) are final before this grid starts
 constexpr int kAttnRec = 132;           // floats per (split, head) partial: o[128], max, sum, pad
 
@@ -93,17 +93,21 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
+template <int kAttnStages>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                        const AttnArgs a) {
   extern __shared__ uint8_t attn_dyn[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(attn_dyn) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full[kAttnStages];
+  __shared__ __align__(8) uint64_t mrg;  // the split records of the merge landed
   __shared__ __align__(16) uint16_t sq[kAttnMaxRep][kHeadDim];      // normed + roped q (bf16), zero padded
   __shared__ __align__(16) uint16_t snew[2][kHeadDim];              // k, v of position pos (bf16)
   __shared__ __align__(16) uint16_t pbuf[kAttnWarps][kAttnMaxRep][16];
   __shared__ float wm[kAttnWarps][kAttnMaxRep], wl[kAttnWarps][kAttnMaxRep];
-  __shared__ float wo[kAttnWarps][kAttnMaxRep][kHeadDim];
+  // the warps' partial outputs of the merge, in the ring once the tiles are
+  // consumed (keeps the static shared memory small: two CTAs fit an SM)
+  float(*wo)[kAttnMaxRep][kHeadDim] = reinterpret_cast<float(*)[kAttnMaxRep][kHeadDim]>(ring);
   __shared__ int sh_flag[2];  // [0] bail (a wait timed out), [1] last split
 
   const int h = blockIdx.x, sp = blockIdx.y, st = blockIdx.z;
@@ -115,6 +119,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (tid == 0) {
     for (int s = 0; s < kAttnStages; ++s) mbar_init(&full[s], 1);
+    mbar_init(&mrg, 1);
     fence_mbar_init();
     sh_flag[0] = 0;
     sh_flag[1] = 0;
@@ -415,6 +420,47 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
   __syncthreads();
   if (!sh_flag[1]) return;
+  const int nact_all = min(a.splits, (s1 + chunk - 1) / chunk);
+  const uint32_t rec_bytes = (uint32_t)(nact_all * rep * kAttnRec * 4);
+  if (rec_bytes <= (uint32_t)(kAttnStages * kAttnStageBytes)) {
+    // every split's records into the idle ring by one bulk copy (one round
+    // trip whatever the split count), merged from shared memory: per head
+    // the largest running max first, then the rescaled sums in split order
+    const float* src = a.partials + (((size_t)st * a.nkv + h) * a.splits * rep) * kAttnRec;
+    const float* rec_s = reinterpret_cast<const float*>(ring);
+    if (tid == 0) {
+      fence_proxy_async_smem();                                // the warp merge's accesses of the ring
+      asm volatile("fence.proxy.async.global;" ::: "memory");  // the records acquired above
+      mbar_arrive_expect_tx(&mrg, rec_bytes);
+      bulk_g2s(ring, src, rec_bytes, &mrg);
+    }
+    if (!mbar_wait(&mrg, 0)) return;  // flagged; the copy is bounded by the wait
+    for (int task = tid; task < rep * 32; task += kAttnThreads) {
+      const int r = task >> 5, d4 = task & 31;
+      float M = -INFINITY;
+      for (int j = 0; j < nact_all; ++j) M = fmaxf(M, rec_s[((size_t)j * rep + r) * kAttnRec + kHeadDim]);
+      float L = 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < nact_all; ++j) {
+        const float* rec = rec_s + ((size_t)j * rep + r) * kAttnRec;
+        const float mj = rec[kHeadDim];
+        const float f = (mj == -INFINITY) ? 0.f : expf(mj - M);
+        const float4 ov = reinterpret_cast<const float4*>(rec)[d4];
+        acc.x = fmaf(ov.x, f, acc.x);
+        acc.y = fmaf(ov.y, f, acc.y);
+        acc.z = fmaf(ov.z, f, acc.z);
+        acc.w = fmaf(ov.w, f, acc.w);
+        L = fmaf(rec[kHeadDim + 1], f, L);
+      }
+      const float inv = 1.0f / L;
+      uint16_t* dst = a.out + (size_t)st * a.nh * kHeadDim + (size_t)(h * rep + r) * kHeadDim + 4 * d4;
+      const uint32_t lo2 = (uint32_t)f32_to_bf16_bits(acc.x * inv) | ((uint32_t)f32_to_bf16_bits(acc.y * inv) << 16);
+      const uint32_t hi2 = (uint32_t)f32_to_bf16_bits(acc.z * inv) | ((uint32_t)f32_to_bf16_bits(acc.w * inv) << 16);
+      *reinterpret_cast<uint2*>(dst) = make_uint2(lo2, hi2);
+    }
+    return;
+  }
+  // records beyond the ring: from global memory, 8 splits per round trip.
   // thread task (head r, dims 4 d4 .. 4 d4 + 3): the splits' records are
   // read 8 at a time with every load issued before any is used; running
   // max / rescale across the groups, sums in split order
@@ -570,11 +616,15 @@ static cudaError_t make_kv_map(CUtensorMap* m, void* base, int nkv, int max_seq,
 }
 
 cudaError_t launch_attn_decode(const AttnArgs& a, int streams, cudaStream_t s, int use_pdl) {
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnDynSmem);
+  // 4 ring stages up to 16 splits; 3 above, so that two CTAs fit an SM
+  const bool three = a.splits > 16;
+  auto kern = three ? attn_decode_kernel<3> : attn_decode_kernel<4>;
+  const int dyn = attn_dyn_smem(three ? 3 : 4);
+  static bool attr_done[2] = {false, false};
+  if (!attr_done[three]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
     if (e != cudaSuccess) return e;
-    attr_done = true;
+    attr_done[three] = true;
   }
   CUtensorMap tk, tv;
   const int map_streams = a.cache_stream_stride ? streams : 1;
@@ -582,8 +632,8 @@ cudaError_t launch_attn_decode(const AttnArgs& a, int streams, cudaStream_t s, i
   if (e == cudaSuccess) e = make_kv_map(&tv, a.v_cache, a.nkv, a.max_seq, map_streams, a.cache_stream_stride);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.nkv, a.splits, streams), dim3(kAttnThreads), kAttnDynSmem, s, attr, use_pdl);
-  return cudaLaunchKernelEx(&cfg, attn_decode_kernel, tk, tv, a);
+  cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.nkv, a.splits, streams), dim3(kAttnThreads), dyn, s, attr, use_pdl);
+  return cudaLaunchKernelEx(&cfg, kern, tk, tv, a);
 }
 
 }  // namespace mtl
