@@ -18,8 +18,10 @@
 // with an online softmax per warp; probabilities exp(s - m) are rounded to
 // bf16 before P.V and the normaliser sums the unrounded values (the rounding
 // point of PyTorch's flash-style SDPA).  The four warps, then the splits
-// (last-arriving CTA, in split order) are merged with the usual max/sum
-// rescaling.
+// are merged with the usual max/sum rescaling: the last-arriving CTA of a
+// head fetches every split's record with one bulk copy into its idle tile
+// ring (one round trip whatever the split count) and merges them in split
+// order from shared memory.
 #include "common.cuh"
 
 #include <cuda.h>
