@@ -268,7 +268,11 @@ class QuantLinear(torch.nn.Module):
 
     @classmethod
     def from_tensors(cls, qweight, qzeros, scales, g_idx=None, group_size: int = 128,
-                     zero_offset: int = 0) -> "QuantLinear":
+                     zero_offset: int = 0, free_source: bool = True) -> "QuantLinear":
+        """Pack the given AutoGPTQ tensors.  With ``free_source`` (default)
+        the module's own AutoGPTQ buffers are emptied after packing: the
+        caller's tensors are the source, and only the tiles stay on the
+        device."""
         K = qweight.shape[0] * 8
         N = qweight.shape[1]
         m = cls(4, group_size, K, N, zero_offset=zero_offset, device=qweight.device)
@@ -277,10 +281,14 @@ class QuantLinear(torch.nn.Module):
         m.scales.copy_(scales)
         if g_idx is not None:
             m.g_idx.copy_(g_idx)
-        m.post_init()
+        m.post_init(free_source=free_source)
         return m
 
-    def post_init(self) -> None:
+    def post_init(self, free_source: bool = False) -> None:
+        """Pack the AutoGPTQ buffers into the device tiles.  ``free_source``
+        empties ``qweight`` / ``qzeros`` / ``scales`` afterwards (the tiles
+        hold the same codes, zeros and scales; keep them for a state_dict in
+        the AutoGPTQ layout)."""
         K, N, g = self.infeatures, self.outfeatures, self.group_size
         gi = self.g_idx.to(torch.int64)
         if gi.min() < 0 or gi.max() >= K // g:
@@ -296,6 +304,10 @@ class QuantLinear(torch.nn.Module):
         _lib.call("mtl_w4_pack_gptq", self.qweight.data_ptr(), self.qzeros.data_ptr(),
                   self.scales.data_ptr(), _ptr(perm), K, N, g, tiles.data_ptr(), _stream())
         self.w = W4Weight(tiles, K, N, g, _lib.MTL_FMT_GPTQ, self.zero_offset, perm)
+        if free_source:
+            self.qweight = self.qweight.new_empty(0)
+            self.qzeros = self.qzeros.new_empty(0)
+            self.scales = self.scales.new_empty(0)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.w is None:
