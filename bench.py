@@ -914,10 +914,11 @@ def profile_chain_rows(streams: int = 16):
     print(json.dumps({"profile": f"batched chain us per launch, {streams} rows", "us": out}))
 
 
-def profile_chain_small(layers: int = 2, launches: int = 6):
+def profile_chain_small(layers: int = 2, launches: int = 6, rows: int = 1):
     """A small ncu case for the persistent W4 chain: `layers` layers of
     configuration-2-shaped strip weights (random codes, ~205 MB, > L2 with
-    two layers), `launches` four-phase chain launches cycling over them."""
+    two layers), `launches` four-phase chain launches cycling over them;
+    with rows > 1 the batched chain (mtl_w4_chain_rows) on that many rows."""
     import torch
     from moss_tts_lite_b200 import kernels
     from moss_tts_lite_b200.quant import StripWeight
@@ -933,11 +934,13 @@ def profile_chain_small(layers: int = 2, launches: int = 6):
         return StripWeight.from_ref(q, qsz, g)
     L = [{"o": strip(H, H), "gu": strip(H, 2 * I), "down": strip(I, H), "qkv": strip(H, NQ)} for _ in range(layers)]
     bf = torch.bfloat16
-    h = torch.randn(H, device=dev, generator=gen).to(bf)
-    attn = torch.randn(H, device=dev, generator=gen).to(bf)
-    act = torch.empty(I, device=dev, dtype=bf)
-    qkv = torch.empty(NQ, device=dev, dtype=bf)
+    lead = (rows,) if rows > 1 else ()
+    h = torch.randn(*lead, H, device=dev, generator=gen).to(bf)
+    attn = torch.randn(*lead, H, device=dev, generator=gen).to(bf)
+    act = torch.empty(*lead, I, device=dev, dtype=bf)
+    qkv = torch.empty(*lead, NQ, device=dev, dtype=bf)
     nw = torch.ones(H, device=dev, dtype=bf)
+    launch = kernels.w4_chain_rows if rows > 1 else kernels.w4_chain
     def phases(w):
         return [{"w": w["o"], "x": attn, "y": h, "residual": h},
                 {"w": w["gu"], "x": h, "y": act, "norm_w": nw, "swiglu": True},
@@ -949,11 +952,11 @@ def profile_chain_small(layers: int = 2, launches: int = 6):
     for i in range(launches):
         if i == launches // 2:
             e0.record()
-        kernels.w4_chain(phases(L[i % layers]), g, bar[i], 1e-6)
+        launch(phases(L[i % layers]), g, bar[i], 1e-6)
     e1.record()
     torch.cuda.synchronize()
     n = launches - launches // 2
-    print(json.dumps({"profile": "w4 chain small case", "layers": layers, "launches": launches,
+    print(json.dumps({"profile": "w4 chain small case", "layers": layers, "launches": launches, "rows": rows,
                       "us_per_launch_eager": e0.elapsed_time(e1) * 1e3 / n}))
 
 
@@ -1215,7 +1218,8 @@ def main():
     ap.add_argument("--profile-gemv-ref", action="store_true", help="reference-format 4096->12288 GEMV (ncu case)")
     ap.add_argument("--profile-gemv-shapes", action="store_true", help="per-projection GEMV times and fixed-cost fit")
     ap.add_argument("--profile-chain", action="store_true", help="persistent W4 chain times per launch")
-    ap.add_argument("--profile-chain-small", action="store_true", help="2-layer W4 chain case (ncu)")
+    ap.add_argument("--profile-chain-small", type=int, nargs="?", const=1, default=0,
+                    help="2-layer W4 chain case (ncu); the value: activation rows (batched chain above 1)")
     ap.add_argument("--profile-chain-rows", type=int, default=0, help="batched chain times for this many rows")
     ap.add_argument("--profile-attn", action="store_true", help="decode attention alone (config 2 heads)")
     ap.add_argument("--profile-attn-launches", action="store_true", help="4 plain attention launches (ncu case)")
@@ -1247,7 +1251,7 @@ def main():
         profile_chain()
         return
     if args.profile_chain_small:
-        profile_chain_small()
+        profile_chain_small(rows=args.profile_chain_small)
         return
     if args.profile_chain_rows:
         profile_chain_rows(args.profile_chain_rows)
