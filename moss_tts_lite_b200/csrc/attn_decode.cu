@@ -7,17 +7,18 @@
 //   at pos, then softmax(q k^T / sqrt(128)) v over positions [0, pos] for the
 //   n_rep query heads sharing each KV head (GQA).
 //
-// Grid (n_kv, splits, streams), 4 warps per CTA.  Split p owns a contiguous,
-// 64-aligned slice of [0, pos]; its K/V rows stream into a 4-stage shared
-// memory ring as 64-position x 64-dim tensor tiles (TMA, 128-byte swizzle,
-// so the fragment loads below are free of bank conflicts).  Each warp owns 16
+// Grid (n_kv, splits, streams), 8 warps per CTA in two pipelines of 4 that
+// take alternate tiles.  Split p owns a contiguous, 64-aligned slice of
+// [0, pos]; its K/V rows stream into a 4-stage shared memory ring as
+// 64-position x 64-dim tensor tiles (TMA, 128-byte swizzle, so the fragment
+// loads below are free of bank conflicts).  Each warp of a pipeline owns 16
 // positions of a tile and computes on the tensor cores (mma.sync m16n8k16,
 // bf16 in, fp32 accumulate):
 //   S^T[16 pos x 8 heads] = K[16 pos x 128] . Q^T[128 x 8 heads]
 //   O^T[128 x 8 heads]   += V^T[128 x 16 pos] . P^T[16 pos x 8 heads]
 // with an online softmax per warp; probabilities exp(s - m) are rounded to
 // bf16 before P.V and the normaliser sums the unrounded values (the rounding
-// point of PyTorch's flash-style SDPA).  The four warps, then the splits
+// point of PyTorch's flash-style SDPA).  The eight warps, then the splits
 // are merged with the usual max/sum rescaling: the last-arriving CTA of a
 // head fetches every split's record with one bulk copy into its idle tile
 // ring (one round trip whatever the split count) and merges them in split
@@ -28,10 +29,11 @@
 
 namespace mtl {
 
-constexpr int kAttnThreads = 128;
-constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = 8;   // two pipelines of 4 warps, alternate tiles
+constexpr int kAttnGroupThreads = 128;
 constexpr int kAttnMaxRep = 8;
-constexpr int kAttnTile = 64;                              // positions per tile, 16 per warp
+constexpr int kAttnTile = 64;                              // positions per tile, 16 per warp of a pipeline
 constexpr int kAttnStages = 4;   // ring stages up to 16 splits; 3 (two CTAs per SM) above
 // Positions per split: at least kAttnMinChunk, and a cache of up to
 // kAttnSoloMax positions goes to one CTA per KV head with no split merge
@@ -111,9 +113,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   // consumed (keeps the static shared memory small: two CTAs fit an SM)
   float(*wo)[kAttnMaxRep][kHeadDim] = reinterpret_cast<float(*)[kAttnMaxRep][kHeadDim]>(ring);
   __shared__ int sh_flag[2];  // [0] bail (a wait timed out), [1] last split
+  __shared__ int last_tile[kAttnStages];  // tile last issued into each stage (drain after a bail)
 
   const int h = blockIdx.x, sp = blockIdx.y, st = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int grp = warp >> 2, tg = tid & (kAttnGroupThreads - 1);  // pipeline, thread in it
   const int g = lane >> 2, t = lane & 3;
   const int rep = a.nh / a.nkv;
   const bool early = (a.flags & kAttnKvStable) != 0;
@@ -150,6 +154,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   auto issue = [&](int i) {         // one thread: tile i into stage i % S
     uint8_t* sb = ring + (size_t)(i % kAttnStages) * kAttnStageBytes;
     uint64_t* bar = &full[i % kAttnStages];
+    last_tile[i % kAttnStages] = i;
     const int y = row0 + lo + i * kAttnTile;
     const int z = a.cache_stream_stride ? st : 0;  // streams may share one cache (prefill rows)
     mbar_arrive_expect_tx(bar, kAttnStageBytes);
@@ -247,7 +252,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     __syncthreads();
     // K/V append at pos (fast.py:145-146) by the split holding pos
-    if (has_pos) {
+    if (has_pos && tid < kHeadDim) {
       kc[(size_t)pos * kHeadDim + tid] = snew[0][tid];
       vc[(size_t)pos * kHeadDim + tid] = snew[1][tid];
     }
@@ -265,28 +270,29 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int c = 0; c < 4; ++c) o[i][c] = 0.f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // heads 2t, 2t+1
     const uint64_t deadline = globaltimer_ns() + kWaitNs;
-    const int rb = warp * 16;
+    const int rb = (warp & 3) * 16;
+    const int bar_id = 1 + grp;  // the pipeline's named barrier
 
-    for (int i = 0; i < ntiles; ++i) {
+    for (int i = grp; i < ntiles; i += 2) {
       const int s = i % kAttnStages;
       uint8_t* sb = ring + (size_t)s * kAttnStageBytes;
       if (!mbar_wait_until(&full[s], (i / kAttnStages) & 1, deadline)) sh_flag[0] = 1;
       const int p0 = lo + i * kAttnTile;
       // the stale row pos is replaced by the new k/v; rows >= hi of V are
       // zeroed (P is 0 there, and 0 * a stale NaN would not be)
-      if (has_pos && pos >= p0 && pos < p0 + kAttnTile && tid < 32) {
-        const int rr = pos - p0, box = tid >> 3, c = tid & 7;  // box: K lo, K hi, V lo, V hi
+      if (has_pos && pos >= p0 && pos < p0 + kAttnTile && tg < 32) {
+        const int rr = pos - p0, box = tg >> 3, c = tg & 7;  // box: K lo, K hi, V lo, V hi
         const uint16_t* srcv = snew[box >> 1] + (box & 1) * 64 + c * 8;
         *reinterpret_cast<uint4*>(sb + box * kAttnBoxBytes + swz(rr, c)) = *reinterpret_cast<const uint4*>(srcv);
       }
       if (hi < p0 + kAttnTile) {
         const int z0 = hi - p0;
-        for (int e = tid; e < (kAttnTile - z0) * 16; e += kAttnThreads) {
+        for (int e = tg; e < (kAttnTile - z0) * 16; e += kAttnGroupThreads) {
           const int row = z0 + (e >> 4), box = 2 + ((e >> 3) & 1), c = e & 7;
           *reinterpret_cast<uint4*>(sb + box * kAttnBoxBytes + row * 128 + c * 16) = make_uint4(0, 0, 0, 0);
         }
       }
-      __syncthreads();
+      asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "n"(kAttnGroupThreads) : "memory");
       if (sh_flag[0]) break;
       const uint32_t kb = smem_addr(sb), vb = kb + 2 * kAttnBoxBytes;
       // ---- S^T = K . Q^T over 8 k-steps of 16 dims
@@ -343,18 +349,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mma_bf16(o[d], af, pb0, pb1);
         }
       }
-      __syncthreads();  // stage s and pbuf free
-      if (tid == 0 && i + kAttnStages < ntiles) {
+      asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "n"(kAttnGroupThreads) : "memory");  // stage s free
+      if (tg == 0 && i + kAttnStages < ntiles) {  // the refill: this pipeline's leader
         fence_proxy_async_smem();
         issue(i + kAttnStages);
-        ++issued;
       }
     }
+    __syncthreads();  // both pipelines done (and last_tile visible)
     // ---- every issued copy has landed before the CTA goes on (and exits)
     if (tid == 0 && sh_flag[0]) {
       const uint64_t dl = globaltimer_ns() + kWaitNs;
-      for (int s = 0; s < kAttnStages && s < issued; ++s) {
-        const int last = s + ((issued - 1 - s) / kAttnStages) * kAttnStages;
+      for (int s = 0; s < kAttnStages && s < min(issued, ntiles); ++s) {
+        const int last = last_tile[s];
         if (!mbar_wait_until(&full[s], (last / kAttnStages) & 1, dl)) {
           flag_error(kDevCopyDrainTimeout);
           break;
@@ -362,7 +368,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       flag_error(kDevWaitTimeout);
     }
-    // ---- merge the 4 warps: row sums over the 8 lanes of each head pair
+    // ---- merge the 8 warps: row sums over the 8 lanes of each head pair
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
       l0 += __shfl_xor_sync(0xffffffffu, l0, off);
@@ -382,7 +388,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       wo[warp][2 * t + 1][16 * d + g + 8] = o[d][3];
     }
     __syncthreads();
-    for (int r = 0; r < rep; ++r) {
+    for (int r = 0; r < rep && tid < kHeadDim; ++r) {
       float M = -INFINITY;
 #pragma unroll
       for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w][r]);
@@ -545,7 +551,9 @@ __device__ __forceinline__ void norm_rope_row(const uint16_t* src, const uint16_
   }
 }
 
-__global__ void __launch_bounds__(kAttnThreads) attn_append_kernel(const AttnArgs a) {
+constexpr int kAppendThreads = 128;  // warps 0 / 1: k / v; warps 2, 3: the q heads
+
+__global__ void __launch_bounds__(kAppendThreads) attn_append_kernel(const AttnArgs a) {
   const int h = blockIdx.x, st = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_launch_dependents();
@@ -643,7 +651,7 @@ cudaError_t launch_attn_decode(const AttnArgs& a, int streams, cudaStream_t s, i
 namespace mtl {
 cudaError_t launch_attn_append(const AttnArgs& a, int streams, cudaStream_t s, int use_pdl) {
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.nkv, streams), dim3(kAttnThreads), 0, s, attr, use_pdl);
+  cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.nkv, streams), dim3(kAppendThreads), 0, s, attr, use_pdl);
   return cudaLaunchKernelEx(&cfg, attn_append_kernel, a);
 }
 }  // namespace mtl
