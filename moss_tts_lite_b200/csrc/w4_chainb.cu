@@ -187,10 +187,10 @@ __global__ void __launch_bounds__((kChainWarps + 2) * 32, 1) w4_chainb_kernel(co
 #pragma unroll
           for (int i = 0; i < 4 * NT; ++i) v[i] = 0.f;
           for (int w = 0; w < kCW; ++w) {
-            const float* src = pbuf + (((size_t)bsel * kCW + w) * 32 + lane) * (4 * NT);
+            const float* src = pbuf + (((size_t)bsel * kCW + w) * NT * 32 + lane) * 4;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-              const float4 p4 = *reinterpret_cast<const float4*>(src + 4 * nt);
+              const float4 p4 = *reinterpret_cast<const float4*>(src + nt * 128);
               v[4 * nt] += p4.x;
               v[4 * nt + 1] += p4.y;
               v[4 * nt + 2] += p4.z;
@@ -299,11 +299,12 @@ __global__ void __launch_bounds__((kChainWarps + 2) * 32, 1) w4_chainb_kernel(co
         const bool freed = mbar_wait(&sfree[bsel], ((sq >> 1) - 1) & 1);
         if (__any_sync(0xffffffffu, !freed)) imisc[0] = 1;
       }
-      float* dst = pbuf + (((size_t)bsel * kCW + warp) * 32 + lane) * (4 * NT);
+      // [buffer][warp][n-tile][lane] float4: a store covers 512 contiguous bytes
+      float* dst = pbuf + (((size_t)bsel * kCW + warp) * NT * 32 + lane) * 4;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
-        *reinterpret_cast<float4*>(dst + 4 * nt) = make_float4(acc[nt][0] + acc2[nt][0], acc[nt][1] + acc2[nt][1],
-                                                               acc[nt][2] + acc2[nt][2], acc[nt][3] + acc2[nt][3]);
+        *reinterpret_cast<float4*>(dst + nt * 128) = make_float4(acc[nt][0] + acc2[nt][0], acc[nt][1] + acc2[nt][1],
+                                                                 acc[nt][2] + acc2[nt][2], acc[nt][3] + acc2[nt][3]);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
