@@ -259,14 +259,12 @@ __global__ void __launch_bounds__((kCW + 1) * 32, 1) w4_chain_kernel(const Chain
         }
       }
     }
-    // stage x as bf16 in MMA-B order, two k16-steps per 16-byte lane load:
-    // lane t of k16-steps (2q, 2q+1) reads x[32q + {2t, 2t+1, 2t+8, 2t+9,
-    // 16+2t, 16+2t+1, 16+2t+8, 16+2t+9}], i.e. 32-bit words [w_t, w_t+4,
-    // w_t+8, w_t+12] of the 32-block at 16 t bytes
+    // stage x as bf16 in its natural order (the strip packing permutes the
+    // MMAs' k positions to match)
     if (tid < nb32) {
       uint4* dst = reinterpret_cast<uint4*>(xs + 32 * tid);
 #pragma unroll
-      for (int t = 0; t < 4; ++t) dst[t] = make_uint4(u[t], u[t + 4], u[t + 8], u[t + 12]);
+      for (int t = 0; t < 4; ++t) dst[t] = make_uint4(u[4 * t], u[4 * t + 1], u[4 * t + 2], u[4 * t + 3]);
     }
     chain_sync();
 
@@ -307,7 +305,7 @@ __global__ void __launch_bounds__((kCW + 1) * 32, 1) w4_chain_kernel(const Chain
 #pragma unroll
           for (int h = 0; h < GS / 64; ++h) {
             const uint4 wv = wt[h * 32 + lane];
-            const uint4 xa = xg[(2 * h) * 4], xb = xg[(2 * h + 1) * 4];  // k16-steps 4h, 4h+1 | 4h+2, 4h+3
+            const uint4 xa = xg[(2 * h) * 4], xb = xg[(2 * h + 1) * 4];  // x[32q + 8t ..], q = 2h | 2h + 1
             const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
             const uint32_t bx[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
@@ -414,13 +412,13 @@ __global__ void pack_strip_kernel(const uint8_t* q, const uint16_t* qsz, int K, 
   uint32_t* out = reinterpret_cast<uint32_t*>(tiles + (size_t)tile * strip_tile_bytes(g));
   if (wi < 2 * g) {
     const int h = wi >> 7, lane = (wi >> 2) & 31, l = wi & 3;
-    const int ks = 4 * h + l, gr = lane >> 2, t = lane & 3;
-    const int r0 = 16 * u + gr, c0 = k * g + 16 * ks + 2 * t;
+    const int gr = lane >> 2, t = lane & 3;
+    const int r0 = 16 * u + gr, c0 = k * g + 32 * (2 * h + (l >> 1)) + 8 * t + 4 * (l & 1);
     uint32_t w = 0;
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
       const int row = r0 + ((s & 1) ? 8 : 0);
-      const int col = c0 + ((s & 2) ? 8 : 0) + (s >> 2);
+      const int col = c0 + ((s & 2) ? 2 : 0) + (s >> 2);
       w |= (uint32_t)(q[(size_t)row * K + col] & 0xFu) << (4 * s);
     }
     out[wi] = w;

@@ -11,16 +11,17 @@
 //            row r + 8h, so a lane's two rows (gr, gr + 8) are adjacent
 //
 // Word (h, lane, l) holds the eight codes lane (gr = lane/4, t = lane%4)
-// feeds as the A fragment of one m16n8k16 MMA at k16-step ks = 4h + l:
-// rows r0 = gr, r1 = gr + 8 of the strip, k = 16 ks + {2t, 2t+1, 2t+8,
-// 2t+9}; slot s (bits 4s..4s+3) holds
-//   s0 = W[r0][2t]    s4 = W[r0][2t+1]     -> A register a0
-//   s1 = W[r1][2t]    s5 = W[r1][2t+1]     -> a1
-//   s2 = W[r0][2t+8]  s6 = W[r0][2t+9]     -> a2
-//   s3 = W[r1][2t+8]  s7 = W[r1][2t+9]     -> a3
-// (the slot order of the 64-column register-MMA tiles, with the four words
-// of a uint4 being four k16-steps of one strip instead of four 16-row
-// subtiles).  A gate|up pair for the SwiGLU epilogue is interleaved in
+// feeds as the A fragment of one m16n8k16 MMA, the l-th of word group h:
+// rows r0 = gr, r1 = gr + 8 of the strip, and columns of the 32-column block
+// q = 2h + l/2 at c = 32 q + 8 t + 4 (l % 2); slot s (bits 4s..4s+3) holds
+//   s0 = W[r0][c]     s4 = W[r0][c+1]      -> A register a0
+//   s1 = W[r1][c]     s5 = W[r1][c+1]      -> a1
+//   s2 = W[r0][c+2]   s6 = W[r0][c+3]      -> a2
+//   s3 = W[r1][c+2]   s7 = W[r1][c+3]      -> a3
+// The MMA's k positions are permuted within each 32-column block - the
+// same way for A and for B - so that lane t's B fragments of MMAs l = 0, 1
+// are the 16 contiguous bytes x[32q + 8t .. 32q + 8t + 7]: x is used in its
+// natural order (no staging permutation).  A gate|up pair for the SwiGLU epilogue is interleaved in
 // blocks of 8 rows: rows 0-7 of strip u are gate rows 8u..8u+7, rows 8-15
 // the up rows of the same outputs, so the MMA lane that holds a gate sum
 // also holds its up sum.

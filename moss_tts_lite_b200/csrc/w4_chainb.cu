@@ -9,9 +9,9 @@
 // the same bf16 operand bf16((q - 8) s + z).  What changes:
 //
 //  * x is staged per K-slice of up to 4096 columns (16 rows x 4096 bf16 do
-//    not leave room for more): the rows land by bulk copies, are normalised
-//    and permuted into MMA-B order in place; the CTA walks its pieces slice
-//    by slice, strip by strip within a slice, and re-stages x between
+//    not leave room for more): the rows land by bulk copies in their natural
+//    order (RMSNorm phases normalise them in place); the CTA walks its pieces
+//    slice by slice, strip by strip within a slice, and re-stages x between
 //    slices (RMSNorm phases have K <= 4096, one slice);
 //  * after each strip every consumer warp writes its fp32 MMA sums (16 rows
 //    x the batch rows) to one of two shared-memory partial buffers and
@@ -317,8 +317,8 @@ __global__ void __launch_bounds__((kChainWarps + 2) * 32, 1) w4_chainb_kernel(co
       const int g0 = sl * r.gps, g1 = min(r.KT, g0 + r.gps);
       const int kc = (g1 - g0) * GS;  // columns of this slice
       // ---- stage x[:, slice] (RMSNorm phases have a single slice): the M
-      //      rows land in shared memory by bulk copies (one round trip), are
-      //      normalised there and permuted in place into MMA-B order
+      //      rows land in shared memory by bulk copies (one round trip) and
+      //      are normalised there
       if (sl > 0) chain_sync();  // every warp is done with the previous slice
       const int nblk = kc / 32;
       if (tid == 0) {
@@ -358,42 +358,30 @@ __global__ void __launch_bounds__((kChainWarps + 2) * 32, 1) w4_chainb_kernel(co
         for (int w = 0; w < swarps; ++w) t += misc[8 + srow * swarps + w];
         rinv = rsqrtf(t / (float)P.K + a.eps);
       }
-      for (int b = scol; b < nblk; b += kTpr) {
-        uint32_t u[16];
-        uint4* blk = reinterpret_cast<uint4*>(xrow + 64 * b);
-        if (srow < M) {
+      // x stays in its natural order (the strip packing permutes the MMAs'
+      // k positions to match); RMSNorm phases normalise it in place.  Rows
+      // past M are never written: they only feed output columns past M,
+      // which are not stored.
+      if (P.norm_w && srow < M) {
+        for (int b = scol; b < nblk; b += kTpr) {
+          uint4* blk = reinterpret_cast<uint4*>(xrow + 64 * b);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const uint4 v = blk[e];
-            u[4 * e] = v.x;
-            u[4 * e + 1] = v.y;
-            u[4 * e + 2] = v.z;
-            u[4 * e + 3] = v.w;
-          }
-          if (P.norm_w) {
+            const uint4 nv = __ldg(reinterpret_cast<const uint4*>(P.norm_w + g0 * GS + 32 * b) + e);
+            uint32_t u4[4] = {v.x, v.y, v.z, v.w};
+            const uint32_t w4[4] = {nv.x, nv.y, nv.z, nv.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const uint4 nv = __ldg(reinterpret_cast<const uint4*>(P.norm_w + g0 * GS + 32 * b) + e);
-              const uint32_t w4[4] = {nv.x, nv.y, nv.z, nv.w};
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const uint32_t x2 = u[4 * e + q];
-                // model.py:34-40: bf16(h * rsqrt(var + eps)), then bf16(weight * that)
-                const float v0 = round_bf16(__uint_as_float(w4[q] << 16) * round_bf16(__uint_as_float(x2 << 16) * rinv));
-                const float v1 = round_bf16(__uint_as_float(w4[q] & 0xFFFF0000u) *
-                                            round_bf16(__uint_as_float(x2 & 0xFFFF0000u) * rinv));
-                u[4 * e + q] = (__float_as_uint(v0) >> 16) | (__float_as_uint(v1) & 0xFFFF0000u);
-              }
+            for (int q = 0; q < 4; ++q) {
+              // model.py:34-40: bf16(h * rsqrt(var + eps)), then bf16(weight * that)
+              const float v0 = round_bf16(__uint_as_float(w4[q] << 16) * round_bf16(__uint_as_float(u4[q] << 16) * rinv));
+              const float v1 = round_bf16(__uint_as_float(w4[q] & 0xFFFF0000u) *
+                                          round_bf16(__uint_as_float(u4[q] & 0xFFFF0000u) * rinv));
+              u4[q] = (__float_as_uint(v0) >> 16) | (__float_as_uint(v1) & 0xFFFF0000u);
             }
+            blk[e] = make_uint4(u4[0], u4[1], u4[2], u4[3]);
           }
-        } else {
-#pragma unroll
-          for (int q = 0; q < 16; ++q) u[q] = 0u;  // padding rows of the n-tile
         }
-        // MMA-B order, two k16-steps per 16-byte lane load (as w4_chain.cu);
-        // this thread alone owns the block, so the permutation is in place
-#pragma unroll
-        for (int t = 0; t < 4; ++t) blk[t] = make_uint4(u[t], u[t + 4], u[t + 8], u[t + 12]);
       }
       chain_sync();
       if (imisc[0]) {
