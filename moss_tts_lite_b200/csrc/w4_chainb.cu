@@ -337,10 +337,9 @@ __global__ void __launch_bounds__((kChainWarps + 2) * 32, 1) w4_chainb_kernel(co
       if (P.norm_w) {
         float ss = 0.f;
         if (srow < M) {
-          for (int b = scol; b < nblk; b += kTpr) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const uint4 v = reinterpret_cast<const uint4*>(xrow + 64 * b)[e];
+          for (int cc = scol; cc < 4 * nblk; cc += kTpr) {  // 16-byte chunks, consecutive per lane
+            {
+              const uint4 v = reinterpret_cast<const uint4*>(xrow)[cc];
               const uint32_t u4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
@@ -363,14 +362,23 @@ __global__ void __launch_bounds__((kChainWarps + 2) * 32, 1) w4_chainb_kernel(co
       // past M are never written: they only feed output columns past M,
       // which are not stored.
       if (P.norm_w && srow < M) {
-        for (int b = scol; b < nblk; b += kTpr) {
-          uint4* blk = reinterpret_cast<uint4*>(xrow + 64 * b);
+        // 16-byte chunks, consecutive per lane (no bank conflicts); the norm
+        // weights of four chunks are loaded before they are used
+        const int nch = 4 * nblk;
+        const uint4* nwp = reinterpret_cast<const uint4*>(P.norm_w + g0 * GS);
+        uint4* xr4 = reinterpret_cast<uint4*>(xrow);
+        for (int c0 = scol; c0 < nch; c0 += 4 * kTpr) {
+          uint4 nv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (c0 + e * kTpr < nch) nv[e] = __ldg(nwp + c0 + e * kTpr);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const uint4 v = blk[e];
-            const uint4 nv = __ldg(reinterpret_cast<const uint4*>(P.norm_w + g0 * GS + 32 * b) + e);
+            const int cc = c0 + e * kTpr;
+            if (cc >= nch) break;
+            const uint4 v = xr4[cc];
             uint32_t u4[4] = {v.x, v.y, v.z, v.w};
-            const uint32_t w4[4] = {nv.x, nv.y, nv.z, nv.w};
+            const uint32_t w4[4] = {nv[e].x, nv[e].y, nv[e].z, nv[e].w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               // model.py:34-40: bf16(h * rsqrt(var + eps)), then bf16(weight * that)
@@ -379,7 +387,7 @@ __global__ void __launch_bounds__((kChainWarps + 2) * 32, 1) w4_chainb_kernel(co
                                           round_bf16(__uint_as_float(u4[q] & 0xFFFF0000u) * rinv));
               u4[q] = (__float_as_uint(v0) >> 16) | (__float_as_uint(v1) & 0xFFFF0000u);
             }
-            blk[e] = make_uint4(u4[0], u4[1], u4[2], u4[3]);
+            xr4[cc] = make_uint4(u4[0], u4[1], u4[2], u4[3]);
           }
         }
       }
