@@ -186,13 +186,16 @@ __global__ void __launch_bounds__((kCW + 1) * 32, 1) w4_chain_kernel(const Chain
     int u0, u1;
     strip_range(P.N / 16, c, G, u0, u1);
     const int nu = u1 - u0, n = nu * KT;
-    const int nb32 = K / 32;  // <= kCThr (K <= 16384): one 32-value block per thread
 
-    // layer constants first: the norm weights of this thread's 32-block
+    // x staging: thread t owns the 16-byte chunks t, t + 512, ... (consecutive
+    // threads on consecutive chunks: coalesced loads, conflict-free stores)
+    const int nch = K / 8;  // <= 4 kCThr (K <= kChainMaxK)
+    // layer constants first: the norm weights of this thread's chunks
     uint4 nw[4];
-    if (P.norm_w && tid < nb32) {
+    if (P.norm_w) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) nw[e] = __ldg(reinterpret_cast<const uint4*>(P.norm_w + 32 * tid) + e);
+      for (int e = 0; e < 4; ++e)
+        if (tid + e * kCThr < nch) nw[e] = __ldg(reinterpret_cast<const uint4*>(P.norm_w) + tid + e * kCThr);
     }
     for (int i = tid; i < nu * kCW * 16; i += kCThr) part[i] = 0.f;
 
@@ -214,28 +217,24 @@ __global__ void __launch_bounds__((kCW + 1) * 32, 1) w4_chain_kernel(const Chain
     // x (L2 loads: it may have been written by this launch), its RMSNorm
     // statistics and the residual this thread's epilogue adds
     uint4 xv[4];
-    if (tid < nb32) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) xv[e] = __ldcg(reinterpret_cast<const uint4*>(P.x + 32 * tid) + e);
-    }
+    for (int e = 0; e < 4; ++e)
+      if (tid + e * kCThr < nch) xv[e] = __ldcg(reinterpret_cast<const uint4*>(P.x) + tid + e * kCThr);
     float rres = 0.f;
     if (P.epi == kEpiResidual && tid < nu * 16) rres = bf16_bits_to_f32(__ldcg(P.residual + 16 * u0 + tid));
-    uint32_t u[16];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      u[4 * e] = xv[e].x;
-      u[4 * e + 1] = xv[e].y;
-      u[4 * e + 2] = xv[e].z;
-      u[4 * e + 3] = xv[e].w;
-    }
+    float rinv = 1.f;
     if (P.norm_w) {
       float ss = 0.f;
-      if (tid < nb32) {
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const float lo = __uint_as_float(u[q] << 16), hi = __uint_as_float(u[q] & 0xFFFF0000u);
-          ss = fmaf(lo, lo, ss);
-          ss = fmaf(hi, hi, ss);
+      for (int e = 0; e < 4; ++e) {
+        if (tid + e * kCThr < nch) {
+          const uint32_t u4[4] = {xv[e].x, xv[e].y, xv[e].z, xv[e].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float lo = __uint_as_float(u4[q] << 16), hi = __uint_as_float(u4[q] & 0xFFFF0000u);
+            ss = fmaf(lo, lo, ss);
+            ss = fmaf(hi, hi, ss);
+          }
         }
       }
       ss = warp_sum(ss);
@@ -245,26 +244,26 @@ __global__ void __launch_bounds__((kCW + 1) * 32, 1) w4_chain_kernel(const Chain
       float tss = 0.f;
 #pragma unroll
       for (int w = 0; w < kCW; ++w) tss += misc[8 + w];
-      const float rinv = rsqrtf(tss / (float)K + a.eps);
-      if (tid < nb32) {
-        const uint32_t w16[16] = {nw[0].x, nw[0].y, nw[0].z, nw[0].w, nw[1].x, nw[1].y, nw[1].z, nw[1].w,
-                                  nw[2].x, nw[2].y, nw[2].z, nw[2].w, nw[3].x, nw[3].y, nw[3].z, nw[3].w};
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          // model.py:34-40: bf16(h * rsqrt(var + eps)), then bf16(weight * that)
-          const float v0 = round_bf16(__uint_as_float(w16[q] << 16) * round_bf16(__uint_as_float(u[q] << 16) * rinv));
-          const float v1 = round_bf16(__uint_as_float(w16[q] & 0xFFFF0000u) *
-                                      round_bf16(__uint_as_float(u[q] & 0xFFFF0000u) * rinv));
-          u[q] = (__float_as_uint(v0) >> 16) | (__float_as_uint(v1) & 0xFFFF0000u);
-        }
-      }
+      rinv = rsqrtf(tss / (float)K + a.eps);
     }
     // stage x as bf16 in its natural order (the strip packing permutes the
     // MMAs' k positions to match)
-    if (tid < nb32) {
-      uint4* dst = reinterpret_cast<uint4*>(xs + 32 * tid);
 #pragma unroll
-      for (int t = 0; t < 4; ++t) dst[t] = make_uint4(u[4 * t], u[4 * t + 1], u[4 * t + 2], u[4 * t + 3]);
+    for (int e = 0; e < 4; ++e) {
+      if (tid + e * kCThr >= nch) break;
+      uint32_t u4[4] = {xv[e].x, xv[e].y, xv[e].z, xv[e].w};
+      if (P.norm_w) {
+        const uint32_t w4[4] = {nw[e].x, nw[e].y, nw[e].z, nw[e].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          // model.py:34-40: bf16(h * rsqrt(var + eps)), then bf16(weight * that)
+          const float v0 = round_bf16(__uint_as_float(w4[q] << 16) * round_bf16(__uint_as_float(u4[q] << 16) * rinv));
+          const float v1 = round_bf16(__uint_as_float(w4[q] & 0xFFFF0000u) *
+                                      round_bf16(__uint_as_float(u4[q] & 0xFFFF0000u) * rinv));
+          u4[q] = (__float_as_uint(v0) >> 16) | (__float_as_uint(v1) & 0xFFFF0000u);
+        }
+      }
+      reinterpret_cast<uint4*>(xs)[tid + e * kCThr] = make_uint4(u4[0], u4[1], u4[2], u4[3]);
     }
     chain_sync();
 
